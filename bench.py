@@ -1,0 +1,394 @@
+#!/usr/bin/env python
+"""Vamana build throughput on B200 (BASELINE.json metric).
+
+One step = one complete Vamana build (medoid, random init, 4 synchronous
+rounds of GreedySearch + online RobustInsert, exact reverse-edge merge,
+RobustPrune) of BASELINE.json configs[1]: N=10,000,000 uint8 vectors, d=128,
+4096-centroid mixture (U[0,255] centroids, N(0,20) noise, clipped, rounded),
+R=64, L=100, C=80, STEPS=64, alpha=1.2, seed 42.  Synthetic data generated
+on the GPU with a seeded torch generator stands in for the reference's
+datasets.  The 1.28 GB vector store exceeds the 126 MB L2, so no flush is
+needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Output: one JSON line on rank 0.  `value` = vectors/s of the device-resident
+build (inputs already in HBM, CUDA events on the build stream, max over
+ranks); `e2e` = the same metric through the reference C ABI
+gpu_vamana_vnew2_build with pinned host buffers (H2D of the vectors and D2H
+of graph + degrees inside the timed region).  `--impl reference` times the
+reference algorithm's CPU restatement (oracle/) on the host cores on a
+bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+WORKLOAD = dict(name="cfg1_u8_10M", N=10_000_000, dim=128, centroids=4096, noise=20.0, R=64, L=100, C=80, STEPS=64,
+                alpha=1.2, iters=4, seed=42, queries=10_000)
+REF_SAMPLE = 32_768      # vectors per step of the --impl reference CPU arm
+CPU_BASELINE_SAMPLE = 65_536  # vectors of the cpu_baseline sample in our arm
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--n", type=int, default=WORKLOAD["N"], help="override N (profiling small cases)")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-recall", action="store_true")
+    ap.add_argument("--ref-gpu", action="store_true",
+                    help="also time the reference's own GPU builder (oracle/_ref, sm_100a) once on the workload")
+    return ap.parse_args()
+
+
+# ------------------------------------------------------------------ helpers
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region."""
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.t = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except FileNotFoundError:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.t.join(timeout=2)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def traffic_per_launch(kernel: str, workload: str):
+    """DRAM bytes (read+write) per launch of `kernel` from the committed ncu summary, or None."""
+    p = ROOT / "profiles" / "traffic.json"
+    if not p.exists():
+        return None
+    d = json.loads(p.read_text())
+    e = d.get(kernel, {}).get(workload)
+    return e.get("bytes_per_launch") if e else None
+
+
+def make_workload(device, n, seed=WORKLOAD["seed"]):
+    from dance_b200 import workloads
+    return workloads.clustered_u8(n, WORKLOAD["dim"], centroids=WORKLOAD["centroids"], noise=WORKLOAD["noise"],
+                                  seed=seed, device=device)
+
+
+def make_queries(device):
+    from dance_b200 import workloads
+    return workloads.clustered_u8(WORKLOAD["queries"], WORKLOAD["dim"], centroids=WORKLOAD["centroids"],
+                                  noise=WORKLOAD["noise"], seed=WORKLOAD["seed"], device=device, stream_offset=1)
+
+
+def oracle_sample_rate(sample_u8, threads, iters=1):
+    """Vectors/s of the CPU oracle building the sample (best of `iters`)."""
+    import oracle
+    best = None
+    for _ in range(iters):
+        t = time.perf_counter()
+        oracle.build_graph(sample_u8, WORKLOAD["R"], WORKLOAD["L"], WORKLOAD["C"], WORKLOAD["STEPS"],
+                           nthreads=threads)
+        dt = time.perf_counter() - t
+        best = dt if best is None else min(best, dt)
+    return len(sample_u8) / best, best
+
+
+# ------------------------------------------------------------------ reference arm
+def run_reference(args):
+    rank, world, local = dist_env()
+    if rank != 0:
+        return 0
+    import numpy as np
+    import torch
+    import oracle
+    oracle.build()
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    sample = make_workload(dev, REF_SAMPLE).cpu().numpy()
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        oracle.build_graph(sample, WORKLOAD["R"], WORKLOAD["L"], WORKLOAD["C"], WORKLOAD["STEPS"], nthreads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.build_graph(sample, WORKLOAD["R"], WORKLOAD["L"], WORKLOAD["C"], WORKLOAD["STEPS"], nthreads=threads)
+    dt = time.perf_counter() - t0
+    value = REF_SAMPLE * args.steps / dt
+    sample_desc = (f"first {REF_SAMPLE} vectors of the {WORKLOAD['name']} workload, full 4-round build per step, "
+                   f"{threads} OpenMP threads")
+    line = {
+        "impl": "reference", "metric": "vamana_build_vectors_per_s", "value": value, "unit": "vectors/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8", "data": "synthetic",
+        "config": config_dict(REF_SAMPLE),
+        "cpu_baseline": {"value": value, "unit": "vectors/s", "cores": threads, "kind": "port",
+                         "sample": sample_desc},
+        "e2e": {"value": value, "unit": "vectors/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": ("DANCE has no CPU implementation of this path and DiskANN's CPU Vamana is not vendored; "
+                 "this arm runs the C++ restatement of the reference algorithm (oracle/vamana_oracle.cpp)"),
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def config_dict(n):
+    return {"workload": WORKLOAD["name"], "N": n, "dim": WORKLOAD["dim"], "R": WORKLOAD["R"], "L": WORKLOAD["L"],
+            "C": WORKLOAD["C"], "STEPS": WORKLOAD["STEPS"], "alpha": WORKLOAD["alpha"], "iters": WORKLOAD["iters"],
+            "seed": WORKLOAD["seed"], "l2": "inputs larger than L2 (1.28 GB vector store), no flush"}
+
+
+# ------------------------------------------------------------------ our arm
+def search_algorithmic_bytes(rep, n, row_bytes, R, iters):
+    """Algorithmic DRAM bytes of the GreedySearch kernel over one build:
+    one gathered vector per distance evaluation, one adjacency row + degree
+    per expansion (+ the 8-byte expansion record written), and per vertex
+    and round its query vector, own row ids+distances and degree."""
+    per_eval = row_bytes
+    per_exp = R * 4 + 4 + 8
+    per_vertex = row_bytes + R * 8 + 4 + 4
+    return rep["search_evals"] * per_eval + rep["expansions"] * per_exp + iters * n * per_vertex
+
+
+def run_ours(args):
+    import numpy as np
+    import torch
+    import dance_b200
+    from dance_b200 import vamana, workloads
+    rank, world, local = dist_env()
+    if world > 1:
+        return run_sharded(args)
+    torch.cuda.set_device(local)
+    dance_b200.load()
+    lib = dance_b200.load()
+    n = args.n
+    R, L, C, S = WORKLOAD["R"], WORKLOAD["L"], WORKLOAD["C"], WORKLOAD["STEPS"]
+    x = make_workload("cuda", n)
+    store, stride = vamana.padded_store(x)
+    row_bytes = stride
+    ws = vamana.Workspace.create(n, R, L, C, S)
+    prm = dance_b200.default_params()
+    graph = torch.empty((n, R), dtype=torch.int32, device="cuda")
+    degree = torch.empty((n,), dtype=torch.int32, device="cuda")
+    dists = torch.empty((n, R), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+
+    def one_build():
+        with torch.cuda.stream(stream):
+            return vamana.build_resident(store, WORKLOAD["dim"], stride, R, L, C, S, params=prm, workspace=ws,
+                                         graph=graph, degree=degree, dists=dists, stream=stream)
+
+    for _ in range(args.warmup):
+        one_build()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    launches0 = lib.dance_kernel_launch_count()
+    reports = []
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        _, _, _, medoid = one_build()
+        reports.append(dance_b200.last_build_report())
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    launches = lib.dance_kernel_launch_count() - launches0
+    clk = clocks.stop()
+    elapsed = ev0.elapsed_time(ev1) * 1e-3
+    value = n * args.steps / elapsed
+
+    # roofline of the dominant kernel (GreedySearch), from the timed builds
+    peak, peak_kind = measured_peaks()
+    alg = sum(search_algorithmic_bytes(r, n, row_bytes, R, WORKLOAD["iters"]) for r in reports)
+    ksec = sum(r["search_kernel_seconds"] for r in reports)
+    achieved = alg / ksec / 1e9
+    launches_per_build = WORKLOAD["iters"]
+    stage = {k: statistics.mean(r[k] for r in reports) for k in reports[0] if k.endswith("_seconds")}
+    counters = {k: reports[-1][k] for k in ("search_evals", "expansions", "replay_pairs", "reverse_evals",
+                                            "prune_pairs")}
+    traffic = traffic_per_launch("search_kernel", WORKLOAD["name"])
+
+    line = {
+        "metric": "vamana_build_vectors_per_s", "value": value, "unit": "vectors/s", "n_gpus": 1,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8",
+        "data": "synthetic (seeded GPU generator, BASELINE.json configs[1] recipe)",
+        "config": config_dict(n),
+        "roofline": {"kernel": "search_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
+                     "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind,
+                     "traffic": traffic, "algorithmic_bytes_per_launch": alg / (len(reports) * launches_per_build),
+                     "avg_launch_ms": ksec / (len(reports) * launches_per_build) * 1e3},
+        "gpu_launches": int(launches),
+        "clocks": clk,
+        "stage_seconds": stage,
+        "counters_per_build": counters,
+    }
+    # ---- e2e through the reference C ABI with pinned host buffers
+    if not args.no_e2e:
+        hx = x.cpu().pin_memory()
+        hg = torch.empty((n, R), dtype=torch.int32).pin_memory()
+        hd = torch.empty((n,), dtype=torch.int32).pin_memory()
+        fn = lib.gpu_vamana_vnew2_build
+
+        def e2e_call():
+            rc = fn(ctypes.c_void_p(hx.data_ptr()), n, WORKLOAD["dim"], R, L, C, S, ctypes.c_void_p(hg.data_ptr()),
+                    ctypes.c_void_p(hd.data_ptr()))
+            dance_b200.check(rc, "gpu_vamana_vnew2_build")
+
+        e2e_call()  # warm-up (allocator, first-touch of pinned pages)
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e2e_call()
+        torch.cuda.synchronize()
+        e2e_dt = time.perf_counter() - t0
+        line["e2e"] = {"value": n * args.steps / e2e_dt, "unit": "vectors/s", "h2d_bytes_per_step": int(hx.numel()),
+                       "d2h_bytes_per_step": int(hg.numel() * 4 + hd.numel() * 4),
+                       "api": "gpu_vamana_vnew2_build (reference C ABI), pinned host buffers, wall clock",
+                       "warmup": 1}
+        # the C-ABI graph equals the device-resident build's graph
+        line["e2e"]["matches_resident_build"] = bool(torch.equal(hg.cuda(), graph))
+        del hx
+    # ---- recall@10 at L_search=100 on 10k queries against brute force
+    if not args.no_recall:
+        q = make_queries("cuda")
+        gt, _ = workloads.brute_force_knn(x, q, 10)
+        ids, _ = vamana.search_queries(store, WORKLOAD["dim"], stride, graph, R, medoid, q, 100, 10)
+        line["recall_at_10"] = {"L_search": 100, "queries": int(q.shape[0]),
+                                "ours": vamana.recall_at_k(ids.cpu().numpy(), gt.cpu().numpy())}
+        deg = degree.cpu().numpy()
+        line["graph"] = {"medoid": int(medoid), "avg_degree": float(deg.mean()), "max_degree": int(deg.max()),
+                         "min_degree": int(deg.min())}
+    # ---- CPU baseline: the oracle restatement on the host cores, bounded sample
+    if not args.no_cpu_baseline:
+        sample = x[:min(CPU_BASELINE_SAMPLE, n)].cpu().numpy()
+        threads = os.cpu_count() or 1
+        rate, secs = oracle_sample_rate(sample, threads)
+        line["cpu_baseline"] = {"value": rate, "unit": "vectors/s", "cores": threads, "kind": "port",
+                                "sample": f"first {len(sample)} vectors of the workload, full 4-round build "
+                                          f"({secs:.1f} s)"}
+    if args.ref_gpu:
+        line["reference_gpu"] = reference_gpu(x, store, stride, medoid, args)
+    print(json.dumps(line), flush=True)
+    ws.close()
+    return 0
+
+
+def reference_gpu(x, store, stride, our_medoid, args):
+    """The reference's own vnew2 builder (DANCE src/gpu_vamana_vnew2.cu compiled
+    for sm_100a, QUALITY profile) on the same vectors through its C ABI."""
+    import numpy as np
+    import torch
+    from dance_b200 import vamana, workloads
+    lib_path = ROOT / "oracle" / "_ref" / "libref_vnew2_quality.so"
+    if not lib_path.exists():
+        return {"unavailable": f"{lib_path.name} not built"}
+    lib = ctypes.CDLL(str(lib_path))
+    f = lib.gpu_vamana_vnew2_build
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.c_void_p] + [ctypes.c_uint32] * 6 + [ctypes.c_void_p] * 2
+    lib.gpu_vamana_vnew2_get_last_medoid.restype = ctypes.c_uint32
+    n = x.shape[0]
+    R, L, C, S = WORKLOAD["R"], WORKLOAD["L"], WORKLOAD["C"], WORKLOAD["STEPS"]
+    hx = x.cpu().numpy()
+    g = np.zeros((n, R), np.uint32)
+    d = np.zeros(n, np.uint32)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    rc = f(ctypes.c_void_p(hx.ctypes.data), n, WORKLOAD["dim"], R, L, C, S, ctypes.c_void_p(g.ctypes.data),
+           ctypes.c_void_p(d.ctypes.data))
+    dt = time.perf_counter() - t0
+    if rc != 0:
+        return {"unavailable": f"reference build returned {rc}"}
+    med = int(lib.gpu_vamana_vnew2_get_last_medoid())
+    q = make_queries("cuda")
+    gt, _ = workloads.brute_force_knn(x, q, 10)
+    gd = torch.from_numpy(g.view(np.int32)).cuda()
+    ids, _ = vamana.search_queries(store, WORKLOAD["dim"], stride, gd, R, med, q, 100, 10)
+    return {"e2e_vectors_per_s": n / dt, "seconds": dt, "recall_at_10": vamana.recall_at_k(ids.cpu().numpy(),
+                                                                                          gt.cpu().numpy()),
+            "medoid": med, "avg_degree": float(d.mean()),
+            "build": "DANCE vnew2 QUALITY profile (fp32/u8 distances, VAMANA_ITERS=4), nvcc 12.9 sm_100a"}
+
+
+def run_sharded(args):
+    raise SystemExit("multi-GPU build is not available in this build yet")
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,169 @@
+"""dance_b200 -- B200-native Vamana graph builder behind DANCE's C ABI.
+
+The product is the shared library ``libdance_b200.so`` (sm_100a CUDA kernels
+plus the C ABI of ``include/gpu_vamana_builder.h`` and ``include/dance_b200.h``).
+This package loads it with ctypes and offers a thin Python mirror of the
+reference interface.  There is no CPU fallback: importing ``lib`` raises if the
+library has not been built.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+__all__ = ["lib", "load", "LIB_PATH", "DanceError", "DANCE_U8", "DANCE_F16", "DANCE_F32",
+           "DanceVamanaParams", "GPUVamanaStats"]
+
+LIB_PATH = Path(__file__).resolve().parent / "libdance_b200.so"
+
+DANCE_U8, DANCE_F16, DANCE_F32 = 0, 1, 2
+
+
+class DanceError(RuntimeError):
+    """A libdance_b200 call returned a non-zero status."""
+
+
+class DanceVamanaParams(ctypes.Structure):
+    """Mirror of ``DanceVamanaParams`` in include/dance_b200.h."""
+    _fields_ = [
+        ("iters", ctypes.c_uint32),
+        ("alpha", ctypes.c_float),
+        ("init_random_seeds", ctypes.c_uint32),
+        ("final_min_degree", ctypes.c_uint32),
+        ("medoid_candidates", ctypes.c_uint32),
+        ("medoid_samples", ctypes.c_uint32),
+        ("coarse_warmup_iters", ctypes.c_uint32),
+        ("warmup_expand_steps", ctypes.c_uint32),
+        ("reverse_heavy_cap", ctypes.c_uint32),
+        ("reverse_heavy_threshold", ctypes.c_uint32),
+        ("reverse_heavy_sample", ctypes.c_uint32),
+        ("visited_log2", ctypes.c_uint32),
+        ("reserved", ctypes.c_uint32 * 8),
+    ]
+
+
+class GPUVamanaStats(ctypes.Structure):
+    """Mirror of ``GPUVamanaStats`` (reference include/gpu_vamana_builder.h:11-28)."""
+    _fields_ = [
+        ("medoid_seconds", ctypes.c_double),
+        ("h2d_seconds", ctypes.c_double),
+        ("search_online_insert_seconds", ctypes.c_double),
+        ("reverse_seconds", ctypes.c_double),
+        ("final_prune_seconds", ctypes.c_double),
+        ("d2h_seconds", ctypes.c_double),
+        ("gpu_build_seconds", ctypes.c_double),
+        ("distance_computations", ctypes.c_uint64),
+        ("online_insert_attempts", ctypes.c_uint64),
+        ("online_insert_mutations", ctypes.c_uint64),
+        ("reverse_candidate_overflows", ctypes.c_uint64),
+        ("reverse_proposals", ctypes.c_uint64),
+        ("reverse_touched_rows", ctypes.c_uint64),
+        ("reverse_csr_seconds", ctypes.c_double),
+        ("selective_active_nodes", ctypes.c_uint32),
+    ]
+
+
+class DanceBuildReport(ctypes.Structure):
+    """Mirror of ``DanceBuildReport`` in include/dance_b200.h."""
+    _fields_ = [(n, ctypes.c_double) for n in (
+        "medoid_seconds", "search_seconds", "search_kernel_seconds", "replay_seconds", "reverse_seconds",
+        "prune_seconds", "total_seconds")] + [(n, ctypes.c_uint64) for n in (
+            "search_evals", "expansions", "replay_pairs", "reverse_evals", "prune_pairs")] + [
+        ("reserved", ctypes.c_uint64 * 3)]
+
+
+_P = ctypes.c_void_p
+_U32 = ctypes.c_uint32
+_U64 = ctypes.c_uint64
+_I = ctypes.c_int
+_F = ctypes.c_float
+_PU32 = ctypes.POINTER(ctypes.c_uint32)
+_PU64 = ctypes.POINTER(ctypes.c_uint64)
+
+# name -> (restype, argtypes); every entry point declared in include/*.h.
+SIGNATURES = {
+    # reference C ABI (include/gpu_vamana_builder.h)
+    "gpu_vamana_build": (_I, [_P, _U32, _U32, _U32, _U32, _U32, _U32, _P, _P]),
+    "gpu_vamana_build_float": (_I, [_P, _U32, _U32, _U32, _U32, _U32, _U32, _P, _P]),
+    "gpu_vamana_vnew2_build": (_I, [_P, _U32, _U32, _U32, _U32, _U32, _U32, _P, _P]),
+    "gpu_vamana_vnew2_build_float": (_I, [_P, _U32, _U32, _U32, _U32, _U32, _U32, _P, _P]),
+    "gpu_vamana_vnew2_build_device": (_I, [_P, _U32, _U32, _U32, _U32, _U32, _U32, _P, _P, _P]),
+    "gpu_vamana_vnew2_build_device_float": (_I, [_P, _U32, _U32, _U32, _U32, _U32, _U32, _P, _P, _P]),
+    "gpu_vamana_get_last_medoid": (_U32, []),
+    "gpu_vamana_get_last_stats": (None, [_P]),
+    "gpu_vamana_vnew2_get_last_medoid": (_U32, []),
+    "gpu_vamana_vnew2_get_last_stats": (None, [_P]),
+    # additive C ABI (include/dance_b200.h)
+    "dance_vamana_default_params": (None, [_P]),
+    "dance_last_error": (ctypes.c_char_p, []),
+    "dance_kernel_launch_count": (_U64, []),
+    "dance_last_build_report": (_I, [_P]),
+    "dance_workspace_create": (_I, [_U32, _U32, _U32, _U32, _U32, _P]),
+    "dance_workspace_destroy": (None, [_P]),
+    "dance_vamana_build_resident": (_I, [_I, _P, _U64, _U32, _U32, _U32, _U32, _U32, _U32, _P, _P, _P, _P, _P,
+                                         _PU32, _P]),
+    "dance_stage_medoid": (_I, [_I, _P, _U64, _U32, _U32, _U32, _U32, _P, _P, _P, _P]),
+    "dance_stage_init": (_I, [_I, _P, _U64, _U32, _U32, _U32, _P, _P, _P, _P]),
+    "dance_stage_search": (_I, [_I, _P, _U64, _U32, _U32, _U32, _U32, _U32, _U32, _U32, _U32, _P, _P, _P, _P, _P,
+                                _P, _U32, _P]),
+    "dance_stage_replay": (_I, [_I, _P, _U64, _U32, _U32, _U32, _U32, _F, _P, _P, _P, _P, _P, _P, _U32, _P, _P, _P,
+                                _P]),
+    "dance_stage_reverse_merge": (_I, [_I, _P, _U64, _U32, _U32, _U32, _U32, _P, _P, _P, _P, _P, _PU64, _P]),
+    "dance_stage_prune": (_I, [_I, _P, _U64, _U32, _U32, _U32, _U32, _F, _U32, _P, _P, _P, _P, _P, _P, _P]),
+    "dance_search_queries": (_I, [_I, _P, _U64, _U32, _U32, _P, _U32, _U32, _P, _U64, _U32, _U32, _U32, _U32, _P,
+                                  _P, _P]),
+}
+
+_lib = None
+
+
+def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
+    """Load libdance_b200.so and declare every exported signature.
+
+    Raises FileNotFoundError when the library has not been built: the CUDA
+    path is the only path (build it with ``python -m dance_b200.build``).
+    """
+    global _lib
+    if _lib is not None and path is None:
+        return _lib
+    p = Path(path) if path else LIB_PATH
+    if not p.exists():
+        raise FileNotFoundError(
+            f"{p} is missing: build the CUDA library with `python -m dance_b200.build` "
+            "(there is no CPU fallback)")
+    cdll = ctypes.CDLL(str(p))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(cdll, name)
+        fn.restype = res
+        fn.argtypes = args
+    if path is None:
+        _lib = cdll
+    return cdll
+
+
+def __getattr__(name):
+    if name == "lib":
+        return load()
+    raise AttributeError(name)
+
+
+def check(rc: int, what: str = "libdance_b200") -> None:
+    """Raise DanceError with the library's last message if rc != 0."""
+    if rc != 0:
+        msg = load().dance_last_error()
+        raise DanceError(f"{what} failed with status {rc}: {msg.decode() if msg else ''}")
+
+
+def last_build_report() -> dict:
+    r = DanceBuildReport()
+    check(load().dance_last_build_report(ctypes.byref(r)), "dance_last_build_report")
+    return {n: getattr(r, n) for n, _ in r._fields_ if n != "reserved"}
+
+
+def default_params(**overrides) -> DanceVamanaParams:
+    p = DanceVamanaParams()
+    load().dance_vamana_default_params(ctypes.byref(p))
+    for k, v in overrides.items():
+        setattr(p, k, v)
+    return p

@@ -1,0 +1,1467 @@
+// vamana_kernels.cuh -- sm_100a kernels of the standard (vnew2) Vamana build.
+//
+// One round of the build (reference src/gpu_vamana_vnew2.cu:2517-2637) is
+//   search_kernel      batched GreedySearch of every vertex on the frozen
+//                      graph; records the expansion sequence  (ref :1119-1439)
+//   replay_kernel      online RobustInsert of that sequence into C-wide
+//                      work rows, pair distances from a shared-memory
+//                      vector cache                            (ref :759-877)
+//   rev_count/scan/fill  exact CSR of the reverse edges        (ref :1604-1661)
+//   merge_kernel (+ heavy_merge_kernel)  reverse-edge merge in ascending
+//                      source order                            (ref :1722-1814)
+//   prune_kernel       RobustPrune(alpha) + last-round fill    (ref :1893-2147)
+// plus medoid_score/medoid_argmin (ref :1032-1064, :2445-2479) and
+// init_graph (ref :1066-1117).
+//
+// Layout in HBM: vectors row-major with a 16-byte-multiple stride; graph
+// rows R-wide (ids uint32, INVALID-padded) with an aligned distance row
+// (float, FLT_MAX-padded); work rows C-wide; expansion lists exp_stride-wide.
+#pragma once
+
+#include "dance_common.cuh"
+
+namespace dance
+{
+
+constexpr int kWarpsPerBlock = 4;
+constexpr int kBlockThreads = kWarpsPerBlock * 32;
+
+struct StoreView
+{
+    const uint8_t *data;
+    uint64_t stride;  // bytes between rows (multiple of 16)
+    uint32_t nchunks; // 16-byte chunks per row that hold data
+    uint32_t N;
+};
+
+__device__ __forceinline__ int warp_id_in_block() { return threadIdx.x >> 5; }
+__device__ __forceinline__ int lane_id() { return threadIdx.x & 31; }
+
+__device__ __forceinline__ uint32_t visited_slot(uint32_t id, uint32_t log2h)
+{
+    return (id * 2654435761u) >> (32u - log2h);
+}
+
+// Per-warp scratch of the search kernels.
+struct SearchSmem
+{
+    uint64_t *pk0;  // two pool key buffers of Lcap keys, sorted ascending
+    uint8_t *pf0;   // two expanded-flag buffers aligned with the keys
+    uint32_t Lcap;
+    uint32_t *bid;  // batch ids (64)
+    float *bd;      // batch distances (64)
+    uint64_t *bkey; // sorted, deduplicated batch keys (64)
+    uint32_t *vis;  // visited table (1 << log2h ids)
+    __device__ __forceinline__ uint64_t *pk(int b) const { return pk0 + (uint32_t)b * Lcap; }
+    __device__ __forceinline__ uint8_t *pf(int b) const { return pf0 + (uint32_t)b * Lcap; }
+};
+
+__host__ __device__ __forceinline__ uint32_t align16(uint32_t x) { return (x + 15u) & ~15u; }
+
+__host__ __device__ __forceinline__ uint32_t search_smem_per_warp(uint32_t Lcap, uint32_t log2h)
+{
+    return align16(16u * Lcap) + align16(2u * Lcap) + 256u + 256u + 512u + align16(4u << log2h);
+}
+
+__device__ __forceinline__ SearchSmem carve_search_smem(uint8_t *base, uint32_t Lcap, uint32_t log2h)
+{
+    SearchSmem s;
+    uint8_t *p = base;
+    s.Lcap = Lcap;
+    s.pk0 = reinterpret_cast<uint64_t *>(p);
+    p += align16(16u * Lcap);
+    s.pf0 = p;
+    p += align16(2u * Lcap);
+    s.bid = reinterpret_cast<uint32_t *>(p);
+    p += 256;
+    s.bd = reinterpret_cast<float *>(p);
+    p += 256;
+    s.bkey = reinterpret_cast<uint64_t *>(p);
+    p += 512;
+    s.vis = reinterpret_cast<uint32_t *>(p);
+    return s;
+}
+
+// Warp-uniform pool state (identical in every lane).
+struct PoolState
+{
+    int P;   // entries in the pool
+    int cur; // which pk/pf buffer is current
+    int L;   // capacity
+};
+
+// Inserts up to 64 candidates (two per lane; kInvalid = none) into the pool.
+// Candidates already in the visited table are skipped (they were evaluated
+// before, so re-inserting them could not change the pool); the rest are
+// evaluated (unless their distance is given), keyed by (distance, id),
+// sorted, deduplicated and merged so the pool keeps the L smallest keys.
+// Returns the number of distances evaluated.
+template <int DT, int CPL>
+__device__ __forceinline__ int pool_insert_batch(const SearchSmem &sm, PoolState &ps, uint32_t log2h,
+                                                 const StoreView &st, const uint4 (&q)[CPL], uint32_t id0,
+                                                 uint32_t id1, float d0, float d1, bool have_dist, int lane)
+{
+    bool ok0 = id0 != kInvalid;
+    bool ok1 = id1 != kInvalid;
+    if (ok0)
+    {
+        const uint32_t s = visited_slot(id0, log2h);
+        if (sm.vis[s] == id0)
+            ok0 = false;
+        else
+            sm.vis[s] = id0;
+    }
+    if (ok1)
+    {
+        const uint32_t s = visited_slot(id1, log2h);
+        if (sm.vis[s] == id1)
+            ok1 = false;
+        else
+            sm.vis[s] = id1;
+    }
+    const unsigned b0 = __ballot_sync(kFull, ok0);
+    const unsigned b1 = __ballot_sync(kFull, ok1);
+    const int m = __popc(b0) + __popc(b1);
+    if (m == 0)
+        return 0;
+    const unsigned lt = (1u << lane) - 1u;
+    if (ok0)
+    {
+        const int pos = __popc(b0 & lt);
+        sm.bid[pos] = id0;
+        sm.bd[pos] = d0;
+    }
+    if (ok1)
+    {
+        const int pos = __popc(b0) + __popc(b1 & lt);
+        sm.bid[pos] = id1;
+        sm.bd[pos] = d1;
+    }
+    __syncwarp();
+    if (!have_dist)
+    {
+        eval_candidates<DT, CPL>(st.data, st.stride, st.nchunks, q, sm.bid, sm.bd, m, lane);
+        __syncwarp();
+    }
+    const uint64_t maxk = (ps.P >= ps.L) ? sm.pk(ps.cur)[ps.L - 1] : kKeyMax;
+    const int e0 = 2 * lane, e1 = 2 * lane + 1;
+    uint64_t k0 = e0 < m ? make_key(sm.bd[e0], sm.bid[e0]) : kKeyMax;
+    uint64_t k1 = e1 < m ? make_key(sm.bd[e1], sm.bid[e1]) : kKeyMax;
+    if (k0 >= maxk)
+        k0 = kKeyMax;
+    if (k1 >= maxk)
+        k1 = kKeyMax;
+    const bool any = __any_sync(kFull, (k0 != kKeyMax) || (k1 != kKeyMax));
+    if (!any)
+        return m;
+    warp_sort64(k0, k1, lane);
+    const uint64_t prev0 = __shfl_up_sync(kFull, k1, 1);
+    bool keep0 = k0 != kKeyMax && !(lane > 0 && prev0 == k0);
+    bool keep1 = k1 != kKeyMax && k1 != k0;
+    const uint64_t *pool = sm.pk(ps.cur);
+    if (keep0)
+    {
+        const int p = lower_bound_u64(pool, ps.P, k0);
+        if (p < ps.P && pool[p] == k0)
+            keep0 = false;
+    }
+    if (keep1)
+    {
+        const int p = lower_bound_u64(pool, ps.P, k1);
+        if (p < ps.P && pool[p] == k1)
+            keep1 = false;
+    }
+    const unsigned c0 = __ballot_sync(kFull, keep0);
+    const unsigned c1 = __ballot_sync(kFull, keep1);
+    const int m2 = __popc(c0) + __popc(c1);
+    if (m2 == 0)
+        return m;
+    {
+        const int before = __popc(c0 & lt) + __popc(c1 & lt);
+        if (keep0)
+            sm.bkey[before] = k0;
+        if (keep1)
+            sm.bkey[before + (keep0 ? 1 : 0)] = k1;
+    }
+    __syncwarp();
+    const int nxt = ps.cur ^ 1;
+    for (int i = lane; i < ps.P; i += 32)
+    {
+        const uint64_t key = pool[i];
+        const int pos = i + lower_bound_u64(sm.bkey, m2, key);
+        if (pos < ps.L)
+        {
+            sm.pk(nxt)[pos] = key;
+            sm.pf(nxt)[pos] = sm.pf(ps.cur)[i];
+        }
+    }
+    for (int j = lane; j < m2; j += 32)
+    {
+        const uint64_t key = sm.bkey[j];
+        const int pos = j + lower_bound_u64(pool, ps.P, key);
+        if (pos < ps.L)
+        {
+            sm.pk(nxt)[pos] = key;
+            sm.pf(nxt)[pos] = 0;
+        }
+    }
+    __syncwarp();
+    ps.P = min(ps.P + m2, ps.L);
+    ps.cur = nxt;
+    return m;
+}
+
+// Index of the first unexpanded pool entry (smallest key), -1 if none.
+__device__ __forceinline__ int pool_select(const SearchSmem &sm, const PoolState &ps, int lane)
+{
+    for (int base = 0; base < ps.P; base += 32)
+    {
+        const int i = base + lane;
+        const bool u = i < ps.P && sm.pf(ps.cur)[i] == 0;
+        const unsigned m = __ballot_sync(kFull, u);
+        if (m)
+            return base + __ffs(m) - 1;
+    }
+    return -1;
+}
+
+__device__ __forceinline__ void clear_visited(uint32_t *vis, uint32_t log2h, int lane)
+{
+    uint4 *v4 = reinterpret_cast<uint4 *>(vis);
+    const uint32_t n4 = (1u << log2h) >> 2;
+    const uint4 inv = make_uint4(kInvalid, kInvalid, kInvalid, kInvalid);
+    for (uint32_t i = lane; i < n4; i += 32)
+        v4[i] = inv;
+    __syncwarp();
+}
+
+// ====================================================================== medoid
+template <int DT, int CPL>
+__global__ void __launch_bounds__(kBlockThreads) medoid_score_kernel(StoreView st, uint32_t nc, uint32_t ns,
+                                                                     float *scores, uint32_t *cand_ids)
+{
+    const int lane = lane_id();
+    const uint32_t w = blockIdx.x * kWarpsPerBlock + warp_id_in_block();
+    if (w >= nc)
+        return;
+    const int g = lane >> 3, gl = lane & 7;
+    const uint32_t cand = hash_u32(w * 9973u + 17u) % st.N;
+    uint4 q[CPL];
+    load_frag<CPL>(q, st.data + (uint64_t)cand * st.stride, st.nchunks, gl);
+    constexpr int U = Unroll<CPL>::value;
+    float sum = 0.0f;
+    for (uint32_t base = 0; base < ns; base += 4 * U)
+    {
+        uint4 buf[U][CPL];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+        {
+            const uint32_t idx = base + 4 * u + g;
+            if (idx < ns)
+            {
+                const uint32_t smp = hash_u32(idx * 10007u + 131u) % st.N;
+                load_frag<CPL>(buf[u], st.data + (uint64_t)smp * st.stride, st.nchunks, gl);
+            }
+            else
+            {
+#pragma unroll
+                for (int t = 0; t < CPL; ++t)
+                    buf[u][t] = make_uint4(0u, 0u, 0u, 0u);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+        {
+            const float d = GroupDist<DT, CPL>::eval(q, buf[u], st.nchunks, gl);
+#pragma unroll
+            for (int gg = 0; gg < 4; ++gg)
+            {
+                const float dg = __shfl_sync(kFull, d, 8 * gg);
+                const uint32_t idx = base + 4 * u + gg;
+                if (lane == 0 && idx < ns)
+                {
+                    const uint32_t smp = hash_u32(idx * 10007u + 131u) % st.N;
+                    if (smp != cand)
+                        sum = __fadd_rn(sum, dg);
+                }
+            }
+        }
+    }
+    if (lane == 0)
+    {
+        scores[w] = __fdiv_rn(sum, (float)ns);
+        cand_ids[w] = cand;
+    }
+}
+
+// Lowest score, first candidate on ties; entry 0 if no finite score.
+__global__ void __launch_bounds__(1024) medoid_argmin_kernel(const float *scores, const uint32_t *cand_ids,
+                                                             uint32_t nc, uint32_t *medoid)
+{
+    __shared__ float s_v[32];
+    __shared__ int s_i[32];
+    float best = FLT_MAX;
+    int bi = -1;
+    for (uint32_t i = threadIdx.x; i < nc; i += blockDim.x)
+    {
+        const float v = scores[i];
+        if (v < best)
+        {
+            best = v;
+            bi = (int)i;
+        }
+    }
+    for (int off = 16; off > 0; off >>= 1)
+    {
+        const float ov = __shfl_down_sync(kFull, best, off);
+        const int oi = __shfl_down_sync(kFull, bi, off);
+        if (oi >= 0 && (ov < best || (ov == best && (bi < 0 || oi < bi))))
+        {
+            best = ov;
+            bi = oi;
+        }
+    }
+    if ((threadIdx.x & 31) == 0)
+    {
+        s_v[threadIdx.x >> 5] = best;
+        s_i[threadIdx.x >> 5] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0)
+    {
+        float b = FLT_MAX;
+        int idx = -1;
+        for (int w = 0; w < (int)((blockDim.x + 31) >> 5); ++w)
+        {
+            if (s_i[w] >= 0 && (s_v[w] < b || (s_v[w] == b && (idx < 0 || s_i[w] < idx))))
+            {
+                b = s_v[w];
+                idx = s_i[w];
+            }
+        }
+        *medoid = idx >= 0 ? cand_ids[idx] : 0u;
+    }
+}
+
+// ====================================================================== init
+template <int DT, int CPL>
+__global__ void __launch_bounds__(kBlockThreads) init_graph_kernel(StoreView st, uint32_t R, uint32_t *cur_ids,
+                                                                   float *cur_dists, uint32_t *degree, uint32_t v0,
+                                                                   uint32_t v1)
+{
+    const int lane = lane_id();
+    const int g = lane >> 3, gl = lane & 7;
+    constexpr int U = Unroll<CPL>::value;
+    for (uint32_t v = v0 + blockIdx.x * kWarpsPerBlock + warp_id_in_block(); v < v1;
+         v += gridDim.x * kWarpsPerBlock)
+    {
+        uint4 q[CPL];
+        load_frag<CPL>(q, st.data + (uint64_t)v * st.stride, st.nchunks, gl);
+        for (uint32_t base = 0; base < R; base += 4 * U)
+        {
+            uint4 buf[U][CPL];
+            uint32_t nb[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+            {
+                const uint32_t idx = base + 4 * u + g;
+                nb[u] = kInvalid;
+                if (idx < R)
+                {
+                    nb[u] = det_neighbor(v, idx, st.N);
+                    if (st.N <= 1 || nb[u] >= st.N || nb[u] == v)
+                        nb[u] = kInvalid;
+                }
+                if (nb[u] != kInvalid)
+                    load_frag<CPL>(buf[u], st.data + (uint64_t)nb[u] * st.stride, st.nchunks, gl);
+                else
+                {
+#pragma unroll
+                    for (int t = 0; t < CPL; ++t)
+                        buf[u][t] = make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+            {
+                const uint32_t idx = base + 4 * u + g;
+                const float d = GroupDist<DT, CPL>::eval(q, buf[u], st.nchunks, gl);
+                if (idx < R && gl == 0)
+                {
+                    cur_ids[(uint64_t)v * R + idx] = nb[u];
+                    cur_dists[(uint64_t)v * R + idx] = nb[u] != kInvalid ? d : FLT_MAX;
+                }
+            }
+        }
+        if (lane == 0)
+            degree[v] = st.N > 1 ? R : 0u;
+    }
+}
+
+// ====================================================================== search
+struct SearchParams
+{
+    StoreView st;
+    uint32_t R, L, Lcap, steps, seeds, log2h;
+    uint32_t entry;            // used when entry_ptr == nullptr
+    const uint32_t *entry_ptr; // device scalar (medoid), optional
+    const uint32_t *cur_ids;
+    const float *cur_dists;
+    const uint32_t *degree;
+    uint32_t *exp_ids;
+    float *exp_dists;
+    uint32_t *exp_count;
+    uint32_t exp_stride;
+    uint32_t v0, v1;
+    unsigned long long *counters; // [0] distance evaluations, [1] expansions
+};
+
+template <int DT, int CPL>
+__global__ void __launch_bounds__(kBlockThreads) search_kernel(SearchParams p)
+{
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    const int lane = lane_id();
+    const int gl = lane & 7;
+    const uint32_t per_warp = search_smem_per_warp(p.Lcap, p.log2h);
+    const SearchSmem sm = carve_search_smem(smem_raw + warp_id_in_block() * per_warp, p.Lcap, p.log2h);
+    const StoreView &st = p.st;
+    const uint32_t N = st.N;
+    const uint32_t entry = p.entry_ptr ? *p.entry_ptr : p.entry;
+    unsigned long long evals = 0, expansions = 0;
+
+    for (uint32_t v = p.v0 + blockIdx.x * kWarpsPerBlock + warp_id_in_block(); v < p.v1;
+         v += gridDim.x * kWarpsPerBlock)
+    {
+        uint4 q[CPL];
+        load_frag<CPL>(q, st.data + (uint64_t)v * st.stride, st.nchunks, gl);
+        clear_visited(sm.vis, p.log2h, lane);
+        PoolState ps{0, 0, (int)p.L};
+
+        // Seeds: entry point and hash seeds (distances computed) ...
+        uint32_t sid = kInvalid;
+        if (lane == 0)
+        {
+            if (entry < N && entry != v)
+                sid = entry;
+        }
+        else if ((uint32_t)lane <= p.seeds)
+        {
+            const uint32_t s = det_neighbor(v, (uint32_t)(lane - 1) + 1024u, N);
+            if (s < N && s != v)
+                sid = s;
+        }
+        evals += pool_insert_batch<DT, CPL>(sm, ps, p.log2h, st, q, sid, kInvalid, 0.0f, 0.0f, false, lane);
+        // ... then the vertex's own neighbours with their stored distances.
+        const uint32_t deg_self = min(p.degree[v], p.R);
+        for (uint32_t b = 0; b < deg_self; b += 64)
+        {
+            const uint32_t i0 = b + lane, i1 = b + 32 + lane;
+            uint32_t a0 = kInvalid, a1 = kInvalid;
+            float f0 = FLT_MAX, f1 = FLT_MAX;
+            if (i0 < deg_self)
+            {
+                a0 = p.cur_ids[(uint64_t)v * p.R + i0];
+                if (a0 < N && a0 != v)
+                    f0 = p.cur_dists[(uint64_t)v * p.R + i0];
+                else
+                    a0 = kInvalid;
+            }
+            if (i1 < deg_self)
+            {
+                a1 = p.cur_ids[(uint64_t)v * p.R + i1];
+                if (a1 < N && a1 != v)
+                    f1 = p.cur_dists[(uint64_t)v * p.R + i1];
+                else
+                    a1 = kInvalid;
+            }
+            pool_insert_batch<DT, CPL>(sm, ps, p.log2h, st, q, a0, a1, f0, f1, true, lane);
+        }
+
+        uint32_t nexp = 0;
+        for (uint32_t step = 0; step < p.steps; ++step)
+        {
+            const int sel = pool_select(sm, ps, lane);
+            if (sel < 0)
+                break;
+            const uint64_t key = sm.pk(ps.cur)[sel];
+            const uint32_t x = key_id(key);
+            if (lane == 0)
+            {
+                sm.pf(ps.cur)[sel] = 1;
+                p.exp_ids[(uint64_t)v * p.exp_stride + step] = x;
+                p.exp_dists[(uint64_t)v * p.exp_stride + step] = key_dist(key);
+            }
+            __syncwarp();
+            ++nexp;
+            const uint32_t degx = min(p.degree[x], p.R);
+            const uint32_t *row = p.cur_ids + (uint64_t)x * p.R;
+            for (uint32_t b = 0; b < p.R; b += 64)
+            {
+                const uint32_t i0 = b + lane, i1 = b + 32 + lane;
+                uint32_t a0 = i0 < degx ? row[i0] : kInvalid;
+                uint32_t a1 = i1 < degx ? row[i1] : kInvalid;
+                if (a0 >= N || a0 == v)
+                    a0 = kInvalid;
+                if (a1 >= N || a1 == v)
+                    a1 = kInvalid;
+                evals += pool_insert_batch<DT, CPL>(sm, ps, p.log2h, st, q, a0, a1, 0.0f, 0.0f, false, lane);
+            }
+        }
+        if (lane == 0)
+            p.exp_count[v] = nexp;
+        expansions += nexp;
+    }
+    if (lane == 0 && p.counters)
+    {
+        atomicAdd(&p.counters[0], evals);
+        atomicAdd(&p.counters[1], expansions);
+    }
+}
+
+// Query search (recall harness): best-first from `start` until every pool
+// entry is expanded; the first K pool keys are the result.
+struct QueryParams
+{
+    StoreView st;
+    const uint8_t *queries;
+    uint64_t qstride;
+    uint32_t nq;
+    const uint32_t *graph;
+    uint32_t R, L, Lcap, K, log2h, start;
+    uint32_t *out_ids;
+    float *out_dists;
+};
+
+template <int DT, int CPL>
+__global__ void __launch_bounds__(kBlockThreads) query_search_kernel(QueryParams p)
+{
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    const int lane = lane_id();
+    const int gl = lane & 7;
+    const uint32_t per_warp = search_smem_per_warp(p.Lcap, p.log2h);
+    const SearchSmem sm = carve_search_smem(smem_raw + warp_id_in_block() * per_warp, p.Lcap, p.log2h);
+    const uint32_t N = p.st.N;
+    for (uint32_t qi = blockIdx.x * kWarpsPerBlock + warp_id_in_block(); qi < p.nq; qi += gridDim.x * kWarpsPerBlock)
+    {
+        uint4 q[CPL];
+        load_frag<CPL>(q, p.queries + (uint64_t)qi * p.qstride, p.st.nchunks, gl);
+        clear_visited(sm.vis, p.log2h, lane);
+        PoolState ps{0, 0, (int)p.L};
+        const uint32_t s0 = (lane == 0 && p.start < N) ? p.start : kInvalid;
+        pool_insert_batch<DT, CPL>(sm, ps, p.log2h, p.st, q, s0, kInvalid, 0.0f, 0.0f, false, lane);
+        while (true)
+        {
+            const int sel = pool_select(sm, ps, lane);
+            if (sel < 0)
+                break;
+            const uint32_t x = key_id(sm.pk(ps.cur)[sel]);
+            if (lane == 0)
+                sm.pf(ps.cur)[sel] = 1;
+            __syncwarp();
+            const uint32_t *row = p.graph + (uint64_t)x * p.R;
+            for (uint32_t b = 0; b < p.R; b += 64)
+            {
+                const uint32_t i0 = b + lane, i1 = b + 32 + lane;
+                uint32_t a0 = i0 < p.R ? row[i0] : kInvalid;
+                uint32_t a1 = i1 < p.R ? row[i1] : kInvalid;
+                if (a0 >= N)
+                    a0 = kInvalid;
+                if (a1 >= N)
+                    a1 = kInvalid;
+                pool_insert_batch<DT, CPL>(sm, ps, p.log2h, p.st, q, a0, a1, 0.0f, 0.0f, false, lane);
+            }
+        }
+        for (uint32_t k = lane; k < p.K; k += 32)
+        {
+            const bool have = (int)k < ps.P;
+            const uint64_t key = have ? sm.pk(ps.cur)[k] : kKeyMax;
+            p.out_ids[(uint64_t)qi * p.K + k] = have ? key_id(key) : kInvalid;
+            p.out_dists[(uint64_t)qi * p.K + k] = have ? key_dist(key) : FLT_MAX;
+        }
+        __syncwarp();
+    }
+}
+
+// ====================================================================== replay
+struct ReplayParams
+{
+    StoreView st;
+    uint32_t R, C;
+    float alpha;
+    const uint32_t *cur_ids;
+    const float *cur_dists;
+    const uint32_t *degree;
+    const uint32_t *exp_ids;
+    const float *exp_dists;
+    const uint32_t *exp_count;
+    uint32_t exp_stride;
+    uint32_t *work_ids;
+    float *work_dists;
+    uint32_t *work_deg;
+    uint32_t v0, v1;
+    uint32_t row_bytes;   // nchunks * 16
+    uint32_t cache_rows;  // R + exp_stride
+    uint32_t per_warp;    // smem bytes per warp
+    unsigned long long *counters; // [2] pair evaluations
+};
+
+__host__ __device__ __forceinline__ uint32_t replay_smem_per_warp(uint32_t C, uint32_t cache_rows, uint32_t row_bytes)
+{
+    return cache_rows * row_bytes + align16(4u * cache_rows) + align16(4u * C) + align16(4u * C) + align16(2u * C) +
+           align16(2u * C);
+}
+
+// Warp argmax over (value, slot) pairs: larger value wins, lower slot on ties.
+__device__ __forceinline__ void warp_argmax_lowslot(float &v, int &s)
+{
+    for (int off = 16; off > 0; off >>= 1)
+    {
+        const float ov = __shfl_down_sync(kFull, v, off);
+        const int os = __shfl_down_sync(kFull, s, off);
+        if (os >= 0 && (s < 0 || ov > v || (ov == v && os < s)))
+        {
+            v = ov;
+            s = os;
+        }
+    }
+    v = __shfl_sync(kFull, v, 0);
+    s = __shfl_sync(kFull, s, 0);
+}
+
+template <int DT, int CPL>
+__global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
+{
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    const int lane = lane_id();
+    const int g = lane >> 3, gl = lane & 7;
+    uint8_t *base = smem_raw + warp_id_in_block() * p.per_warp;
+    uint8_t *cache = base;
+    uint8_t *q = cache + p.cache_rows * p.row_bytes;
+    uint32_t *gid = reinterpret_cast<uint32_t *>(q);
+    q += align16(4u * p.cache_rows);
+    uint32_t *wid = reinterpret_cast<uint32_t *>(q);
+    q += align16(4u * p.C);
+    float *wd = reinterpret_cast<float *>(q);
+    q += align16(4u * p.C);
+    uint16_t *wu = reinterpret_cast<uint16_t *>(q);
+    q += align16(2u * p.C);
+    uint16_t *lst = reinterpret_cast<uint16_t *>(q);
+    q += align16(2u * p.C);
+    const uint32_t N = p.st.N;
+    const uint32_t C = p.C;
+    unsigned long long pairs = 0;
+
+    for (uint32_t v = p.v0 + blockIdx.x * kWarpsPerBlock + warp_id_in_block(); v < p.v1;
+         v += gridDim.x * kWarpsPerBlock)
+    {
+        const uint32_t deg_self = min(p.degree[v], p.R);
+        for (uint32_t i = lane; i < C; i += 32)
+        {
+            uint32_t nb = kInvalid;
+            float d = FLT_MAX;
+            uint16_t u = 0xFFFFu;
+            if (i < deg_self)
+            {
+                nb = p.cur_ids[(uint64_t)v * p.R + i];
+                if (nb < N && nb != v)
+                {
+                    d = p.cur_dists[(uint64_t)v * p.R + i];
+                    u = (uint16_t)i;
+                }
+                else
+                    nb = kInvalid;
+            }
+            wid[i] = nb;
+            wd[i] = d;
+            wu[i] = u;
+        }
+        const uint32_t cnt = min(p.exp_count[v], p.exp_stride);
+        for (uint32_t i = lane; i < p.R + cnt; i += 32)
+        {
+            uint32_t id;
+            if (i < p.R)
+            {
+                id = i < deg_self ? p.cur_ids[(uint64_t)v * p.R + i] : v;
+                if (id >= N)
+                    id = v;
+            }
+            else
+            {
+                id = p.exp_ids[(uint64_t)v * p.exp_stride + (i - p.R)];
+                if (id >= N)
+                    id = v;
+            }
+            gid[i] = id;
+        }
+        __syncwarp();
+        // rows [0, deg_self) and [R, R + cnt) of the cache
+        gather_rows_to_smem(p.st.data, p.st.stride, p.st.nchunks, gid, (int)deg_self, cache, p.row_bytes, lane);
+        gather_rows_to_smem(p.st.data, p.st.stride, p.st.nchunks, gid + p.R, (int)cnt, cache + p.R * p.row_bytes,
+                            p.row_bytes, lane);
+        __syncwarp();
+        uint32_t wdeg = deg_self;
+
+        for (uint32_t k = 0; k < cnt; ++k)
+        {
+            const uint32_t x = p.exp_ids[(uint64_t)v * p.exp_stride + k];
+            const float dx = p.exp_dists[(uint64_t)v * p.exp_stride + k];
+            if (x >= N || x == v)
+                continue;
+            const uint32_t deg = min(wdeg, C);
+            bool present = false;
+            for (uint32_t b = 0; b < deg; b += 32)
+            {
+                const uint32_t i = b + lane;
+                if (__any_sync(kFull, i < deg && wid[i] == x))
+                {
+                    present = true;
+                    break;
+                }
+            }
+            if (present)
+                continue;
+            uint4 xf[CPL];
+            load_frag_smem<CPL>(xf, cache + (p.R + k) * p.row_bytes, p.st.nchunks, gl);
+
+            // Occlusion: some kept y with d(v,y) <= d(v,x) and alpha*d(y,x) <= d(v,x).
+            int na = 0;
+            for (uint32_t b = 0; b < deg; b += 32)
+            {
+                const uint32_t i = b + lane;
+                bool in = false;
+                if (i < deg)
+                {
+                    const uint32_t y = wid[i];
+                    in = y < N && y != v && wd[i] <= dx;
+                }
+                const unsigned bm = __ballot_sync(kFull, in);
+                if (in)
+                    lst[na + __popc(bm & ((1u << lane) - 1u))] = (uint16_t)i;
+                na += __popc(bm);
+            }
+            __syncwarp();
+            bool occluded = false;
+            for (int b = 0; b < na; b += 4)
+            {
+                const int idx = b + g;
+                uint4 c[CPL];
+                if (idx < na)
+                    load_frag_smem<CPL>(c, cache + (uint32_t)wu[lst[idx]] * p.row_bytes, p.st.nchunks, gl);
+                else
+                {
+#pragma unroll
+                    for (int t = 0; t < CPL; ++t)
+                        c[t] = make_uint4(0u, 0u, 0u, 0u);
+                }
+                const float d = GroupDist<DT, CPL>::eval(xf, c, p.st.nchunks, gl);
+                const bool hit = idx < na && gl == 0 && __fmul_rn(p.alpha, d) <= dx;
+                if (lane == 0)
+                    pairs += (uint32_t)min(4, na - b);
+                if (__any_sync(kFull, hit))
+                {
+                    occluded = true;
+                    break;
+                }
+            }
+            if (occluded)
+                continue;
+
+            // Worst kept entry and the victim (farthest y with d(v,y) > d(v,x) and
+            // alpha*d(x,y) <= d(v,y)); both lowest slot on ties.
+            float wv = -FLT_MAX;
+            int ws = -1;
+            int nb_ = 0;
+            for (uint32_t b = 0; b < deg; b += 32)
+            {
+                const uint32_t i = b + lane;
+                bool in = false;
+                if (i < deg)
+                {
+                    const uint32_t y = wid[i];
+                    if (y < N && y != v)
+                    {
+                        const float dy = wd[i];
+                        if (dy > wv)
+                        {
+                            wv = dy;
+                            ws = (int)i;
+                        }
+                        in = dy > dx;
+                    }
+                }
+                const unsigned bm = __ballot_sync(kFull, in);
+                if (in)
+                    lst[nb_ + __popc(bm & ((1u << lane) - 1u))] = (uint16_t)i;
+                nb_ += __popc(bm);
+            }
+            warp_argmax_lowslot(wv, ws);
+            __syncwarp();
+            float vv = -FLT_MAX;
+            int vs = -1;
+            for (int b = 0; b < nb_; b += 4)
+            {
+                const int idx = b + g;
+                uint4 c[CPL];
+                if (idx < nb_)
+                    load_frag_smem<CPL>(c, cache + (uint32_t)wu[lst[idx]] * p.row_bytes, p.st.nchunks, gl);
+                else
+                {
+#pragma unroll
+                    for (int t = 0; t < CPL; ++t)
+                        c[t] = make_uint4(0u, 0u, 0u, 0u);
+                }
+                const float d = GroupDist<DT, CPL>::eval(xf, c, p.st.nchunks, gl);
+                if (lane == 0)
+                    pairs += (uint32_t)min(4, nb_ - b);
+                if (idx < nb_ && gl == 0)
+                {
+                    const int slot = lst[idx];
+                    const float dy = wd[slot];
+                    if (__fmul_rn(p.alpha, d) <= dy && (vs < 0 || dy > vv || (dy == vv && slot < vs)))
+                    {
+                        vv = dy;
+                        vs = slot;
+                    }
+                }
+            }
+            warp_argmax_lowslot(vv, vs);
+            if (lane == 0)
+            {
+                const uint16_t ux = (uint16_t)(p.R + k);
+                if (vs >= 0)
+                {
+                    wid[vs] = x;
+                    wd[vs] = dx;
+                    wu[vs] = ux;
+                }
+                else if (deg < C)
+                {
+                    wid[deg] = x;
+                    wd[deg] = dx;
+                    wu[deg] = ux;
+                }
+                else if (ws >= 0 && dx < wv)
+                {
+                    wid[ws] = x;
+                    wd[ws] = dx;
+                    wu[ws] = ux;
+                }
+            }
+            if (vs < 0 && deg < C)
+                wdeg = deg + 1;
+            __syncwarp();
+        }
+        for (uint32_t i = lane; i < C; i += 32)
+        {
+            p.work_ids[(uint64_t)v * C + i] = wid[i];
+            p.work_dists[(uint64_t)v * C + i] = wd[i];
+        }
+        if (lane == 0)
+            p.work_deg[v] = wdeg;
+        __syncwarp();
+    }
+    if (lane == 0 && p.counters)
+        atomicAdd(&p.counters[2], pairs);
+}
+
+// ====================================================================== reverse CSR
+// Sources are all rows [s0, s1) of the work graph (first min(deg, R) slots).
+__global__ void rev_count_kernel(const uint32_t *work_ids, const uint32_t *work_deg, uint32_t N, uint32_t R,
+                                 uint32_t C, uint32_t s0, uint32_t s1, uint32_t *cnt)
+{
+    const uint64_t total = (uint64_t)(s1 - s0) * R;
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total;
+         i += (uint64_t)gridDim.x * blockDim.x)
+    {
+        const uint32_t src = s0 + (uint32_t)(i / R);
+        const uint32_t slot = (uint32_t)(i % R);
+        if (slot < min(work_deg[src], R))
+        {
+            const uint32_t t = work_ids[(uint64_t)src * C + slot];
+            if (t < N && t != src)
+                atomicAdd(&cnt[t], 1u);
+        }
+    }
+}
+
+__global__ void rev_fill_kernel(const uint32_t *work_ids, const uint32_t *work_deg, uint32_t N, uint32_t R,
+                                uint32_t C, uint32_t s0, uint32_t s1, uint32_t *cursor, uint32_t *rev)
+{
+    const uint64_t total = (uint64_t)(s1 - s0) * R;
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total;
+         i += (uint64_t)gridDim.x * blockDim.x)
+    {
+        const uint32_t src = s0 + (uint32_t)(i / R);
+        const uint32_t slot = (uint32_t)(i % R);
+        if (slot < min(work_deg[src], R))
+        {
+            const uint32_t t = work_ids[(uint64_t)src * C + slot];
+            if (t < N && t != src)
+                rev[atomicAdd(&cursor[t], 1u)] = src;
+        }
+    }
+}
+
+// Exclusive scan of n uint32 counts into offsets[0..n] (offsets[n] = total),
+// three passes over tiles of kScanTile elements.
+constexpr int kScanThreads = 1024;
+constexpr int kScanItems = 4;
+constexpr int kScanTile = kScanThreads * kScanItems;
+
+__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t *s_warp, uint32_t &total)
+{
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    uint32_t x = v;
+    for (int off = 1; off < 32; off <<= 1)
+    {
+        const uint32_t y = __shfl_up_sync(kFull, x, off);
+        if (lane >= off)
+            x += y;
+    }
+    if (lane == 31)
+        s_warp[w] = x;
+    __syncthreads();
+    if (w == 0)
+    {
+        uint32_t s = lane < (int)(blockDim.x >> 5) ? s_warp[lane] : 0u;
+        for (int off = 1; off < 32; off <<= 1)
+        {
+            const uint32_t y = __shfl_up_sync(kFull, s, off);
+            if (lane >= off)
+                s += y;
+        }
+        s_warp[lane] = s;
+    }
+    __syncthreads();
+    total = s_warp[31];
+    const uint32_t before = w > 0 ? s_warp[w - 1] : 0u;
+    __syncthreads();
+    return before + x - v;
+}
+
+__global__ void __launch_bounds__(kScanThreads) scan_tile_sums_kernel(const uint32_t *in, uint32_t n,
+                                                                      uint32_t *tile_sums)
+{
+    __shared__ uint32_t s_warp[32];
+    const uint64_t base = (uint64_t)blockIdx.x * kScanTile + threadIdx.x * kScanItems;
+    uint32_t s = 0;
+#pragma unroll
+    for (int k = 0; k < kScanItems; ++k)
+        if (base + k < n)
+            s += in[base + k];
+    uint32_t total;
+    block_exclusive_scan(s, s_warp, total);
+    if (threadIdx.x == 0)
+        tile_sums[blockIdx.x] = total;
+}
+
+__global__ void __launch_bounds__(kScanThreads) scan_tile_offsets_kernel(uint32_t *tile_sums, uint32_t ntiles)
+{
+    __shared__ uint32_t s_warp[32];
+    uint32_t carry = 0;
+    for (uint32_t b = 0; b < ntiles; b += kScanThreads)
+    {
+        const uint32_t i = b + threadIdx.x;
+        const uint32_t v = i < ntiles ? tile_sums[i] : 0u;
+        uint32_t total;
+        const uint32_t ex = block_exclusive_scan(v, s_warp, total);
+        if (i < ntiles)
+            tile_sums[i] = carry + ex;
+        carry += total;
+        __syncthreads();
+    }
+}
+
+__global__ void __launch_bounds__(kScanThreads) scan_apply_kernel(const uint32_t *in, uint32_t n,
+                                                                  const uint32_t *tile_offsets, uint32_t *out,
+                                                                  uint32_t *cursor)
+{
+    __shared__ uint32_t s_warp[32];
+    const uint64_t base = (uint64_t)blockIdx.x * kScanTile + threadIdx.x * kScanItems;
+    uint32_t vals[kScanItems];
+    uint32_t s = 0;
+#pragma unroll
+    for (int k = 0; k < kScanItems; ++k)
+    {
+        vals[k] = base + k < n ? in[base + k] : 0u;
+        s += vals[k];
+    }
+    uint32_t total;
+    uint32_t ex = block_exclusive_scan(s, s_warp, total) + tile_offsets[blockIdx.x];
+#pragma unroll
+    for (int k = 0; k < kScanItems; ++k)
+    {
+        if (base + k < n)
+        {
+            out[base + k] = ex;
+            if (cursor)
+                cursor[base + k] = ex;
+        }
+        ex += vals[k];
+        if (base + k + 1 == n)
+            out[n] = ex;
+    }
+}
+
+// ====================================================================== reverse merge
+struct MergeParams
+{
+    StoreView st;
+    uint32_t C;
+    uint32_t *work_ids;
+    float *work_dists;
+    uint32_t *work_deg;
+    const uint32_t *offsets;
+    uint32_t *rev; // sorted in place per target by the merge kernels
+    uint32_t heavy_cap, heavy_threshold, heavy_sample;
+    uint32_t *heavy_list;
+    uint32_t *heavy_count;
+    uint32_t t0, t1;
+    uint32_t sort_cap;  // light kernel: segments up to this length
+    uint32_t per_warp;  // light kernel smem bytes per warp
+    unsigned long long *counters; // [3] reverse distance evaluations
+};
+
+constexpr uint32_t kMergeSortCap = 512;
+constexpr uint32_t kHeavySortCap = 16384;
+
+__host__ __device__ __forceinline__ uint32_t merge_smem_per_warp(uint32_t C, uint32_t sort_cap)
+{
+    return align16(4u * sort_cap) + align16(4u * C) + align16(4u * C) + 256u + 256u;
+}
+
+// Reference reverse merge of target t over the sorted source list
+// srcs[0..n) (ascending, duplicates adjacent), executed by one warp.  The
+// row lives in wid/wd (C entries); nl/nd are 64-entry scratch.
+template <int DT, int CPL>
+__device__ void merge_sorted_sources(const MergeParams &p, uint32_t t, const uint32_t *srcs, uint32_t n, uint32_t *wid,
+                                     float *wd, uint32_t *nl, float *nd, int lane, unsigned long long &evals)
+{
+    const uint32_t N = p.st.N;
+    const uint32_t C = p.C;
+    const int gl = lane & 7;
+    for (uint32_t i = lane; i < C; i += 32)
+    {
+        wid[i] = p.work_ids[(uint64_t)t * C + i];
+        wd[i] = p.work_dists[(uint64_t)t * C + i];
+    }
+    const uint32_t deg0 = min(p.work_deg[t], C);
+    __syncwarp();
+    uint32_t count = n;
+    bool sampled = false;
+    if (p.heavy_cap && n > p.heavy_threshold)
+    {
+        count = min(p.heavy_sample, n);
+        if (count == 0)
+            count = 1;
+        sampled = count < n;
+    }
+    uint4 q[CPL];
+    load_frag<CPL>(q, p.st.data + (uint64_t)t * p.st.stride, p.st.nchunks, gl);
+    uint32_t deg = deg0;
+    // New sources: valid, not the target, not in the row as the search left
+    // it, and not a repeat of the previous source.  Any other source is a
+    // no-op in the reference loop (present in the row, or evicted earlier as
+    // the worst, hence not closer than the current worst).
+    for (uint32_t b = 0; b < count; b += 64)
+    {
+        int m = 0;
+#pragma unroll
+        for (int h = 0; h < 2; ++h)
+        {
+            const uint32_t k = b + h * 32 + lane;
+            bool keep = false;
+            uint32_t s = kInvalid;
+            if (k < count)
+            {
+                const uint32_t i = sampled ? (uint32_t)(((uint64_t)k * n) / count) : k;
+                s = srcs[i];
+                keep = s < N && s != t;
+                if (keep && k > 0)
+                {
+                    const uint32_t ip = sampled ? (uint32_t)(((uint64_t)(k - 1) * n) / count) : k - 1;
+                    if (srcs[ip] == s)
+                        keep = false;
+                }
+                if (keep)
+                {
+                    for (uint32_t j = 0; j < deg0; ++j)
+                        if (wid[j] == s)
+                        {
+                            keep = false;
+                            break;
+                        }
+                }
+            }
+            const unsigned bm = __ballot_sync(kFull, keep);
+            if (keep)
+                nl[m + __popc(bm & ((1u << lane) - 1u))] = s;
+            m += __popc(bm);
+        }
+        __syncwarp();
+        if (m == 0)
+            continue;
+        eval_candidates<DT, CPL>(p.st.data, p.st.stride, p.st.nchunks, q, nl, nd, m, lane);
+        __syncwarp();
+        evals += (lane == 0) ? (unsigned long long)m : 0ull;
+        for (int j = 0; j < m; ++j)
+        {
+            const uint32_t s = nl[j];
+            const float d = nd[j];
+            if (deg < C)
+            {
+                if (lane == 0)
+                {
+                    wid[deg] = s;
+                    wd[deg] = d;
+                }
+                ++deg;
+            }
+            else
+            {
+                float w = -FLT_MAX;
+                int ws = -1;
+                for (uint32_t i = lane; i < C; i += 32)
+                    if (wd[i] > w)
+                    {
+                        w = wd[i];
+                        ws = (int)i;
+                    }
+                warp_argmax_lowslot(w, ws);
+                if (lane == 0 && ws >= 0 && d < w)
+                {
+                    wid[ws] = s;
+                    wd[ws] = d;
+                }
+            }
+            __syncwarp();
+        }
+    }
+    for (uint32_t i = lane; i < C; i += 32)
+    {
+        p.work_ids[(uint64_t)t * C + i] = wid[i];
+        p.work_dists[(uint64_t)t * C + i] = wd[i];
+    }
+    if (lane == 0)
+        p.work_deg[t] = deg;
+    __syncwarp();
+}
+
+template <int DT, int CPL>
+__global__ void __launch_bounds__(kBlockThreads) merge_kernel(MergeParams p)
+{
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    const int lane = lane_id();
+    uint8_t *b = smem_raw + warp_id_in_block() * p.per_warp;
+    uint32_t *buf = reinterpret_cast<uint32_t *>(b);
+    b += align16(4u * p.sort_cap);
+    uint32_t *wid = reinterpret_cast<uint32_t *>(b);
+    b += align16(4u * p.C);
+    float *wd = reinterpret_cast<float *>(b);
+    b += align16(4u * p.C);
+    uint32_t *nl = reinterpret_cast<uint32_t *>(b);
+    b += 256;
+    float *nd = reinterpret_cast<float *>(b);
+    unsigned long long evals = 0;
+    for (uint32_t t = p.t0 + blockIdx.x * kWarpsPerBlock + warp_id_in_block(); t < p.t1;
+         t += gridDim.x * kWarpsPerBlock)
+    {
+        const uint32_t beg = p.offsets[t], end = p.offsets[t + 1];
+        const uint32_t n = end - beg;
+        if (n == 0)
+            continue;
+        if (n > p.sort_cap)
+        {
+            if (lane == 0)
+                p.heavy_list[atomicAdd(p.heavy_count, 1u)] = t;
+            continue;
+        }
+        const int n2 = max(32, next_pow2((int)n));
+        for (int i = lane; i < n2; i += 32)
+            buf[i] = (uint32_t)i < n ? p.rev[beg + i] : kInvalid;
+        __syncwarp();
+        warp_sort_smem_u32(buf, n2, lane);
+        merge_sorted_sources<DT, CPL>(p, t, buf, n, wid, wd, nl, nd, lane, evals);
+    }
+    if (lane == 0 && p.counters)
+        atomicAdd(&p.counters[3], evals);
+}
+
+// Heavy targets (more than sort_cap sources): one block per target, sorted
+// in shared memory by the whole block when they fit kHeavySortCap, else
+// sorted in place in global memory by the block (rare: in-degree > 16384).
+template <int DT, int CPL>
+__global__ void __launch_bounds__(256) heavy_merge_kernel(MergeParams p)
+{
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    uint32_t *sbuf = reinterpret_cast<uint32_t *>(smem_raw);
+    uint8_t *b = smem_raw + 4u * kHeavySortCap;
+    uint32_t *wid = reinterpret_cast<uint32_t *>(b);
+    b += align16(4u * p.C);
+    float *wd = reinterpret_cast<float *>(b);
+    b += align16(4u * p.C);
+    uint32_t *nl = reinterpret_cast<uint32_t *>(b);
+    b += 256;
+    float *nd = reinterpret_cast<float *>(b);
+    const int lane = threadIdx.x & 31;
+    const uint32_t nheavy = *p.heavy_count;
+    unsigned long long evals = 0;
+    for (uint32_t h = blockIdx.x; h < nheavy; h += gridDim.x)
+    {
+        const uint32_t t = p.heavy_list[h];
+        const uint32_t beg = p.offsets[t], end = p.offsets[t + 1];
+        const uint32_t n = end - beg;
+        const uint32_t *sorted;
+        if (n <= kHeavySortCap)
+        {
+            const uint32_t n2 = (uint32_t)next_pow2((int)n);
+            for (uint32_t i = threadIdx.x; i < n2; i += blockDim.x)
+                sbuf[i] = i < n ? p.rev[beg + i] : kInvalid;
+            __syncthreads();
+            for (uint32_t size = 2; size <= n2; size <<= 1)
+                for (uint32_t j = size >> 1; j > 0; j >>= 1)
+                {
+                    for (uint32_t i = threadIdx.x; i < n2; i += blockDim.x)
+                    {
+                        const uint32_t l = i ^ j;
+                        if (l > i)
+                        {
+                            const uint32_t x = sbuf[i], y = sbuf[l];
+                            const bool asc = (i & size) == 0;
+                            if (asc ? (x > y) : (x < y))
+                            {
+                                sbuf[i] = y;
+                                sbuf[l] = x;
+                            }
+                        }
+                    }
+                    __syncthreads();
+                }
+            sorted = sbuf;
+        }
+        else
+        {
+            // Odd-even transposition sort in place: n rounds, each a
+            // parallel compare-exchange of disjoint neighbours.
+            uint32_t *a = p.rev + beg;
+            for (uint32_t r = 0; r < n; ++r)
+            {
+                for (uint32_t i = 2 * threadIdx.x + (r & 1u); i + 1 < n; i += 2 * blockDim.x)
+                {
+                    const uint32_t x = a[i], y = a[i + 1];
+                    if (x > y)
+                    {
+                        a[i] = y;
+                        a[i + 1] = x;
+                    }
+                }
+                __syncthreads();
+            }
+            sorted = a;
+        }
+        if (threadIdx.x < 32)
+            merge_sorted_sources<DT, CPL>(p, t, sorted, n, wid, wd, nl, nd, lane, evals);
+        __syncthreads();
+    }
+    if (threadIdx.x == 0 && p.counters)
+        atomicAdd(&p.counters[3], evals);
+}
+
+// ====================================================================== prune
+struct PruneParams
+{
+    StoreView st;
+    uint32_t R, C, Cp; // Cp = next_pow2(C), >= 32
+    float alpha;
+    uint32_t min_degree;
+    const uint32_t *work_ids;
+    const float *work_dists;
+    const uint32_t *work_deg;
+    uint32_t *cur_ids;
+    float *cur_dists;
+    uint32_t *degree;
+    uint32_t v0, v1;
+    uint32_t row_bytes;
+    uint32_t per_warp;
+    unsigned long long *counters; // [4] pair evaluations
+};
+
+__host__ __device__ __forceinline__ uint32_t prune_smem_per_warp(uint32_t C, uint32_t Cp, uint32_t R,
+                                                                 uint32_t row_bytes)
+{
+    return C * row_bytes + align16(8u * Cp) + align16(4u * C) + align16(4u * C) + align16(C) + align16(2u * C) +
+           align16(4u * C) + align16(4u * R) + align16(4u * R);  // cache, keys, cid, cd, state, lst, rid, oid, od
+}
+
+template <int DT, int CPL>
+__global__ void __launch_bounds__(kBlockThreads) prune_kernel(PruneParams p)
+{
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    const int lane = lane_id();
+    const int g = lane >> 3, gl = lane & 7;
+    uint8_t *b = smem_raw + warp_id_in_block() * p.per_warp;
+    uint8_t *cache = b;
+    b += p.C * p.row_bytes;
+    uint64_t *keys = reinterpret_cast<uint64_t *>(b);
+    b += align16(8u * p.Cp);
+    uint32_t *cid = reinterpret_cast<uint32_t *>(b);
+    b += align16(4u * p.C);
+    float *cd = reinterpret_cast<float *>(b);
+    b += align16(4u * p.C);
+    uint8_t *state = b; // 0 open, 1 occluded, 2 selected
+    b += align16(p.C);
+    uint16_t *lst = reinterpret_cast<uint16_t *>(b);
+    b += align16(2u * p.C);
+    uint32_t *rid = reinterpret_cast<uint32_t *>(b); // row ids by slot
+    b += align16(4u * p.C);
+    uint32_t *oid = reinterpret_cast<uint32_t *>(b);
+    b += align16(4u * p.R);
+    float *od = reinterpret_cast<float *>(b);
+    const uint32_t N = p.st.N;
+    const uint32_t C = p.C;
+    unsigned long long pairs = 0;
+
+    for (uint32_t v = p.v0 + blockIdx.x * kWarpsPerBlock + warp_id_in_block(); v < p.v1;
+         v += gridDim.x * kWarpsPerBlock)
+    {
+        const uint32_t deg = min(p.work_deg[v], C);
+        // Candidates ordered by (distance, slot): the reference's selection order.
+        for (uint32_t i = lane; i < p.Cp; i += 32)
+        {
+            uint64_t key = kKeyMax;
+            if (i < deg)
+            {
+                const uint32_t id = p.work_ids[(uint64_t)v * C + i];
+                const float d = p.work_dists[(uint64_t)v * C + i];
+                rid[i] = id;
+                if (id < N && id != v && d < FLT_MAX)
+                    key = ((uint64_t)__float_as_uint(d) << 32) | i;
+            }
+            keys[i] = key;
+        }
+        __syncwarp();
+        warp_sort_smem_u64(keys, (int)p.Cp, lane);
+        // Keep the first occurrence of every id (a selected id removes its
+        // copies; an occluded one has occluded copies).
+        int m = 0;
+        for (uint32_t bb = 0; bb < C; bb += 32)
+        {
+            const uint32_t j = bb + lane;
+            bool keep = false;
+            uint32_t id = kInvalid;
+            float d = FLT_MAX;
+            if (j < C && keys[j] != kKeyMax)
+            {
+                const uint32_t slot = (uint32_t)(keys[j] & 0xFFFFFFFFu);
+                id = rid[slot];
+                d = __uint_as_float((uint32_t)(keys[j] >> 32));
+                keep = true;
+                for (uint32_t jj = 0; jj < j; ++jj)
+                {
+                    if (rid[(uint32_t)(keys[jj] & 0xFFFFFFFFu)] == id)
+                    {
+                        keep = false;
+                        break;
+                    }
+                }
+            }
+            const unsigned bm = __ballot_sync(kFull, keep);
+            if (keep)
+            {
+                const int pos = m + __popc(bm & ((1u << lane) - 1u));
+                cid[pos] = id;
+                cd[pos] = d;
+                state[pos] = 0;
+            }
+            m += __popc(bm);
+        }
+        __syncwarp();
+        gather_rows_to_smem(p.st.data, p.st.stride, p.st.nchunks, cid, m, cache, p.row_bytes, lane);
+        __syncwarp();
+        uint32_t out = 0;
+        for (int j = 0; j < m; ++j)
+        {
+            if (state[j] != 0)
+                continue;
+            const float seld = cd[j];
+            if (lane == 0)
+            {
+                state[j] = 2;
+                oid[out] = cid[j];
+                od[out] = seld;
+            }
+            ++out;
+            __syncwarp();
+            if (out >= p.R)
+                break;
+            int nq = 0;
+            for (int bb = j + 1; bb < m; bb += 32)
+            {
+                const int qq = bb + lane;
+                const bool in = qq < m && state[qq] == 0;
+                const unsigned bm = __ballot_sync(kFull, in);
+                if (in)
+                    lst[nq + __popc(bm & ((1u << lane) - 1u))] = (uint16_t)qq;
+                nq += __popc(bm);
+            }
+            __syncwarp();
+            if (nq == 0)
+                continue;
+            uint4 sf[CPL];
+            load_frag_smem<CPL>(sf, cache + (uint32_t)j * p.row_bytes, p.st.nchunks, gl);
+            for (int bb = 0; bb < nq; bb += 4)
+            {
+                const int idx = bb + g;
+                uint4 c[CPL];
+                if (idx < nq)
+                    load_frag_smem<CPL>(c, cache + (uint32_t)lst[idx] * p.row_bytes, p.st.nchunks, gl);
+                else
+                {
+#pragma unroll
+                    for (int t = 0; t < CPL; ++t)
+                        c[t] = make_uint4(0u, 0u, 0u, 0u);
+                }
+                const float d = GroupDist<DT, CPL>::eval(sf, c, p.st.nchunks, gl);
+                if (idx < nq && gl == 0)
+                {
+                    const int qq = lst[idx];
+                    const float dq = cd[qq];
+                    if (seld <= dq && __fmul_rn(p.alpha, d) <= dq)
+                        state[qq] = 1;
+                }
+            }
+            if (lane == 0)
+                pairs += (unsigned long long)nq;
+            __syncwarp();
+        }
+        // Last-round fill: nearest unselected candidates, ignoring occlusion.
+        const uint32_t min_deg = min(p.min_degree, p.R);
+        if (out < min_deg)
+        {
+            for (int j = 0; j < m && out < min_deg; ++j)
+            {
+                if (state[j] == 2)
+                    continue;
+                if (lane == 0)
+                {
+                    oid[out] = cid[j];
+                    od[out] = cd[j];
+                }
+                ++out;
+            }
+            __syncwarp();
+        }
+        for (uint32_t i = lane; i < p.R; i += 32)
+        {
+            p.cur_ids[(uint64_t)v * p.R + i] = i < out ? oid[i] : kInvalid;
+            p.cur_dists[(uint64_t)v * p.R + i] = i < out ? od[i] : FLT_MAX;
+        }
+        if (lane == 0)
+            p.degree[v] = out;
+        __syncwarp();
+    }
+    if (lane == 0 && p.counters)
+        atomicAdd(&p.counters[4], pairs);
+}
+
+} // namespace dance

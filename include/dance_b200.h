@@ -1,0 +1,146 @@
+/*
+ * dance_b200.h -- additive C ABI of libdance_b200.so.
+ *
+ * These entry points have no one-to-one counterpart in the reference C ABI;
+ * they expose what the reference keeps as compile-time macros or static
+ * functions so that in-process callers (benchmarks, parity tests, the
+ * multi-GPU driver) can run the same build on vectors already resident in
+ * device memory, one stage at a time, or sharded over several GPUs.
+ * All pointers named d_* are device pointers on the current CUDA device,
+ * all streams are cudaStream_t passed as void* (NULL = legacy default).
+ * Return codes: 0 success, -1 invalid argument, -2 CUDA error, -3 NCCL error,
+ * -4 a bounded device wait timed out.  The message of the last failure is
+ * available from dance_last_error().
+ */
+#ifndef DANCE_B200_H
+#define DANCE_B200_H
+
+#include <stdint.h>
+
+/* Exported with default visibility even when the library is built with
+ * -fvisibility=hidden. */
+#ifndef DANCE_API
+#if defined(__GNUC__)
+#define DANCE_API __attribute__((visibility("default")))
+#else
+#define DANCE_API
+#endif
+#endif
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types of the vector store. */
+enum
+{
+    DANCE_U8 = 0,  /* uint8, exact integer squared L2 */
+    DANCE_F16 = 1, /* IEEE binary16 storage, half-precision diff/square as the reference */
+    DANCE_F32 = 2  /* float32 */
+};
+
+/* Runtime form of the knobs in gpu_vamana_config.h (same names, lower case). */
+typedef struct DanceVamanaParams
+{
+    uint32_t iters;               /* VAMANA_ITERS */
+    float alpha;                  /* VAMANA_ALPHA, used in the last round */
+    uint32_t init_random_seeds;   /* INIT_RANDOM_SEEDS */
+    uint32_t final_min_degree;    /* FINAL_MIN_DEGREE (0 = no refill) */
+    uint32_t medoid_candidates;   /* MEDOID_NUM_CANDIDATES */
+    uint32_t medoid_samples;      /* MEDOID_NUM_SAMPLES */
+    uint32_t coarse_warmup_iters; /* COARSE_WARMUP_ITERS (0 = off) */
+    uint32_t warmup_expand_steps; /* WARMUP_EXPAND_STEPS */
+    uint32_t reverse_heavy_cap;   /* ENABLE_REVERSE_HEAVY_CAP */
+    uint32_t reverse_heavy_threshold;
+    uint32_t reverse_heavy_sample;
+    uint32_t visited_log2;        /* log2 of the per-search visited table (performance only) */
+    uint32_t reserved[8];
+} DanceVamanaParams;
+
+DANCE_API void dance_vamana_default_params(DanceVamanaParams *params);
+
+/* Message of the most recent failure in this thread ("" if none). */
+DANCE_API const char *dance_last_error(void);
+
+/* Number of kernels launched by this library in this process so far. */
+DANCE_API uint64_t dance_kernel_launch_count(void);
+
+/* ---- workspace --------------------------------------------------------- */
+/* Opaque device scratch sized for (N, R, L, C, STEPS); reused across builds
+ * of at most that size on the device that created it. */
+typedef struct DanceWorkspace DanceWorkspace;
+DANCE_API int dance_workspace_create(uint32_t num_points, uint32_t R, uint32_t L, uint32_t C, uint32_t STEPS,
+                           DanceWorkspace **ws);
+DANCE_API void dance_workspace_destroy(DanceWorkspace *ws);
+
+/* ---- whole build on device-resident vectors ----------------------------- */
+/* d_data: num_points rows of row_stride_bytes (a multiple of 16, at least
+ * dim * element size; padding bytes must be zero).  Writes d_graph
+ * (num_points x R, INVALID padded), d_degree, optionally d_graph_dists
+ * (num_points x R, FLT_MAX padded), and *medoid_out (host).  ws may be NULL.
+ * Asynchronous on stream except for the final medoid read-back. */
+DANCE_API int dance_vamana_build_resident(int dtype, const void *d_data, uint64_t row_stride_bytes, uint32_t num_points,
+                                uint32_t dim, uint32_t R, uint32_t L, uint32_t C, uint32_t STEPS,
+                                const DanceVamanaParams *params, DanceWorkspace *ws, uint32_t *d_graph,
+                                uint32_t *d_degree, float *d_graph_dists, uint32_t *medoid_out, void *stream);
+
+/* Device-side timings (seconds, CUDA events on the build stream, summed over
+ * rounds) and work counters of the last dance_vamana_build_resident call in
+ * this thread.  search includes the online-insert replay (the reference's
+ * search_online_insert_seconds); search_kernel is the GreedySearch kernel
+ * alone.  Counters: distance evaluations of the search, expansions,
+ * pair distances of the insert replay, reverse-merge evaluations, pair
+ * distances of the prune. */
+typedef struct DanceBuildReport
+{
+    double medoid_seconds, search_seconds, search_kernel_seconds, replay_seconds, reverse_seconds, prune_seconds,
+        total_seconds;
+    uint64_t search_evals, expansions, replay_pairs, reverse_evals, prune_pairs;
+    uint64_t reserved[3];
+} DanceBuildReport;
+DANCE_API int dance_last_build_report(DanceBuildReport *report);
+
+/* ---- single stages (parity tests) ---------------------------------------- */
+DANCE_API int dance_stage_medoid(int dtype, const void *d_data, uint64_t row_stride_bytes, uint32_t num_points,
+                       uint32_t dim, uint32_t num_candidates, uint32_t num_samples, float *d_scores,
+                       uint32_t *d_candidate_ids, uint32_t *d_medoid, void *stream);
+DANCE_API int dance_stage_init(int dtype, const void *d_data, uint64_t row_stride_bytes, uint32_t num_points, uint32_t dim,
+                     uint32_t R, uint32_t *d_cur_ids, float *d_cur_dists, uint32_t *d_degree, void *stream);
+/* Batched GreedySearch of every vertex on the frozen graph; records each
+ * vertex's expansion sequence (exp_stride entries per vertex). */
+DANCE_API int dance_stage_search(int dtype, const void *d_data, uint64_t row_stride_bytes, uint32_t num_points, uint32_t dim,
+                       uint32_t R, uint32_t L, uint32_t steps, uint32_t entry, uint32_t init_random_seeds,
+                       uint32_t visited_log2, const uint32_t *d_cur_ids, const float *d_cur_dists,
+                       const uint32_t *d_degree, uint32_t *d_exp_ids, float *d_exp_dists, uint32_t *d_exp_count,
+                       uint32_t exp_stride, void *stream);
+/* Online RobustInsert replay of the expansion sequences into C-wide work rows. */
+DANCE_API int dance_stage_replay(int dtype, const void *d_data, uint64_t row_stride_bytes, uint32_t num_points, uint32_t dim,
+                       uint32_t R, uint32_t C, float alpha, const uint32_t *d_cur_ids, const float *d_cur_dists,
+                       const uint32_t *d_degree, const uint32_t *d_exp_ids, const float *d_exp_dists,
+                       const uint32_t *d_exp_count, uint32_t exp_stride, uint32_t *d_work_ids,
+                       float *d_work_dists, uint32_t *d_work_deg, void *stream);
+/* Exact CSR reverse-edge merge into the work rows (in place). */
+DANCE_API int dance_stage_reverse_merge(int dtype, const void *d_data, uint64_t row_stride_bytes, uint32_t num_points,
+                              uint32_t dim, uint32_t R, uint32_t C, const DanceVamanaParams *params,
+                              DanceWorkspace *ws, uint32_t *d_work_ids, float *d_work_dists, uint32_t *d_work_deg,
+                              uint64_t *reverse_edges_out, void *stream);
+/* RobustPrune(alpha) of the work rows into the R-wide graph. */
+DANCE_API int dance_stage_prune(int dtype, const void *d_data, uint64_t row_stride_bytes, uint32_t num_points, uint32_t dim,
+                      uint32_t R, uint32_t C, float alpha, uint32_t min_degree, const uint32_t *d_work_ids,
+                      const float *d_work_dists, const uint32_t *d_work_deg, uint32_t *d_cur_ids,
+                      float *d_cur_dists, uint32_t *d_degree, void *stream);
+
+/* ---- query search over a built graph (recall harness) -------------------- */
+/* DiskANN-style best-first search from `start` with list size L_search; the
+ * K nearest found per query go to d_out_ids / d_out_dists (nq x K). */
+DANCE_API int dance_search_queries(int dtype, const void *d_data, uint64_t row_stride_bytes, uint32_t num_points,
+                         uint32_t dim, const uint32_t *d_graph, uint32_t R, uint32_t start, const void *d_queries,
+                         uint64_t query_stride_bytes, uint32_t num_queries, uint32_t L_search, uint32_t K,
+                         uint32_t visited_log2, uint32_t *d_out_ids, float *d_out_dists, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DANCE_B200_H */

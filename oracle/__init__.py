@@ -1,0 +1,235 @@
+"""ctypes binding of the CPU parity oracle (oracle/liboracle.so).
+
+TEST INFRASTRUCTURE ONLY: imported by tests/, __graft_entry__.smoke() and
+bench.py's cpu_baseline / --impl reference leg, never by the product.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB = HERE / "liboracle.so"
+
+_P = ctypes.c_void_p
+_U32 = ctypes.c_uint32
+_U64 = ctypes.c_uint64
+_I = ctypes.c_int
+_F = ctypes.c_float
+
+_SIGS = {
+    "oracle_default_params": (None, [_P]),
+    "oracle_reset_counters": (None, []),
+    "oracle_get_counters": (None, [_P]),
+    "oracle_distance": (_F, [_I, _P, _P, _U32]),
+    "oracle_float_to_half": (None, [_P, _P, _U64]),
+    "oracle_hash_u32": (_U32, [_U32]),
+    "oracle_det_neighbor": (_U32, [_U32, _U32, _U32]),
+    "oracle_medoid": (_U32, [_I, _P, _U64, _U32, _U32, _U32, _U32, _P, _P, _I]),
+    "oracle_init": (_I, [_I, _P, _U64, _U32, _U32, _U32, _P, _P, _P, _I]),
+    "oracle_search": (_I, [_I, _P, _U64, _U32, _U32, _U32, _U32, _U32, _U32, _U32, _I, _P, _P, _P, _P, _P, _P,
+                           _U32, _I]),
+    "oracle_replay": (_I, [_I, _P, _U64, _U32, _U32, _U32, _U32, _F, _P, _P, _P, _P, _P, _P, _U32, _P, _P, _P,
+                           _I]),
+    "oracle_reverse_merge": (_I, [_I, _P, _U64, _U32, _U32, _U32, _U32, _P, _P, _P, _P, _P, _I]),
+    "oracle_prune": (_I, [_I, _P, _U64, _U32, _U32, _U32, _U32, _F, _U32, _P, _P, _P, _P, _P, _P, _I]),
+    "oracle_build": (_I, [_I, _P, _U64, _U32, _U32, _U32, _U32, _U32, _U32, _P, _I, _I, _P, _P, _P, _P]),
+    "oracle_search_queries": (_I, [_I, _P, _U64, _U32, _U32, _P, _U32, _U32, _P, _U64, _U32, _U32, _U32, _P, _P,
+                                   _I]),
+}
+
+_lib = None
+
+
+def build(force: bool = False) -> Path:
+    src = HERE / "vamana_oracle.cpp"
+    if force or not LIB.exists() or LIB.stat().st_mtime < src.stat().st_mtime:
+        subprocess.run(["make", "-s", "-C", str(HERE), "liboracle.so"], check=True)
+    return LIB
+
+
+def load():
+    global _lib
+    if _lib is None:
+        if not LIB.exists():
+            build()
+        lib = ctypes.CDLL(str(LIB))
+        for k, (r, a) in _SIGS.items():
+            f = getattr(lib, k)
+            f.restype = r
+            f.argtypes = a
+        _lib = lib
+    return _lib
+
+
+def _p(a):
+    return ctypes.c_void_p(a.ctypes.data) if a is not None else ctypes.c_void_p(0)
+
+
+DTYPE = {np.dtype(np.uint8): 0, np.dtype(np.float16): 1, np.dtype(np.float32): 2}
+
+
+def _store(data: np.ndarray):
+    """Oracle rows use the same 16-byte padded stride as the product."""
+    data = np.ascontiguousarray(data)
+    n, dim = data.shape
+    es = data.dtype.itemsize
+    stride = (dim * es + 15) // 16 * 16
+    if stride != dim * es:
+        pad = np.zeros((n, stride // es), dtype=data.dtype)
+        pad[:, :dim] = data
+        data = pad
+    return data, stride, DTYPE[np.dtype(data.dtype)]
+
+
+class Params(ctypes.Structure):
+    _fields_ = [("iters", _U32), ("alpha", _F), ("init_random_seeds", _U32), ("final_min_degree", _U32),
+                ("medoid_candidates", _U32), ("medoid_samples", _U32), ("coarse_warmup_iters", _U32),
+                ("warmup_expand_steps", _U32), ("reverse_heavy_cap", _U32), ("reverse_heavy_threshold", _U32),
+                ("reverse_heavy_sample", _U32), ("visited_log2", _U32), ("reserved", _U32 * 8)]
+
+
+def params(**kw) -> Params:
+    p = Params()
+    load().oracle_default_params(ctypes.byref(p))
+    for k, v in kw.items():
+        setattr(p, k, v)
+    return p
+
+
+def threads() -> int:
+    return int(os.environ.get("ORACLE_THREADS", os.cpu_count() or 1))
+
+
+def distance(a: np.ndarray, b: np.ndarray) -> float:
+    a = np.ascontiguousarray(a)
+    b = np.ascontiguousarray(b, dtype=a.dtype)
+    return float(load().oracle_distance(DTYPE[a.dtype], _p(a), _p(b), a.shape[-1]))
+
+
+def float_to_half(x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, dtype=np.float32)
+    out = np.empty(x.shape, dtype=np.uint16)
+    load().oracle_float_to_half(_p(x), _p(out), x.size)
+    return out.view(np.float16)
+
+
+def medoid(data, num_candidates=1024, num_samples=4096):
+    d, stride, dt = _store(data)
+    n, dim = data.shape
+    nc = min(num_candidates, n)
+    scores = np.zeros(nc, np.float32)
+    cand = np.zeros(nc, np.uint32)
+    m = load().oracle_medoid(dt, _p(d), stride, n, dim, num_candidates, num_samples, _p(scores), _p(cand), threads())
+    return int(m), scores, cand
+
+
+def init(data, R):
+    d, stride, dt = _store(data)
+    n, dim = data.shape
+    ids = np.zeros((n, R), np.uint32)
+    ds = np.zeros((n, R), np.float32)
+    deg = np.zeros(n, np.uint32)
+    load().oracle_init(dt, _p(d), stride, n, dim, R, _p(ids), _p(ds), _p(deg), threads())
+    return ids, ds, deg
+
+
+def search(data, R, L, steps, entry, seeds, cur_ids, cur_dists, degree, exp_stride, pool_mode=0):
+    d, stride, dt = _store(data)
+    n, dim = data.shape
+    eids = np.zeros((n, exp_stride), np.uint32)
+    eds = np.zeros((n, exp_stride), np.float32)
+    ecnt = np.zeros(n, np.uint32)
+    rc = load().oracle_search(dt, _p(d), stride, n, dim, R, L, steps, entry, seeds, pool_mode,
+                              _p(np.ascontiguousarray(cur_ids, np.uint32)),
+                              _p(np.ascontiguousarray(cur_dists, np.float32)),
+                              _p(np.ascontiguousarray(degree, np.uint32)), _p(eids), _p(eds), _p(ecnt), exp_stride,
+                              threads())
+    assert rc == 0
+    return eids, eds, ecnt
+
+
+def replay(data, R, C, alpha, cur_ids, cur_dists, degree, exp_ids, exp_dists, exp_count):
+    d, stride, dt = _store(data)
+    n, dim = data.shape
+    wid = np.zeros((n, C), np.uint32)
+    wd = np.zeros((n, C), np.float32)
+    wdeg = np.zeros(n, np.uint32)
+    rc = load().oracle_replay(dt, _p(d), stride, n, dim, R, C, alpha,
+                              _p(np.ascontiguousarray(cur_ids, np.uint32)),
+                              _p(np.ascontiguousarray(cur_dists, np.float32)),
+                              _p(np.ascontiguousarray(degree, np.uint32)),
+                              _p(np.ascontiguousarray(exp_ids, np.uint32)),
+                              _p(np.ascontiguousarray(exp_dists, np.float32)),
+                              _p(np.ascontiguousarray(exp_count, np.uint32)), exp_ids.shape[1], _p(wid), _p(wd),
+                              _p(wdeg), threads())
+    assert rc == 0
+    return wid, wd, wdeg
+
+
+def reverse_merge(data, R, C, work_ids, work_dists, work_deg, prm=None):
+    d, stride, dt = _store(data)
+    n, dim = data.shape
+    wid = np.array(work_ids, dtype=np.uint32, copy=True, order="C")
+    wd = np.array(work_dists, dtype=np.float32, copy=True, order="C")
+    wdeg = np.array(work_deg, dtype=np.uint32, copy=True, order="C")
+    edges = ctypes.c_uint64(0)
+    rc = load().oracle_reverse_merge(dt, _p(d), stride, n, dim, R, C, ctypes.byref(prm) if prm else None, _p(wid),
+                                     _p(wd), _p(wdeg), ctypes.byref(edges), threads())
+    assert rc == 0
+    return wid, wd, wdeg, int(edges.value)
+
+
+def prune(data, R, C, alpha, min_degree, work_ids, work_dists, work_deg):
+    d, stride, dt = _store(data)
+    n, dim = data.shape
+    ids = np.zeros((n, R), np.uint32)
+    ds = np.zeros((n, R), np.float32)
+    deg = np.zeros(n, np.uint32)
+    rc = load().oracle_prune(dt, _p(d), stride, n, dim, R, C, alpha, min_degree,
+                             _p(np.ascontiguousarray(work_ids, np.uint32)),
+                             _p(np.ascontiguousarray(work_dists, np.float32)),
+                             _p(np.ascontiguousarray(work_deg, np.uint32)), _p(ids), _p(ds), _p(deg), threads())
+    assert rc == 0
+    return ids, ds, deg
+
+
+def build_graph(data, R, L, C, STEPS, prm=None, pool_mode=0, nthreads=None):
+    """Whole oracle build; returns (graph, degree, dists, medoid)."""
+    d, stride, dt = _store(data)
+    n, dim = data.shape
+    g = np.zeros((n, R), np.uint32)
+    deg = np.zeros(n, np.uint32)
+    ds = np.zeros((n, R), np.float32)
+    med = ctypes.c_uint32(0)
+    rc = load().oracle_build(dt, _p(d), stride, n, dim, R, L, C, STEPS, ctypes.byref(prm) if prm else None,
+                             pool_mode, nthreads or threads(), _p(g), _p(deg), _p(ds), ctypes.byref(med))
+    assert rc == 0, rc
+    return g, deg, ds, int(med.value)
+
+
+def search_queries(data, graph, R, start, queries, L, K):
+    d, stride, dt = _store(data)
+    q, qstride, _ = _store(np.ascontiguousarray(queries, dtype=data.dtype))
+    n, dim = data.shape
+    nq = queries.shape[0]
+    ids = np.zeros((nq, K), np.uint32)
+    ds = np.zeros((nq, K), np.float32)
+    load().oracle_search_queries(dt, _p(d), stride, n, dim, _p(np.ascontiguousarray(graph, np.uint32)), R, start,
+                                 _p(q), qstride, nq, L, K, _p(ids), _p(ds), threads())
+    return ids, ds
+
+
+def counters():
+    out = np.zeros(6, np.uint64)
+    load().oracle_get_counters(_p(out))
+    return dict(zip(["search_evals", "expansions", "pair_evals", "reverse_evals", "reverse_edges",
+                     "seed_mismatch"], out.tolist()))
+
+
+def reset_counters():
+    load().oracle_reset_counters()

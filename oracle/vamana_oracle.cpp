@@ -1,0 +1,1206 @@
+// vamana_oracle.cpp -- CPU restatement of the DANCE vnew2 Vamana build.
+//
+// TEST INFRASTRUCTURE ONLY.  This file is the parity oracle: it is compiled
+// into oracle/liboracle.so and loaded exclusively by tests/, by
+// __graft_entry__.smoke() and by bench.py's cpu_baseline / --impl reference
+// leg.  The product (dance_b200/libdance_b200.so) never links or calls it.
+//
+// It restates, sequentially and per vertex, the algorithm of the reference
+// file src/gpu_vamana_vnew2.cu (paths are relative to the DANCE repository):
+//   hash / deterministic_neighbor ........ :169-191
+//   distance arithmetic .................. :268-290 (u8), :336-362 (f32),
+//                                          :391-418 (f16)
+//   approximate medoid ................... :1032-1064, host argmin :2445-2479
+//   random initial graph ................. :1066-1117
+//   GreedySearch + online RobustInsert ... :1119-1439, :598-734, :759-877
+//   CSR reverse count / fill / merge ..... :1604-1661, :1722-1814
+//   RobustPrune + final degree fill ...... :1893-2147
+//   round driver ......................... :2170-2855 (alpha schedule :201-213)
+//
+// Canonical choices where the reference is order-dependent:
+//   * search pool ties: pool_mode 0 (the product's rule) orders candidates by
+//     the key (distance, id); pool_mode 1 restates the reference's unsorted
+//     slot pool literally (ties -> lowest slot) and is used only to pin this
+//     oracle against outputs of the reference itself;
+//   * reverse CSR order: sources of each target in ascending source id (the
+//     reference fills with atomics, so its order varies run to run).
+// Everything else -- the online insert, reverse merge and prune decisions and
+// their slot tie-breaks -- follows the reference rules exactly.
+//
+// Distances reproduce the reference warp arithmetic: 32 lane partial sums
+// over 16-byte chunks (f32: float4 index mod 32, per chunk
+// fma(dw,dw,fma(dz,dz,fma(dx,dx,dy*dy))); f16: half2 index mod 32, half
+// precision diff and square, float sum of the pair), then the shfl_down tree
+// 16,8,4,2,1.  u8 is the exact integer sum.  Build with -ffp-contract=off.
+
+#include <algorithm>
+#include <atomic>
+#include <cfloat>
+#include <cmath>
+#include <cstdint>
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#include "../include/dance_b200.h"
+
+namespace
+{
+constexpr uint32_t kInvalid = 0xFFFFFFFFu;
+
+// ---------------------------------------------------------------- hashing
+uint32_t hash_u32(uint32_t x)
+{
+    x ^= x >> 16;
+    x *= 0x7feb352du;
+    x ^= x >> 15;
+    x *= 0x846ca68bu;
+    x ^= x >> 16;
+    return x;
+}
+
+uint32_t det_neighbor(uint32_t node, uint32_t k, uint32_t N)
+{
+    if (N <= 1)
+        return kInvalid;
+    uint32_t v = hash_u32(node * 0x9e3779b1u + k * 0x85ebca6bu + 17u) % N;
+    if (v == node)
+        v = (v + 1u) % N;
+    return v;
+}
+
+// ------------------------------------------------------------ binary16
+// IEEE-754 binary16 with round-to-nearest-even, written from the format
+// definition (1 sign, 5 exponent bits biased by 15, 10 fraction bits).
+uint16_t double_to_half(double x)
+{
+    uint16_t sign = std::signbit(x) ? 0x8000u : 0u;
+    double a = std::fabs(x);
+    if (std::isnan(a))
+        return 0x7E00u;
+    if (a >= 65520.0)
+        return sign | 0x7C00u;
+    if (a < 6.103515625e-05) // 2^-14: subnormal range, unit 2^-24
+    {
+        double q = std::nearbyint(a * 16777216.0);
+        return sign | (uint16_t)q;
+    }
+    int k = 0;
+    double f = std::frexp(a, &k); // a = f * 2^k, f in [0.5, 1)
+    int e = k - 1;
+    double m = std::nearbyint((f * 2.0 - 1.0) * 1024.0);
+    if (m >= 1024.0)
+    {
+        m = 0.0;
+        e += 1;
+    }
+    if (e > 15)
+        return sign | 0x7C00u;
+    return sign | (uint16_t)((e + 15) << 10) | (uint16_t)m;
+}
+
+float half_to_float(uint16_t h)
+{
+    uint32_t sign = (h & 0x8000u) ? 1u : 0u;
+    uint32_t e = (h >> 10) & 0x1Fu;
+    uint32_t m = h & 0x3FFu;
+    double v;
+    if (e == 0)
+        v = std::ldexp((double)m, -24);
+    else if (e == 31)
+        v = m ? NAN : INFINITY;
+    else
+        v = std::ldexp((double)(m | 0x400u), (int)e - 25);
+    return (float)(sign ? -v : v);
+}
+
+// ------------------------------------------------------------ distances
+struct Store
+{
+    int dtype;
+    const uint8_t *base;
+    uint64_t stride;
+    uint32_t dim;
+    const uint8_t *row(uint32_t i) const { return base + (uint64_t)i * stride; }
+};
+
+float tree32(float *acc)
+{
+    for (int off = 16; off > 0; off >>= 1)
+        for (int l = 0; l < off; ++l)
+            acc[l] = acc[l] + acc[l + off];
+    return acc[0];
+}
+
+float dist_f32(const float *x, const float *y, uint32_t dim)
+{
+    float acc[32] = {0};
+    const uint32_t chunks = (dim + 3) / 4;
+    for (uint32_t c = 0; c < chunks; ++c)
+    {
+        float d[4];
+        for (int i = 0; i < 4; ++i)
+        {
+            uint32_t e = c * 4 + i;
+            d[i] = e < dim ? x[e] - y[e] : 0.0f;
+        }
+        float p = d[1] * d[1];
+        p = std::fma(d[0], d[0], p);
+        p = std::fma(d[2], d[2], p);
+        p = std::fma(d[3], d[3], p);
+        acc[c & 31] = acc[c & 31] + p;
+    }
+    return tree32(acc);
+}
+
+float half_sq_diff(uint16_t a, uint16_t b)
+{
+    uint16_t diff = double_to_half((double)half_to_float(a) - (double)half_to_float(b));
+    double df = (double)half_to_float(diff);
+    return half_to_float(double_to_half(df * df));
+}
+
+float dist_f16(const uint16_t *x, const uint16_t *y, uint32_t dim)
+{
+    float acc[32] = {0};
+    const uint32_t pairs = dim / 2;
+    for (uint32_t h = 0; h < pairs; ++h)
+    {
+        float lo = half_sq_diff(x[2 * h], y[2 * h]);
+        float hi = half_sq_diff(x[2 * h + 1], y[2 * h + 1]);
+        acc[h & 31] = acc[h & 31] + (lo + hi);
+    }
+    if (dim & 1u)
+    {
+        float d = half_to_float(x[dim - 1]) - half_to_float(y[dim - 1]);
+        acc[0] = std::fma(d, d, acc[0]);
+    }
+    return tree32(acc);
+}
+
+float dist_u8(const uint8_t *x, const uint8_t *y, uint32_t dim)
+{
+    uint64_t s = 0;
+    for (uint32_t e = 0; e < dim; ++e)
+    {
+        int d = (int)x[e] - (int)y[e];
+        s += (uint64_t)(d * d);
+    }
+    return (float)(int32_t)(uint32_t)s;
+}
+
+float dist(const Store &st, uint32_t a, uint32_t b)
+{
+    switch (st.dtype)
+    {
+    case DANCE_U8:
+        return dist_u8(st.row(a), st.row(b), st.dim);
+    case DANCE_F16:
+        return dist_f16(reinterpret_cast<const uint16_t *>(st.row(a)), reinterpret_cast<const uint16_t *>(st.row(b)),
+                        st.dim);
+    default:
+        return dist_f32(reinterpret_cast<const float *>(st.row(a)), reinterpret_cast<const float *>(st.row(b)),
+                        st.dim);
+    }
+}
+
+float dist_query(const Store &st, const uint8_t *q, uint32_t b)
+{
+    switch (st.dtype)
+    {
+    case DANCE_U8:
+        return dist_u8(q, st.row(b), st.dim);
+    case DANCE_F16:
+        return dist_f16(reinterpret_cast<const uint16_t *>(q), reinterpret_cast<const uint16_t *>(st.row(b)), st.dim);
+    default:
+        return dist_f32(reinterpret_cast<const float *>(q), reinterpret_cast<const float *>(st.row(b)), st.dim);
+    }
+}
+
+inline uint64_t make_key(float d, uint32_t id)
+{
+    uint32_t bits;
+    std::memcpy(&bits, &d, 4);
+    return ((uint64_t)bits << 32) | id;
+}
+
+// ------------------------------------------------------------ counters
+std::atomic<uint64_t> g_search_evals{0};
+std::atomic<uint64_t> g_search_expansions{0};
+std::atomic<uint64_t> g_pair_evals{0};
+std::atomic<uint64_t> g_reverse_evals{0};
+std::atomic<uint64_t> g_reverse_edges{0};
+std::atomic<uint64_t> g_seed_mismatch{0};
+
+// ------------------------------------------------------------ visited set
+// Per-thread epoch-tagged array over all ids: exact membership.
+struct Visited
+{
+    std::vector<uint32_t> tag;
+    uint32_t epoch = 0;
+    void reset(uint32_t N)
+    {
+        if (tag.size() < N)
+            tag.assign(N, 0);
+        if (++epoch == 0)
+        {
+            std::fill(tag.begin(), tag.end(), 0);
+            epoch = 1;
+        }
+    }
+    bool test_and_set(uint32_t id)
+    {
+        if (tag[id] == epoch)
+            return true;
+        tag[id] = epoch;
+        return false;
+    }
+};
+
+// ------------------------------------------------------------ search pools
+// pool_mode 0: candidates ordered by key (distance, id); the pool holds the
+// L smallest keys seen; expansion takes the smallest unexpanded key.
+struct KeyPool
+{
+    uint32_t L;
+    std::vector<uint64_t> keys;
+    std::vector<uint8_t> expanded;
+    explicit KeyPool(uint32_t L_) : L(L_) {}
+    void insert(uint32_t id, float d)
+    {
+        uint64_t k = make_key(d, id);
+        if (!keys.empty() && keys.size() >= L && k >= keys.back())
+            return;
+        auto it = std::lower_bound(keys.begin(), keys.end(), k);
+        size_t pos = (size_t)(it - keys.begin());
+        if (it != keys.end() && *it == k)
+            return;
+        keys.insert(it, k);
+        expanded.insert(expanded.begin() + (ptrdiff_t)pos, 0);
+        if (keys.size() > L)
+        {
+            keys.pop_back();
+            expanded.pop_back();
+        }
+    }
+    bool next(uint32_t &id, float &d)
+    {
+        for (size_t i = 0; i < keys.size(); ++i)
+            if (!expanded[i])
+            {
+                expanded[i] = 1;
+                id = (uint32_t)(keys[i] & 0xFFFFFFFFu);
+                uint32_t bits = (uint32_t)(keys[i] >> 32);
+                std::memcpy(&d, &bits, 4);
+                return true;
+            }
+        return false;
+    }
+};
+
+// pool_mode 1: literal restatement of the reference slot pool
+// (insert_top_l_state_warp :598-692, select_next_unexpanded_size_warp :694-734).
+struct SlotPool
+{
+    uint32_t L;
+    std::vector<uint32_t> ids;
+    std::vector<float> d;
+    std::vector<uint8_t> exp;
+    uint32_t size = 0;
+    int max_pos = -1;
+    float max_d = -FLT_MAX;
+    explicit SlotPool(uint32_t L_) : L(L_), ids(L_, kInvalid), d(L_, FLT_MAX), exp(L_, 0) {}
+    void recompute_max()
+    {
+        max_pos = -1;
+        max_d = -FLT_MAX;
+        for (uint32_t p = 0; p < size; ++p)
+            if (ids[p] != kInvalid && d[p] > max_d)
+            {
+                max_d = d[p];
+                max_pos = (int)p;
+            }
+    }
+    void insert(uint32_t id, float dist)
+    {
+        if (id == kInvalid)
+            return;
+        if (size >= L && max_pos >= 0 && dist >= max_d)
+            return;
+        for (uint32_t p = 0; p < size; ++p)
+            if (ids[p] == id)
+            {
+                if (dist < d[p])
+                {
+                    d[p] = dist;
+                    exp[p] = 0;
+                    if ((int)p == max_pos)
+                        recompute_max();
+                }
+                return;
+            }
+        if (size < L)
+        {
+            ids[size] = id;
+            d[size] = dist;
+            exp[size] = 0;
+            if (max_pos < 0 || dist > max_d)
+            {
+                max_pos = (int)size;
+                max_d = dist;
+            }
+            ++size;
+            return;
+        }
+        if (max_pos >= 0 && dist < max_d)
+        {
+            ids[max_pos] = id;
+            d[max_pos] = dist;
+            exp[max_pos] = 0;
+            recompute_max();
+        }
+    }
+    bool next(uint32_t &id, float &dist)
+    {
+        int best = -1;
+        float bd = FLT_MAX;
+        for (uint32_t p = 0; p < size; ++p)
+            if (ids[p] != kInvalid && !exp[p] && d[p] < bd)
+            {
+                bd = d[p];
+                best = (int)p;
+            }
+        if (best < 0)
+            return false;
+        exp[best] = 1;
+        id = ids[best];
+        dist = d[best];
+        return true;
+    }
+};
+
+struct Graph
+{
+    uint32_t N, R, C;
+    std::vector<uint32_t> cur_ids;   // N x R
+    std::vector<float> cur_dists;    // N x R
+    std::vector<uint32_t> degree;    // N
+    std::vector<uint32_t> work_ids;  // N x C
+    std::vector<float> work_dists;   // N x C
+    std::vector<uint32_t> work_deg;  // N
+};
+
+// GreedySearch of vertex v on the frozen graph; returns the expansion
+// sequence (reference :1166-1423 without the inline insert).
+template <class Pool>
+void search_vertex(const Store &st, uint32_t N, uint32_t R, uint32_t L, uint32_t max_steps, uint32_t entry,
+                   uint32_t seeds, const uint32_t *cur_ids, const float *cur_dists, const uint32_t *degree,
+                   uint32_t v, Visited &vis, std::vector<uint32_t> &exp_ids, std::vector<float> &exp_d)
+{
+    Pool pool(L);
+    vis.reset(N);
+    exp_ids.clear();
+    exp_d.clear();
+    uint64_t evals = 0;
+    vis.test_and_set(v);
+    if (entry < N && entry != v)
+    {
+        if (!vis.test_and_set(entry))
+        {
+            pool.insert(entry, dist(st, v, entry));
+            ++evals;
+        }
+    }
+    uint32_t deg_self = std::min(degree[v], R);
+    for (uint32_t i = 0; i < deg_self; ++i)
+    {
+        uint32_t nb = cur_ids[(size_t)v * R + i];
+        if (nb == kInvalid || nb >= N || nb == v)
+            continue;
+        float d = cur_dists[(size_t)v * R + i];
+        if (vis.test_and_set(nb))
+        {
+            // Already evaluated (the entry point): the stored distance must
+            // equal the computed one for the skip to be exact.
+            if (nb == entry && d != dist(st, v, nb))
+                g_seed_mismatch.fetch_add(1, std::memory_order_relaxed);
+            continue;
+        }
+        pool.insert(nb, d);
+    }
+    for (uint32_t k = 0; k < seeds; ++k)
+    {
+        uint32_t s = det_neighbor(v, k + 1024u, N);
+        if (s == kInvalid || s >= N || s == v)
+            continue;
+        if (vis.test_and_set(s))
+            continue;
+        pool.insert(s, dist(st, v, s));
+        ++evals;
+    }
+    for (uint32_t step = 0; step < max_steps; ++step)
+    {
+        uint32_t x;
+        float dx;
+        if (!pool.next(x, dx))
+            break;
+        if (x == kInvalid || x >= N)
+            break;
+        exp_ids.push_back(x);
+        exp_d.push_back(dx);
+        uint32_t deg = std::min(degree[x], R);
+        for (uint32_t p = 0; p < deg; ++p)
+        {
+            uint32_t c = cur_ids[(size_t)x * R + p];
+            if (c == kInvalid || c >= N || c == v)
+                continue;
+            if (vis.test_and_set(c))
+                continue;
+            pool.insert(c, dist(st, v, c));
+            ++evals;
+        }
+    }
+    g_search_evals.fetch_add(evals, std::memory_order_relaxed);
+    g_search_expansions.fetch_add(exp_ids.size(), std::memory_order_relaxed);
+}
+
+// Work row initialisation (reference :1175-1204).
+void init_work_row(uint32_t N, uint32_t R, uint32_t C, const uint32_t *cur_ids, const float *cur_dists,
+                   const uint32_t *degree, uint32_t v, uint32_t *wid, float *wd, uint32_t &wdeg)
+{
+    uint32_t deg_self = std::min(degree[v], R);
+    for (uint32_t i = 0; i < C; ++i)
+    {
+        uint32_t nb = kInvalid;
+        float d = FLT_MAX;
+        if (i < deg_self)
+        {
+            nb = cur_ids[(size_t)v * R + i];
+            if (nb != kInvalid && nb < N && nb != v)
+                d = cur_dists[(size_t)v * R + i];
+            else
+                nb = kInvalid;
+        }
+        wid[i] = nb;
+        wd[i] = d;
+    }
+    wdeg = deg_self;
+}
+
+// Online RobustInsert of x into v's C-wide work row
+// (dynamic_robust_insert_C_warp, reference :759-877).
+void robust_insert(const Store &st, uint32_t N, uint32_t C, uint32_t v, uint32_t x, float d_px, float alpha,
+                   uint32_t *row, float *drow, uint32_t &wdeg, uint64_t &pairs)
+{
+    if (x == kInvalid || x >= N || x == v)
+        return;
+    uint32_t deg = std::min(wdeg, C);
+    for (uint32_t i = 0; i < deg; ++i)
+        if (row[i] == x)
+            return;
+    for (uint32_t i = 0; i < deg; ++i)
+    {
+        uint32_t y = row[i];
+        if (y == kInvalid || y >= N || y == v)
+            continue;
+        if (drow[i] <= d_px)
+        {
+            float d_yx = dist(st, y, x);
+            ++pairs;
+            if (alpha * d_yx <= d_px)
+                return; // occluded
+        }
+    }
+    int worst_pos = -1, victim_pos = -1;
+    float worst = -FLT_MAX, victim = -FLT_MAX;
+    for (uint32_t i = 0; i < deg; ++i)
+    {
+        uint32_t y = row[i];
+        if (y == kInvalid || y >= N || y == v)
+            continue;
+        float d_py = drow[i];
+        if (d_py > worst)
+        {
+            worst = d_py;
+            worst_pos = (int)i;
+        }
+        if (d_py > d_px)
+        {
+            float d_xy = dist(st, x, y);
+            ++pairs;
+            if (alpha * d_xy <= d_py && d_py > victim)
+            {
+                victim = d_py;
+                victim_pos = (int)i;
+            }
+        }
+    }
+    if (victim_pos >= 0)
+    {
+        row[victim_pos] = x;
+        drow[victim_pos] = d_px;
+    }
+    else if (deg < C)
+    {
+        row[deg] = x;
+        drow[deg] = d_px;
+        wdeg = deg + 1;
+    }
+    else if (worst_pos >= 0 && d_px < worst)
+    {
+        row[worst_pos] = x;
+        drow[worst_pos] = d_px;
+    }
+}
+
+// Reverse merge of target t (reverse_merge_csr_kernel, reference :1722-1814)
+// over its sources in CSR order.
+void reverse_merge_target(const Store &st, uint32_t N, uint32_t C, uint32_t t, const uint32_t *srcs, uint32_t indeg,
+                          const DanceVamanaParams &p, uint32_t *row, float *drow, uint32_t &wdeg, uint64_t &evals)
+{
+    uint32_t deg = std::min(wdeg, C);
+    uint32_t count = indeg;
+    bool sampled = false;
+    if (p.reverse_heavy_cap && indeg > p.reverse_heavy_threshold)
+    {
+        count = std::min(p.reverse_heavy_sample, indeg);
+        if (count == 0)
+            count = 1;
+        sampled = count < indeg;
+    }
+    for (uint32_t k = 0; k < count; ++k)
+    {
+        uint32_t i = sampled ? (uint32_t)(((uint64_t)k * indeg) / count) : k;
+        uint32_t s = srcs[i];
+        if (s == kInvalid || s >= N || s == t)
+            continue;
+        bool present = false;
+        for (uint32_t j = 0; j < deg; ++j)
+            if (row[j] == s)
+            {
+                present = true;
+                break;
+            }
+        if (present)
+            continue;
+        float d = dist(st, t, s);
+        ++evals;
+        if (deg < C)
+        {
+            row[deg] = s;
+            drow[deg] = d;
+            ++deg;
+            continue;
+        }
+        int wpos = -1;
+        float w = -FLT_MAX;
+        for (uint32_t j = 0; j < C; ++j)
+            if (drow[j] > w)
+            {
+                w = drow[j];
+                wpos = (int)j;
+            }
+        if (wpos >= 0 && d < w)
+        {
+            row[wpos] = s;
+            drow[wpos] = d;
+        }
+    }
+    wdeg = deg;
+}
+
+// RobustPrune(alpha) + optional degree fill (final_prune_kernel_shared,
+// reference :1893-2147).  Writes the R-wide output row.
+void prune_vertex(const Store &st, uint32_t N, uint32_t R, uint32_t C, float alpha, uint32_t min_degree, uint32_t v,
+                  const uint32_t *wid, const float *wd, uint32_t wdeg, uint32_t *out_ids, float *out_d,
+                  uint32_t &out_deg, uint64_t &pairs)
+{
+    std::vector<uint32_t> sid(C);
+    std::vector<float> sd(C);
+    std::vector<uint8_t> removed(C);
+    uint32_t deg = std::min(wdeg, C);
+    for (uint32_t i = 0; i < C; ++i)
+    {
+        uint32_t id = kInvalid;
+        float d = FLT_MAX;
+        uint8_t rm = 1;
+        if (i < deg)
+        {
+            id = wid[i];
+            d = wd[i];
+            if (id != kInvalid && id < N && id != v && d < FLT_MAX)
+                rm = 0;
+            else
+                id = kInvalid;
+        }
+        sid[i] = id;
+        sd[i] = d;
+        removed[i] = rm;
+    }
+    for (uint32_t i = 0; i < R; ++i)
+    {
+        out_ids[i] = kInvalid;
+        out_d[i] = FLT_MAX;
+    }
+    uint32_t out = 0;
+    for (uint32_t round = 0; round < R; ++round)
+    {
+        int best = -1;
+        float bd = FLT_MAX;
+        for (uint32_t i = 0; i < C; ++i)
+            if (!removed[i] && sid[i] != kInvalid && sid[i] < N && sid[i] != v)
+                if (sd[i] < bd || (sd[i] == bd && best < 0))
+                {
+                    bd = sd[i];
+                    best = (int)i;
+                }
+        if (best < 0)
+            break;
+        uint32_t sel = sid[best];
+        float seld = sd[best];
+        out_ids[out] = sel;
+        out_d[out] = seld;
+        ++out;
+        if (out >= R)
+            break;
+        for (uint32_t i = 0; i < C; ++i)
+            if (!removed[i] && sid[i] == sel)
+                removed[i] = 1;
+        for (uint32_t q = 0; q < C; ++q)
+        {
+            if (removed[q] || sid[q] == kInvalid || sid[q] >= N || sid[q] == v)
+                continue;
+            if (seld <= sd[q])
+            {
+                float dq = dist(st, sel, sid[q]);
+                ++pairs;
+                if (alpha * dq <= sd[q])
+                    removed[q] = 1;
+            }
+        }
+    }
+    if (min_degree > R)
+        min_degree = R;
+    while (out < min_degree)
+    {
+        int best = -1;
+        float bd = FLT_MAX;
+        for (uint32_t i = 0; i < C; ++i)
+        {
+            uint32_t id = sid[i];
+            if (id == kInvalid || id >= N || id == v)
+                continue;
+            bool dup = false;
+            for (uint32_t j = 0; j < out; ++j)
+                if (out_ids[j] == id)
+                {
+                    dup = true;
+                    break;
+                }
+            if (dup)
+                continue;
+            if (sd[i] < bd || (sd[i] == bd && best < 0))
+            {
+                bd = sd[i];
+                best = (int)i;
+            }
+        }
+        if (best < 0)
+            break;
+        out_ids[out] = sid[best];
+        out_d[out] = sd[best];
+        sid[best] = kInvalid;
+        ++out;
+    }
+    out_deg = out;
+}
+
+void set_threads(int threads)
+{
+#ifdef _OPENMP
+    if (threads > 0)
+        omp_set_num_threads(threads);
+#else
+    (void)threads;
+#endif
+}
+
+Store make_store(int dtype, const void *data, uint64_t stride, uint32_t dim)
+{
+    Store st;
+    st.dtype = dtype;
+    st.base = reinterpret_cast<const uint8_t *>(data);
+    st.stride = stride;
+    st.dim = dim;
+    return st;
+}
+
+uint32_t medoid(const Store &st, uint32_t N, uint32_t nc, uint32_t ns, float *scores, uint32_t *cand_ids)
+{
+    nc = std::min(nc, N);
+    ns = std::min(ns, N);
+    if (nc == 0 || ns == 0)
+        return 0;
+    std::vector<float> sc(nc);
+    std::vector<uint32_t> ci(nc);
+#pragma omp parallel for schedule(dynamic, 8)
+    for (int64_t w = 0; w < (int64_t)nc; ++w)
+    {
+        uint32_t cand = hash_u32((uint32_t)w * 9973u + 17u) % N;
+        float sum = 0.0f;
+        for (uint32_t s = 0; s < ns; ++s)
+        {
+            uint32_t smp = hash_u32(s * 10007u + 131u) % N;
+            if (smp == cand)
+                continue;
+            sum = sum + dist(st, cand, smp);
+        }
+        sc[w] = sum / (float)ns;
+        ci[w] = cand;
+    }
+    uint32_t best = 0;
+    float bs = FLT_MAX;
+    bool found = false;
+    for (uint32_t w = 0; w < nc; ++w)
+        if (sc[w] < bs)
+        {
+            bs = sc[w];
+            best = ci[w];
+            found = true;
+        }
+    if (scores)
+        std::memcpy(scores, sc.data(), nc * sizeof(float));
+    if (cand_ids)
+        std::memcpy(cand_ids, ci.data(), nc * sizeof(uint32_t));
+    return found ? best : 0;
+}
+
+void init_graph(const Store &st, Graph &g)
+{
+#pragma omp parallel for schedule(static)
+    for (int64_t v = 0; v < (int64_t)g.N; ++v)
+    {
+        for (uint32_t i = 0; i < g.R; ++i)
+        {
+            uint32_t nb = det_neighbor((uint32_t)v, i, g.N);
+            if (g.N <= 1 || nb == kInvalid || nb >= g.N || nb == (uint32_t)v)
+                nb = kInvalid;
+            g.cur_ids[(size_t)v * g.R + i] = nb;
+            g.cur_dists[(size_t)v * g.R + i] = nb != kInvalid ? dist(st, (uint32_t)v, nb) : FLT_MAX;
+        }
+        g.degree[v] = g.N > 1 ? g.R : 0;
+    }
+}
+
+void search_and_replay_all(const Store &st, Graph &g, uint32_t L, uint32_t steps, uint32_t entry, uint32_t seeds,
+                           float alpha, int pool_mode)
+{
+    std::atomic<uint64_t> pairs_total{0};
+#pragma omp parallel
+    {
+        Visited vis;
+        std::vector<uint32_t> eid;
+        std::vector<float> ed;
+        uint64_t pairs = 0;
+#pragma omp for schedule(dynamic, 64)
+        for (int64_t vv = 0; vv < (int64_t)g.N; ++vv)
+        {
+            uint32_t v = (uint32_t)vv;
+            if (pool_mode == 1)
+                search_vertex<SlotPool>(st, g.N, g.R, L, steps, entry, seeds, g.cur_ids.data(), g.cur_dists.data(),
+                                        g.degree.data(), v, vis, eid, ed);
+            else
+                search_vertex<KeyPool>(st, g.N, g.R, L, steps, entry, seeds, g.cur_ids.data(), g.cur_dists.data(),
+                                       g.degree.data(), v, vis, eid, ed);
+            uint32_t *wid = &g.work_ids[(size_t)v * g.C];
+            float *wd = &g.work_dists[(size_t)v * g.C];
+            init_work_row(g.N, g.R, g.C, g.cur_ids.data(), g.cur_dists.data(), g.degree.data(), v, wid, wd,
+                          g.work_deg[v]);
+            for (size_t k = 0; k < eid.size(); ++k)
+                robust_insert(st, g.N, g.C, v, eid[k], ed[k], alpha, wid, wd, g.work_deg[v], pairs);
+        }
+        pairs_total.fetch_add(pairs);
+    }
+    g_pair_evals.fetch_add(pairs_total.load());
+}
+
+// Reverse CSR over the first min(deg, R) work slots, sources ascending.
+void build_reverse(const Graph &g, std::vector<uint32_t> &offsets, std::vector<uint32_t> &srcs)
+{
+    offsets.assign((size_t)g.N + 1, 0);
+    for (uint32_t s = 0; s < g.N; ++s)
+    {
+        uint32_t deg = std::min(g.work_deg[s], g.R);
+        for (uint32_t p = 0; p < deg; ++p)
+        {
+            uint32_t t = g.work_ids[(size_t)s * g.C + p];
+            if (t != kInvalid && t < g.N && t != s)
+                offsets[(size_t)t + 1]++;
+        }
+    }
+    for (size_t i = 0; i < g.N; ++i)
+        offsets[i + 1] += offsets[i];
+    srcs.assign(offsets[g.N], 0);
+    std::vector<uint32_t> cursor(offsets.begin(), offsets.end() - 1);
+    for (uint32_t s = 0; s < g.N; ++s)
+    {
+        uint32_t deg = std::min(g.work_deg[s], g.R);
+        for (uint32_t p = 0; p < deg; ++p)
+        {
+            uint32_t t = g.work_ids[(size_t)s * g.C + p];
+            if (t != kInvalid && t < g.N && t != s)
+                srcs[cursor[t]++] = s;
+        }
+    }
+}
+
+void reverse_merge_all(const Store &st, Graph &g, const DanceVamanaParams &p, uint64_t *edges_out)
+{
+    std::vector<uint32_t> offsets, srcs;
+    build_reverse(g, offsets, srcs);
+    g_reverse_edges.fetch_add(srcs.size());
+    if (edges_out)
+        *edges_out = srcs.size();
+    std::atomic<uint64_t> ev{0};
+#pragma omp parallel
+    {
+        uint64_t local = 0;
+#pragma omp for schedule(dynamic, 256)
+        for (int64_t tt = 0; tt < (int64_t)g.N; ++tt)
+        {
+            uint32_t t = (uint32_t)tt;
+            uint32_t b = offsets[t], e = offsets[t + 1];
+            if (e == b)
+                continue;
+            reverse_merge_target(st, g.N, g.C, t, &srcs[b], e - b, p, &g.work_ids[(size_t)t * g.C],
+                                 &g.work_dists[(size_t)t * g.C], g.work_deg[t], local);
+        }
+        ev.fetch_add(local);
+    }
+    g_reverse_evals.fetch_add(ev.load());
+}
+
+void prune_all(const Store &st, Graph &g, float alpha, uint32_t min_degree)
+{
+    std::atomic<uint64_t> pt{0};
+#pragma omp parallel
+    {
+        uint64_t pairs = 0;
+#pragma omp for schedule(dynamic, 64)
+        for (int64_t vv = 0; vv < (int64_t)g.N; ++vv)
+        {
+            uint32_t v = (uint32_t)vv;
+            prune_vertex(st, g.N, g.R, g.C, alpha, min_degree, v, &g.work_ids[(size_t)v * g.C],
+                         &g.work_dists[(size_t)v * g.C], g.work_deg[v], &g.cur_ids[(size_t)v * g.R],
+                         &g.cur_dists[(size_t)v * g.R], g.degree[v], pairs);
+        }
+        pt.fetch_add(pairs);
+    }
+    g_pair_evals.fetch_add(pt.load());
+}
+
+} // namespace
+
+// ====================================================================== C ABI
+extern "C" {
+
+void oracle_default_params(DanceVamanaParams *p)
+{
+    std::memset(p, 0, sizeof(*p));
+    p->iters = 4;
+    p->alpha = 1.2f;
+    p->init_random_seeds = 8;
+    p->final_min_degree = 64;
+    p->medoid_candidates = 1024;
+    p->medoid_samples = 4096;
+    p->coarse_warmup_iters = 2;
+    p->warmup_expand_steps = 64;
+    p->reverse_heavy_cap = 0;
+    p->reverse_heavy_threshold = 256;
+    p->reverse_heavy_sample = 256;
+    p->visited_log2 = 11;
+}
+
+void oracle_reset_counters(void)
+{
+    g_search_evals = 0;
+    g_search_expansions = 0;
+    g_pair_evals = 0;
+    g_reverse_evals = 0;
+    g_reverse_edges = 0;
+    g_seed_mismatch = 0;
+}
+
+// out[0..5] = search evals, expansions, pair evals (insert + prune),
+// reverse evals, reverse edges, stored/computed distance mismatches.
+void oracle_get_counters(uint64_t *out)
+{
+    out[0] = g_search_evals;
+    out[1] = g_search_expansions;
+    out[2] = g_pair_evals;
+    out[3] = g_reverse_evals;
+    out[4] = g_reverse_edges;
+    out[5] = g_seed_mismatch;
+}
+
+float oracle_distance(int dtype, const void *a, const void *b, uint32_t dim)
+{
+    switch (dtype)
+    {
+    case DANCE_U8:
+        return dist_u8((const uint8_t *)a, (const uint8_t *)b, dim);
+    case DANCE_F16:
+        return dist_f16((const uint16_t *)a, (const uint16_t *)b, dim);
+    default:
+        return dist_f32((const float *)a, (const float *)b, dim);
+    }
+}
+
+// float32 -> binary16 (round to nearest even) for the fp16 storage mode.
+void oracle_float_to_half(const float *src, uint16_t *dst, uint64_t n)
+{
+    for (uint64_t i = 0; i < n; ++i)
+        dst[i] = double_to_half((double)src[i]);
+}
+
+uint32_t oracle_hash_u32(uint32_t x) { return hash_u32(x); }
+uint32_t oracle_det_neighbor(uint32_t node, uint32_t k, uint32_t N) { return det_neighbor(node, k, N); }
+
+uint32_t oracle_medoid(int dtype, const void *data, uint64_t stride, uint32_t N, uint32_t dim, uint32_t nc,
+                       uint32_t ns, float *scores, uint32_t *cand_ids, int threads)
+{
+    set_threads(threads);
+    Store st = make_store(dtype, data, stride, dim);
+    return medoid(st, N, nc, ns, scores, cand_ids);
+}
+
+int oracle_init(int dtype, const void *data, uint64_t stride, uint32_t N, uint32_t dim, uint32_t R,
+                uint32_t *cur_ids, float *cur_dists, uint32_t *degree, int threads)
+{
+    set_threads(threads);
+    Store st = make_store(dtype, data, stride, dim);
+    Graph g;
+    g.N = N;
+    g.R = R;
+    g.C = R;
+    g.cur_ids.resize((size_t)N * R);
+    g.cur_dists.resize((size_t)N * R);
+    g.degree.resize(N);
+    init_graph(st, g);
+    std::memcpy(cur_ids, g.cur_ids.data(), g.cur_ids.size() * 4);
+    std::memcpy(cur_dists, g.cur_dists.data(), g.cur_dists.size() * 4);
+    std::memcpy(degree, g.degree.data(), g.degree.size() * 4);
+    return 0;
+}
+
+// Expansion sequences of every vertex (exp_stride slots each).
+int oracle_search(int dtype, const void *data, uint64_t stride, uint32_t N, uint32_t dim, uint32_t R, uint32_t L,
+                  uint32_t steps, uint32_t entry, uint32_t seeds, int pool_mode, const uint32_t *cur_ids,
+                  const float *cur_dists, const uint32_t *degree, uint32_t *exp_ids, float *exp_dists,
+                  uint32_t *exp_count, uint32_t exp_stride, int threads)
+{
+    set_threads(threads);
+    Store st = make_store(dtype, data, stride, dim);
+    steps = std::min(steps, L);
+    if (steps > exp_stride)
+        return -1;
+#pragma omp parallel
+    {
+        Visited vis;
+        std::vector<uint32_t> eid;
+        std::vector<float> ed;
+#pragma omp for schedule(dynamic, 64)
+        for (int64_t vv = 0; vv < (int64_t)N; ++vv)
+        {
+            uint32_t v = (uint32_t)vv;
+            if (pool_mode == 1)
+                search_vertex<SlotPool>(st, N, R, L, steps, entry, seeds, cur_ids, cur_dists, degree, v, vis, eid,
+                                        ed);
+            else
+                search_vertex<KeyPool>(st, N, R, L, steps, entry, seeds, cur_ids, cur_dists, degree, v, vis, eid, ed);
+            exp_count[v] = (uint32_t)eid.size();
+            for (uint32_t k = 0; k < exp_stride; ++k)
+            {
+                exp_ids[(size_t)v * exp_stride + k] = k < eid.size() ? eid[k] : kInvalid;
+                exp_dists[(size_t)v * exp_stride + k] = k < eid.size() ? ed[k] : FLT_MAX;
+            }
+        }
+    }
+    return 0;
+}
+
+int oracle_replay(int dtype, const void *data, uint64_t stride, uint32_t N, uint32_t dim, uint32_t R, uint32_t C,
+                  float alpha, const uint32_t *cur_ids, const float *cur_dists, const uint32_t *degree,
+                  const uint32_t *exp_ids, const float *exp_dists, const uint32_t *exp_count, uint32_t exp_stride,
+                  uint32_t *work_ids, float *work_dists, uint32_t *work_deg, int threads)
+{
+    set_threads(threads);
+    Store st = make_store(dtype, data, stride, dim);
+#pragma omp parallel for schedule(dynamic, 64)
+    for (int64_t vv = 0; vv < (int64_t)N; ++vv)
+    {
+        uint32_t v = (uint32_t)vv;
+        uint64_t pairs = 0;
+        uint32_t *wid = &work_ids[(size_t)v * C];
+        float *wd = &work_dists[(size_t)v * C];
+        init_work_row(N, R, C, cur_ids, cur_dists, degree, v, wid, wd, work_deg[v]);
+        for (uint32_t k = 0; k < exp_count[v]; ++k)
+            robust_insert(st, N, C, v, exp_ids[(size_t)v * exp_stride + k], exp_dists[(size_t)v * exp_stride + k],
+                          alpha, wid, wd, work_deg[v], pairs);
+    }
+    return 0;
+}
+
+int oracle_reverse_merge(int dtype, const void *data, uint64_t stride, uint32_t N, uint32_t dim, uint32_t R,
+                         uint32_t C, const DanceVamanaParams *params, uint32_t *work_ids, float *work_dists,
+                         uint32_t *work_deg, uint64_t *edges_out, int threads)
+{
+    set_threads(threads);
+    Store st = make_store(dtype, data, stride, dim);
+    Graph g;
+    g.N = N;
+    g.R = R;
+    g.C = C;
+    g.work_ids.assign(work_ids, work_ids + (size_t)N * C);
+    g.work_dists.assign(work_dists, work_dists + (size_t)N * C);
+    g.work_deg.assign(work_deg, work_deg + N);
+    DanceVamanaParams p;
+    if (params)
+        p = *params;
+    else
+        oracle_default_params(&p);
+    reverse_merge_all(st, g, p, edges_out);
+    std::memcpy(work_ids, g.work_ids.data(), g.work_ids.size() * 4);
+    std::memcpy(work_dists, g.work_dists.data(), g.work_dists.size() * 4);
+    std::memcpy(work_deg, g.work_deg.data(), g.work_deg.size() * 4);
+    return 0;
+}
+
+int oracle_prune(int dtype, const void *data, uint64_t stride, uint32_t N, uint32_t dim, uint32_t R, uint32_t C,
+                 float alpha, uint32_t min_degree, const uint32_t *work_ids, const float *work_dists,
+                 const uint32_t *work_deg, uint32_t *cur_ids, float *cur_dists, uint32_t *degree, int threads)
+{
+    set_threads(threads);
+    Store st = make_store(dtype, data, stride, dim);
+#pragma omp parallel for schedule(dynamic, 64)
+    for (int64_t vv = 0; vv < (int64_t)N; ++vv)
+    {
+        uint32_t v = (uint32_t)vv;
+        uint64_t pairs = 0;
+        prune_vertex(st, N, R, C, alpha, min_degree, v, &work_ids[(size_t)v * C], &work_dists[(size_t)v * C],
+                     work_deg[v], &cur_ids[(size_t)v * R], &cur_dists[(size_t)v * R], degree[v], pairs);
+    }
+    return 0;
+}
+
+// Whole build (round driver, reference :2170-2855).
+int oracle_build(int dtype, const void *data, uint64_t stride, uint32_t N, uint32_t dim, uint32_t R, uint32_t L,
+                 uint32_t C, uint32_t STEPS, const DanceVamanaParams *params, int pool_mode, int threads,
+                 uint32_t *graph, uint32_t *degree, float *dists, uint32_t *medoid_out)
+{
+    if (!data || !graph || !degree || N == 0 || dim == 0 || R == 0 || L == 0 || C == 0 || STEPS == 0 || C < R)
+        return -1;
+    set_threads(threads);
+    DanceVamanaParams p;
+    if (params)
+        p = *params;
+    else
+        oracle_default_params(&p);
+    if (STEPS > L)
+        STEPS = L;
+    Store st = make_store(dtype, data, stride, dim);
+    uint32_t entry = medoid(st, N, p.medoid_candidates, p.medoid_samples, nullptr, nullptr);
+    Graph g;
+    g.N = N;
+    g.R = R;
+    g.C = C;
+    g.cur_ids.resize((size_t)N * R);
+    g.cur_dists.resize((size_t)N * R);
+    g.degree.resize(N);
+    g.work_ids.resize((size_t)N * C);
+    g.work_dists.resize((size_t)N * C);
+    g.work_deg.resize(N);
+    init_graph(st, g);
+    for (uint32_t it = 0; it < p.iters; ++it)
+    {
+        float alpha = (it + 1 >= p.iters) ? p.alpha : 1.0f;
+        uint32_t steps = STEPS;
+        if (it < p.coarse_warmup_iters && steps > p.warmup_expand_steps)
+            steps = p.warmup_expand_steps;
+        search_and_replay_all(st, g, L, steps, entry, p.init_random_seeds, alpha, pool_mode);
+        reverse_merge_all(st, g, p, nullptr);
+        uint32_t min_degree = (it + 1 == p.iters) ? p.final_min_degree : 0;
+        prune_all(st, g, alpha, min_degree);
+    }
+    std::memcpy(graph, g.cur_ids.data(), g.cur_ids.size() * 4);
+    std::memcpy(degree, g.degree.data(), g.degree.size() * 4);
+    if (dists)
+        std::memcpy(dists, g.cur_dists.data(), g.cur_dists.size() * 4);
+    if (medoid_out)
+        *medoid_out = entry;
+    return 0;
+}
+
+// DiskANN-style best-first query search (list size L, K results), pool
+// ordered by (distance, id); runs until every list entry is expanded.
+int oracle_search_queries(int dtype, const void *data, uint64_t stride, uint32_t N, uint32_t dim,
+                          const uint32_t *graph, uint32_t R, uint32_t start, const void *queries, uint64_t qstride,
+                          uint32_t nq, uint32_t L, uint32_t K, uint32_t *out_ids, float *out_dists, int threads)
+{
+    set_threads(threads);
+    Store st = make_store(dtype, data, stride, dim);
+    const uint8_t *qb = reinterpret_cast<const uint8_t *>(queries);
+#pragma omp parallel
+    {
+        Visited vis;
+#pragma omp for schedule(dynamic, 16)
+        for (int64_t qi = 0; qi < (int64_t)nq; ++qi)
+        {
+            const uint8_t *q = qb + (uint64_t)qi * qstride;
+            KeyPool pool(L);
+            vis.reset(N);
+            if (start < N)
+            {
+                vis.test_and_set(start);
+                pool.insert(start, dist_query(st, q, start));
+            }
+            uint32_t x;
+            float dx;
+            while (pool.next(x, dx))
+            {
+                for (uint32_t p = 0; p < R; ++p)
+                {
+                    uint32_t c = graph[(size_t)x * R + p];
+                    if (c == kInvalid || c >= N)
+                        continue;
+                    if (vis.test_and_set(c))
+                        continue;
+                    pool.insert(c, dist_query(st, q, c));
+                }
+            }
+            for (uint32_t k = 0; k < K; ++k)
+            {
+                if (k < pool.keys.size())
+                {
+                    out_ids[(size_t)qi * K + k] = (uint32_t)(pool.keys[k] & 0xFFFFFFFFu);
+                    uint32_t bits = (uint32_t)(pool.keys[k] >> 32);
+                    float d;
+                    std::memcpy(&d, &bits, 4);
+                    out_dists[(size_t)qi * K + k] = d;
+                }
+                else
+                {
+                    out_ids[(size_t)qi * K + k] = kInvalid;
+                    out_dists[(size_t)qi * K + k] = FLT_MAX;
+                }
+            }
+        }
+    }
+    return 0;
+}
+
+} // extern "C"
