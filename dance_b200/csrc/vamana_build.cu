@@ -25,449 +25,13 @@
 #include "../../include/dance_b200.h"
 #include "../../include/gpu_vamana_builder.h"
 #include "../../include/gpu_vamana_config.h"
-#include "vamana_kernels.cuh"
+#include "host_common.cuh"
 
 namespace dance
 {
+thread_local char g_err[512] = "";
+std::atomic<uint64_t> g_launches{0};
 
-// ---------------------------------------------------------------- errors
-static thread_local char g_err[512] = "";
-static std::atomic<uint64_t> g_launches{0};
-
-static int fail(int code, const char *fmt, ...)
-{
-    va_list ap;
-    va_start(ap, fmt);
-    vsnprintf(g_err, sizeof(g_err), fmt, ap);
-    va_end(ap);
-    fprintf(stderr, "[dance_b200] %s\n", g_err);
-    return code;
-}
-
-#define DANCE_CUDA(call)                                                                                        \
-    do                                                                                                          \
-    {                                                                                                           \
-        cudaError_t e__ = (call);                                                                               \
-        if (e__ != cudaSuccess)                                                                                 \
-            return fail(-2, "CUDA error %s at %s:%d (%s)", cudaGetErrorString(e__), __FILE__, __LINE__, #call); \
-    } while (0)
-
-#define DANCE_LAUNCHED()                                                                                        \
-    do                                                                                                          \
-    {                                                                                                           \
-        g_launches.fetch_add(1, std::memory_order_relaxed);                                                    \
-        cudaError_t e__ = cudaGetLastError();                                                                   \
-        if (e__ != cudaSuccess)                                                                                 \
-            return fail(-2, "kernel launch failed: %s at %s:%d", cudaGetErrorString(e__), __FILE__, __LINE__);  \
-    } while (0)
-
-static inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
-
-// ---------------------------------------------------------------- device buffer
-struct DevBuf
-{
-    void *p = nullptr;
-    size_t bytes = 0;
-    DevBuf() = default;
-    DevBuf(const DevBuf &) = delete;
-    DevBuf &operator=(const DevBuf &) = delete;
-    ~DevBuf() { release(); }
-    void release()
-    {
-        if (p)
-            cudaFree(p);
-        p = nullptr;
-        bytes = 0;
-    }
-    cudaError_t ensure(size_t b)
-    {
-        if (b <= bytes && p)
-            return cudaSuccess;
-        release();
-        cudaError_t e = cudaMalloc(&p, b ? b : 16);
-        if (e == cudaSuccess)
-            bytes = b;
-        return e;
-    }
-    template <class T>
-    T *as() const
-    {
-        return reinterpret_cast<T *>(p);
-    }
-};
-
-static int elem_size(int dtype)
-{
-    switch (dtype)
-    {
-    case kU8:
-        return 1;
-    case kF16:
-        return 2;
-    case kF32:
-        return 4;
-    default:
-        return 0;
-    }
-}
-
-static int sm_count()
-{
-    int dev = 0, n = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    return n > 0 ? n : 1;
-}
-
-// One wave of resident blocks (a multiple of the SM count), or fewer when
-// there is less work than that.
-template <class K>
-static int wave_grid(K kernel, int threads, size_t smem, uint64_t work_warps)
-{
-    int per_sm = 0;
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, smem);
-    if (per_sm < 1)
-        per_sm = 1;
-    const uint64_t wave = (uint64_t)per_sm * sm_count();
-    const uint64_t need = (work_warps + (threads / 32) - 1) / (threads / 32);
-    uint64_t g = need < wave ? need : wave;
-    return (int)(g ? g : 1);
-}
-
-template <class K>
-static cudaError_t allow_smem(K kernel, size_t smem)
-{
-    if (smem <= 48 * 1024)
-        return cudaSuccess;
-    return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-}
-
-static int max_optin_smem()
-{
-    int dev = 0, v = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
-    return v;
-}
-
-// ---------------------------------------------------------------- CPL dispatch
-// Chunks (16 bytes) per group lane; instantiated widths cover rows up to
-// 1024 bytes (f32 dim <= 256, f16 <= 512, u8 <= 1024).
-template <template <int, int> class F, int DT, class... A>
-static int dispatch_cpl(uint32_t nchunks, A &&...args)
-{
-    const uint32_t cpl = (nchunks + 7) / 8;
-    if (cpl <= 1)
-        return F<DT, 1>::run(args...);
-    if (cpl <= 2)
-        return F<DT, 2>::run(args...);
-    if (cpl <= 3)
-        return F<DT, 3>::run(args...);
-    if (cpl <= 4)
-        return F<DT, 4>::run(args...);
-    if (cpl <= 8)
-        return F<DT, 8>::run(args...);
-    return fail(-1, "row of %u bytes exceeds the 1024-byte limit of this build", nchunks * 16);
-}
-
-template <template <int, int> class F, class... A>
-static int dispatch(int dtype, uint32_t nchunks, A &&...args)
-{
-    switch (dtype)
-    {
-    case kU8:
-        return dispatch_cpl<F, kU8>(nchunks, args...);
-    case kF16:
-        return dispatch_cpl<F, kF16>(nchunks, args...);
-    case kF32:
-        return dispatch_cpl<F, kF32>(nchunks, args...);
-    default:
-        return fail(-1, "unknown dtype %d", dtype);
-    }
-}
-
-// ---------------------------------------------------------------- launchers
-template <int DT, int CPL>
-struct LaunchMedoid
-{
-    static int run(const StoreView &st, uint32_t nc, uint32_t ns, float *scores, uint32_t *cand, uint32_t *medoid,
-                   cudaStream_t s)
-    {
-        const int blocks = (int)((nc + kWarpsPerBlock - 1) / kWarpsPerBlock);
-        medoid_score_kernel<DT, CPL><<<blocks, kBlockThreads, 0, s>>>(st, nc, ns, scores, cand);
-        DANCE_LAUNCHED();
-        medoid_argmin_kernel<<<1, 1024, 0, s>>>(scores, cand, nc, medoid);
-        DANCE_LAUNCHED();
-        return 0;
-    }
-};
-
-template <int DT, int CPL>
-struct LaunchInit
-{
-    static int run(const StoreView &st, uint32_t R, uint32_t *ids, float *dists, uint32_t *deg, uint32_t v0,
-                   uint32_t v1, cudaStream_t s)
-    {
-        auto k = init_graph_kernel<DT, CPL>;
-        const int grid = wave_grid(k, kBlockThreads, 0, v1 - v0);
-        k<<<grid, kBlockThreads, 0, s>>>(st, R, ids, dists, deg, v0, v1);
-        DANCE_LAUNCHED();
-        return 0;
-    }
-};
-
-template <int DT, int CPL>
-struct LaunchSearch
-{
-    static int run(const SearchParams &p, cudaStream_t s)
-    {
-        auto k = search_kernel<DT, CPL>;
-        const size_t smem = (size_t)search_smem_per_warp(p.Lcap, p.log2h) * kWarpsPerBlock;
-        if ((int)smem > max_optin_smem())
-            return fail(-1, "search scratch %zu B exceeds shared memory (L=%u, visited 2^%u)", smem, p.L, p.log2h);
-        DANCE_CUDA(allow_smem(k, smem));
-        const int grid = wave_grid(k, kBlockThreads, smem, p.v1 - p.v0);
-        k<<<grid, kBlockThreads, smem, s>>>(p);
-        DANCE_LAUNCHED();
-        return 0;
-    }
-};
-
-template <int DT, int CPL>
-struct LaunchQuery
-{
-    static int run(const QueryParams &p, cudaStream_t s)
-    {
-        auto k = query_search_kernel<DT, CPL>;
-        const size_t smem = (size_t)search_smem_per_warp(p.Lcap, p.log2h) * kWarpsPerBlock;
-        if ((int)smem > max_optin_smem())
-            return fail(-1, "query scratch %zu B exceeds shared memory", smem);
-        DANCE_CUDA(allow_smem(k, smem));
-        const int grid = wave_grid(k, kBlockThreads, smem, p.nq);
-        k<<<grid, kBlockThreads, smem, s>>>(p);
-        DANCE_LAUNCHED();
-        return 0;
-    }
-};
-
-template <int DT, int CPL>
-struct LaunchReplay
-{
-    static int run(ReplayParams p, cudaStream_t s)
-    {
-        auto k = replay_kernel<DT, CPL>;
-        p.per_warp = align16(replay_smem_per_warp(p.C, p.cache_rows, p.row_bytes));
-        const size_t smem = (size_t)p.per_warp * kWarpsPerBlock;
-        if ((int)smem > max_optin_smem())
-            return fail(-1, "replay vector cache %zu B exceeds shared memory (R+steps=%u rows of %u B)", smem,
-                        p.cache_rows, p.row_bytes);
-        DANCE_CUDA(allow_smem(k, smem));
-        const int grid = wave_grid(k, kBlockThreads, smem, p.v1 - p.v0);
-        k<<<grid, kBlockThreads, smem, s>>>(p);
-        DANCE_LAUNCHED();
-        return 0;
-    }
-};
-
-template <int DT, int CPL>
-struct LaunchMerge
-{
-    static int run(MergeParams p, cudaStream_t s)
-    {
-        auto k = merge_kernel<DT, CPL>;
-        p.sort_cap = kMergeSortCap;
-        p.per_warp = align16(merge_smem_per_warp(p.C, p.sort_cap));
-        const size_t smem = (size_t)p.per_warp * kWarpsPerBlock;
-        DANCE_CUDA(allow_smem(k, smem));
-        const int grid = wave_grid(k, kBlockThreads, smem, p.t1 - p.t0);
-        k<<<grid, kBlockThreads, smem, s>>>(p);
-        DANCE_LAUNCHED();
-        auto hk = heavy_merge_kernel<DT, CPL>;
-        const size_t hsmem = 4u * kHeavySortCap + align16(4u * p.C) * 2 + 512u;
-        DANCE_CUDA(allow_smem(hk, hsmem));
-        hk<<<sm_count(), 256, hsmem, s>>>(p);
-        DANCE_LAUNCHED();
-        return 0;
-    }
-};
-
-template <int DT, int CPL>
-struct LaunchPrune
-{
-    static int run(PruneParams p, cudaStream_t s)
-    {
-        auto k = prune_kernel<DT, CPL>;
-        p.Cp = (uint32_t)next_pow2((int)p.C);
-        if (p.Cp < 32)
-            p.Cp = 32;
-        p.per_warp = align16(prune_smem_per_warp(p.C, p.Cp, p.R, p.row_bytes));
-        const size_t smem = (size_t)p.per_warp * kWarpsPerBlock;
-        if ((int)smem > max_optin_smem())
-            return fail(-1, "prune vector cache %zu B exceeds shared memory", smem);
-        DANCE_CUDA(allow_smem(k, smem));
-        const int grid = wave_grid(k, kBlockThreads, smem, p.v1 - p.v0);
-        k<<<grid, kBlockThreads, smem, s>>>(p);
-        DANCE_LAUNCHED();
-        return 0;
-    }
-};
-
-// ---------------------------------------------------------------- validation
-static int check_store(int dtype, const void *d_data, uint64_t stride, uint32_t N, uint32_t dim)
-{
-    const int es = elem_size(dtype);
-    if (!es)
-        return fail(-1, "unknown dtype %d", dtype);
-    if (!d_data || N == 0 || dim == 0)
-        return fail(-1, "null data or empty store (N=%u dim=%u)", N, dim);
-    if (stride % 16 != 0 || stride < (uint64_t)dim * es)
-        return fail(-1, "row stride %llu must be a multiple of 16 and hold dim*%d bytes", (unsigned long long)stride,
-                    es);
-    if (dtype == kF16 && (dim & 1u))
-        return fail(-1, "fp16 storage needs an even dimension (dim=%u)", dim);
-    if ((reinterpret_cast<uintptr_t>(d_data) & 15u) != 0)
-        return fail(-1, "vector store must be 16-byte aligned");
-    return 0;
-}
-
-static StoreView make_view(const void *d_data, uint64_t stride, uint32_t N, uint32_t dim, int dtype)
-{
-    StoreView st;
-    st.data = reinterpret_cast<const uint8_t *>(d_data);
-    st.stride = stride;
-    st.nchunks = (uint32_t)(((uint64_t)dim * elem_size(dtype) + 15u) / 16u);
-    st.N = N;
-    return st;
-}
-
-static uint32_t lcap_of(uint32_t L) { return (L + 31u) & ~31u; }
-
-} // namespace dance
-
-using namespace dance;
-
-// ====================================================================== workspace
-struct DanceWorkspace
-{
-    int device = 0;
-    uint32_t N = 0, R = 0, L = 0, C = 0, S = 0;
-    DevBuf cur_ids, cur_dists, degree;
-    DevBuf work_ids, work_dists, work_deg;
-    DevBuf exp_ids, exp_dists, exp_count;
-    DevBuf rev_cnt, rev_off, rev_cursor, rev, tiles;
-    DevBuf heavy_list, heavy_count;
-    DevBuf med_scores, med_cand, medoid;
-    DevBuf counters;
-
-    int reserve(uint32_t n, uint32_t r, uint32_t l, uint32_t c, uint32_t s)
-    {
-        N = n;
-        R = r;
-        L = l;
-        C = c;
-        S = s;
-        const uint64_t nr = (uint64_t)n * r, nc = (uint64_t)n * c, ns = (uint64_t)n * s;
-        const uint64_t ntiles = (n + kScanTile - 1) / kScanTile + 1;
-        DANCE_CUDA(cur_ids.ensure(nr * 4));
-        DANCE_CUDA(cur_dists.ensure(nr * 4));
-        DANCE_CUDA(degree.ensure((uint64_t)n * 4));
-        DANCE_CUDA(work_ids.ensure(nc * 4));
-        DANCE_CUDA(work_dists.ensure(nc * 4));
-        DANCE_CUDA(work_deg.ensure((uint64_t)n * 4));
-        DANCE_CUDA(exp_ids.ensure(ns * 4));
-        DANCE_CUDA(exp_dists.ensure(ns * 4));
-        DANCE_CUDA(exp_count.ensure((uint64_t)n * 4));
-        DANCE_CUDA(rev_cnt.ensure((uint64_t)n * 4));
-        DANCE_CUDA(rev_off.ensure(((uint64_t)n + 1) * 4));
-        DANCE_CUDA(rev_cursor.ensure((uint64_t)n * 4));
-        DANCE_CUDA(rev.ensure(nr * 4));
-        DANCE_CUDA(tiles.ensure(ntiles * 4));
-        DANCE_CUDA(heavy_list.ensure((uint64_t)n * 4));
-        DANCE_CUDA(heavy_count.ensure(16));
-        DANCE_CUDA(med_scores.ensure(4096 * 4));
-        DANCE_CUDA(med_cand.ensure(4096 * 4));
-        DANCE_CUDA(medoid.ensure(16));
-        DANCE_CUDA(counters.ensure(8 * 8));
-        return 0;
-    }
-};
-
-namespace dance
-{
-
-// Reverse CSR of the work rows + merge, for targets [t0, t1); sources are
-// rows [s0, s1).  Sorting inside the merge kernels puts every target's
-// sources in ascending order, so the merge is deterministic.
-static int reverse_merge_impl(int dtype, const StoreView &st, uint32_t R, uint32_t C, const DanceVamanaParams &prm,
-                              DanceWorkspace &ws, uint32_t *work_ids, float *work_dists, uint32_t *work_deg,
-                              uint32_t s0, uint32_t s1, uint32_t t0, uint32_t t1, cudaStream_t s)
-{
-    const uint32_t N = st.N;
-    DANCE_CUDA(cudaMemsetAsync(ws.rev_cnt.p, 0, (size_t)N * 4, s));
-    {
-        const uint64_t total = (uint64_t)(s1 - s0) * R;
-        int grid = (int)std::min<uint64_t>((total + 255) / 256, (uint64_t)sm_count() * 16);
-        if (grid < 1)
-            grid = 1;
-        rev_count_kernel<<<grid, 256, 0, s>>>(work_ids, work_deg, N, R, C, s0, s1, ws.rev_cnt.as<uint32_t>());
-        DANCE_LAUNCHED();
-    }
-    const uint32_t ntiles = (N + kScanTile - 1) / kScanTile;
-    scan_tile_sums_kernel<<<ntiles, kScanThreads, 0, s>>>(ws.rev_cnt.as<uint32_t>(), N, ws.tiles.as<uint32_t>());
-    DANCE_LAUNCHED();
-    scan_tile_offsets_kernel<<<1, kScanThreads, 0, s>>>(ws.tiles.as<uint32_t>(), ntiles);
-    DANCE_LAUNCHED();
-    scan_apply_kernel<<<ntiles, kScanThreads, 0, s>>>(ws.rev_cnt.as<uint32_t>(), N, ws.tiles.as<uint32_t>(),
-                                                      ws.rev_off.as<uint32_t>(), ws.rev_cursor.as<uint32_t>());
-    DANCE_LAUNCHED();
-    {
-        const uint64_t total = (uint64_t)(s1 - s0) * R;
-        int grid = (int)std::min<uint64_t>((total + 255) / 256, (uint64_t)sm_count() * 16);
-        if (grid < 1)
-            grid = 1;
-        rev_fill_kernel<<<grid, 256, 0, s>>>(work_ids, work_deg, N, R, C, s0, s1, ws.rev_cursor.as<uint32_t>(),
-                                             ws.rev.as<uint32_t>());
-        DANCE_LAUNCHED();
-    }
-    DANCE_CUDA(cudaMemsetAsync(ws.heavy_count.p, 0, 4, s));
-    MergeParams mp{};
-    mp.st = st;
-    mp.C = C;
-    mp.work_ids = work_ids;
-    mp.work_dists = work_dists;
-    mp.work_deg = work_deg;
-    mp.offsets = ws.rev_off.as<uint32_t>();
-    mp.rev = ws.rev.as<uint32_t>();
-    mp.heavy_cap = prm.reverse_heavy_cap;
-    mp.heavy_threshold = prm.reverse_heavy_threshold;
-    mp.heavy_sample = prm.reverse_heavy_sample;
-    mp.heavy_list = ws.heavy_list.as<uint32_t>();
-    mp.heavy_count = ws.heavy_count.as<uint32_t>();
-    mp.t0 = t0;
-    mp.t1 = t1;
-    mp.counters = ws.counters.as<unsigned long long>();
-    return dispatch<LaunchMerge>(dtype, st.nchunks, mp, s);
-}
-
-static uint32_t steps_for_round(uint32_t it, uint32_t STEPS, const DanceVamanaParams &p)
-{
-    uint32_t steps = STEPS;
-    if (it < p.coarse_warmup_iters && steps > p.warmup_expand_steps)
-        steps = p.warmup_expand_steps;
-    return steps;
-}
-
-// Device time per stage of one build (seconds), summed over rounds; the
-// search stage includes the online-insert replay, as in the reference's
-// search_online_insert_seconds.  search_kernel is the GreedySearch kernel
-// alone, from events recorded right after each of its launches.
-struct StageTimes
-{
-    double medoid = 0, search = 0, replay = 0, reverse = 0, prune = 0, total = 0, search_kernel = 0;
-};
-
-// The whole build on resident vectors.  graph_out/dists_out/degree_out may
-// alias the workspace's own buffers.
 static int build_resident_impl(int dtype, const void *d_data, uint64_t stride, uint32_t N, uint32_t dim, uint32_t R,
                                uint32_t L, uint32_t C, uint32_t STEPS, const DanceVamanaParams &prm,
                                DanceWorkspace &ws, uint32_t *graph_out, uint32_t *degree_out, float *dists_out,
@@ -533,7 +97,7 @@ static int build_resident_impl(int dtype, const void *d_data, uint64_t stride, u
     else
         DANCE_CUDA(cudaMemsetAsync(d_medoid, 0, 4, s));
     DANCE_CUDA(mark(1));
-    rc = dispatch<LaunchInit>(dtype, st.nchunks, st, R, cur_ids, cur_dists, degree, 0u, N, s);
+    rc = dispatch<LaunchInit>(dtype, st.nchunks, st, R, cur_ids, cur_dists, degree, 0u, N, 0u, s);
     if (rc)
         return rc;
 
@@ -591,7 +155,8 @@ static int build_resident_impl(int dtype, const void *d_data, uint64_t stride, u
         if (rc)
             return rc;
         DANCE_CUDA(mark(3 + 4 * (int)it));
-        rc = reverse_merge_impl(dtype, st, R, C, prm, ws, rp.work_ids, rp.work_dists, rp.work_deg, 0, N, 0, N, s);
+        rc = reverse_merge_impl(dtype, st, R, C, prm, ws, rp.work_ids, C, rp.work_deg, 0, N, rp.work_ids,
+                                rp.work_dists, rp.work_deg, 0, N, s);
         if (rc)
             return rc;
         DANCE_CUDA(mark(4 + 4 * (int)it));
@@ -770,7 +335,7 @@ int dance_stage_init(int dtype, const void *d_data, uint64_t stride, uint32_t N,
     if (rc)
         return rc;
     StoreView st = make_view(d_data, stride, N, dim, dtype);
-    return dispatch<LaunchInit>(dtype, st.nchunks, st, R, d_cur_ids, d_cur_dists, d_degree, 0u, N,
+    return dispatch<LaunchInit>(dtype, st.nchunks, st, R, d_cur_ids, d_cur_dists, d_degree, 0u, N, 0u,
                                 as_stream(stream));
 }
 
@@ -870,7 +435,8 @@ int dance_stage_reverse_merge(int dtype, const void *d_data, uint64_t stride, ui
     }
     cudaStream_t s = as_stream(stream);
     StoreView st = make_view(d_data, stride, N, dim, dtype);
-    rc = reverse_merge_impl(dtype, st, R, C, prm, *ws, d_work_ids, d_work_dists, d_work_deg, 0, N, 0, N, s);
+    rc = reverse_merge_impl(dtype, st, R, C, prm, *ws, d_work_ids, C, d_work_deg, 0, N, d_work_ids, d_work_dists,
+                            d_work_deg, 0, N, s);
     if (!rc && reverse_edges_out)
     {
         uint32_t tot = 0;

@@ -347,7 +347,7 @@ __global__ void __launch_bounds__(1024) medoid_argmin_kernel(const float *scores
 template <int DT, int CPL>
 __global__ void __launch_bounds__(kBlockThreads) init_graph_kernel(StoreView st, uint32_t R, uint32_t *cur_ids,
                                                                    float *cur_dists, uint32_t *degree, uint32_t v0,
-                                                                   uint32_t v1)
+                                                                   uint32_t v1, uint32_t lrow0)
 {
     const int lane = lane_id();
     const int g = lane >> 3, gl = lane & 7;
@@ -389,7 +389,7 @@ __global__ void __launch_bounds__(kBlockThreads) init_graph_kernel(StoreView st,
                 if (idx < R && gl == 0)
                 {
                     cur_ids[(uint64_t)v * R + idx] = nb[u];
-                    cur_dists[(uint64_t)v * R + idx] = nb[u] != kInvalid ? d : FLT_MAX;
+                    cur_dists[(uint64_t)(v - lrow0) * R + idx] = nb[u] != kInvalid ? d : FLT_MAX;
                 }
             }
         }
@@ -413,6 +413,7 @@ struct SearchParams
     uint32_t *exp_count;
     uint32_t exp_stride;
     uint32_t v0, v1;
+    uint32_t lrow0; // first vertex of the per-rank arrays (own distance rows, expansion lists)
     unsigned long long *counters; // [0] distance evaluations, [1] expansions
 };
 
@@ -462,7 +463,7 @@ __global__ void __launch_bounds__(kBlockThreads) search_kernel(SearchParams p)
             {
                 a0 = p.cur_ids[(uint64_t)v * p.R + i0];
                 if (a0 < N && a0 != v)
-                    f0 = p.cur_dists[(uint64_t)v * p.R + i0];
+                    f0 = p.cur_dists[(uint64_t)(v - p.lrow0) * p.R + i0];
                 else
                     a0 = kInvalid;
             }
@@ -470,7 +471,7 @@ __global__ void __launch_bounds__(kBlockThreads) search_kernel(SearchParams p)
             {
                 a1 = p.cur_ids[(uint64_t)v * p.R + i1];
                 if (a1 < N && a1 != v)
-                    f1 = p.cur_dists[(uint64_t)v * p.R + i1];
+                    f1 = p.cur_dists[(uint64_t)(v - p.lrow0) * p.R + i1];
                 else
                     a1 = kInvalid;
             }
@@ -488,8 +489,8 @@ __global__ void __launch_bounds__(kBlockThreads) search_kernel(SearchParams p)
             if (lane == 0)
             {
                 sm.pf(ps.cur)[sel] = 1;
-                p.exp_ids[(uint64_t)v * p.exp_stride + step] = x;
-                p.exp_dists[(uint64_t)v * p.exp_stride + step] = key_dist(key);
+                p.exp_ids[(uint64_t)(v - p.lrow0) * p.exp_stride + step] = x;
+                p.exp_dists[(uint64_t)(v - p.lrow0) * p.exp_stride + step] = key_dist(key);
             }
             __syncwarp();
             ++nexp;
@@ -508,7 +509,7 @@ __global__ void __launch_bounds__(kBlockThreads) search_kernel(SearchParams p)
             }
         }
         if (lane == 0)
-            p.exp_count[v] = nexp;
+            p.exp_count[v - p.lrow0] = nexp;
         expansions += nexp;
     }
     if (lane == 0 && p.counters)
@@ -599,6 +600,7 @@ struct ReplayParams
     float *work_dists;
     uint32_t *work_deg;
     uint32_t v0, v1;
+    uint32_t lrow0;       // first vertex of the per-rank arrays
     uint32_t row_bytes;   // nchunks * 16
     uint32_t cache_rows;  // R + exp_stride
     uint32_t per_warp;    // smem bytes per warp
@@ -665,7 +667,7 @@ __global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
                 nb = p.cur_ids[(uint64_t)v * p.R + i];
                 if (nb < N && nb != v)
                 {
-                    d = p.cur_dists[(uint64_t)v * p.R + i];
+                    d = p.cur_dists[(uint64_t)(v - p.lrow0) * p.R + i];
                     u = (uint16_t)i;
                 }
                 else
@@ -675,7 +677,8 @@ __global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
             wd[i] = d;
             wu[i] = u;
         }
-        const uint32_t cnt = min(p.exp_count[v], p.exp_stride);
+        const uint64_t lv = v - p.lrow0;
+        const uint32_t cnt = min(p.exp_count[lv], p.exp_stride);
         for (uint32_t i = lane; i < p.R + cnt; i += 32)
         {
             uint32_t id;
@@ -687,7 +690,7 @@ __global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
             }
             else
             {
-                id = p.exp_ids[(uint64_t)v * p.exp_stride + (i - p.R)];
+                id = p.exp_ids[lv * p.exp_stride + (i - p.R)];
                 if (id >= N)
                     id = v;
             }
@@ -703,8 +706,8 @@ __global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
 
         for (uint32_t k = 0; k < cnt; ++k)
         {
-            const uint32_t x = p.exp_ids[(uint64_t)v * p.exp_stride + k];
-            const float dx = p.exp_dists[(uint64_t)v * p.exp_stride + k];
+            const uint32_t x = p.exp_ids[lv * p.exp_stride + k];
+            const float dx = p.exp_dists[lv * p.exp_stride + k];
             if (x >= N || x == v)
                 continue;
             const uint32_t deg = min(wdeg, C);
@@ -853,11 +856,11 @@ __global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
         }
         for (uint32_t i = lane; i < C; i += 32)
         {
-            p.work_ids[(uint64_t)v * C + i] = wid[i];
-            p.work_dists[(uint64_t)v * C + i] = wd[i];
+            p.work_ids[lv * C + i] = wid[i];
+            p.work_dists[lv * C + i] = wd[i];
         }
         if (lane == 0)
-            p.work_deg[v] = wdeg;
+            p.work_deg[lv] = wdeg;
         __syncwarp();
     }
     if (lane == 0 && p.counters)
@@ -865,9 +868,11 @@ __global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
 }
 
 // ====================================================================== reverse CSR
-// Sources are all rows [s0, s1) of the work graph (first min(deg, R) slots).
-__global__ void rev_count_kernel(const uint32_t *work_ids, const uint32_t *work_deg, uint32_t N, uint32_t R,
-                                 uint32_t C, uint32_t s0, uint32_t s1, uint32_t *cnt)
+// Reverse edges: source rows [s0, s1) of an edge table (row stride
+// src_stride, first min(src_deg, R) slots), kept when the target lies in
+// [t0, t1); counts and cursors are indexed by target - t0.
+__global__ void rev_count_kernel(const uint32_t *src_ids, uint64_t src_stride, const uint32_t *src_deg, uint32_t N,
+                                 uint32_t R, uint32_t s0, uint32_t s1, uint32_t t0, uint32_t t1, uint32_t *cnt)
 {
     const uint64_t total = (uint64_t)(s1 - s0) * R;
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total;
@@ -875,17 +880,18 @@ __global__ void rev_count_kernel(const uint32_t *work_ids, const uint32_t *work_
     {
         const uint32_t src = s0 + (uint32_t)(i / R);
         const uint32_t slot = (uint32_t)(i % R);
-        if (slot < min(work_deg[src], R))
+        if (slot < min(src_deg[src - s0], R))
         {
-            const uint32_t t = work_ids[(uint64_t)src * C + slot];
-            if (t < N && t != src)
-                atomicAdd(&cnt[t], 1u);
+            const uint32_t t = src_ids[(uint64_t)(src - s0) * src_stride + slot];
+            if (t < N && t != src && t >= t0 && t < t1)
+                atomicAdd(&cnt[t - t0], 1u);
         }
     }
 }
 
-__global__ void rev_fill_kernel(const uint32_t *work_ids, const uint32_t *work_deg, uint32_t N, uint32_t R,
-                                uint32_t C, uint32_t s0, uint32_t s1, uint32_t *cursor, uint32_t *rev)
+__global__ void rev_fill_kernel(const uint32_t *src_ids, uint64_t src_stride, const uint32_t *src_deg, uint32_t N,
+                                uint32_t R, uint32_t s0, uint32_t s1, uint32_t t0, uint32_t t1, uint32_t *cursor,
+                                uint32_t *rev)
 {
     const uint64_t total = (uint64_t)(s1 - s0) * R;
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total;
@@ -893,12 +899,29 @@ __global__ void rev_fill_kernel(const uint32_t *work_ids, const uint32_t *work_d
     {
         const uint32_t src = s0 + (uint32_t)(i / R);
         const uint32_t slot = (uint32_t)(i % R);
-        if (slot < min(work_deg[src], R))
+        if (slot < min(src_deg[src - s0], R))
         {
-            const uint32_t t = work_ids[(uint64_t)src * C + slot];
-            if (t < N && t != src)
-                rev[atomicAdd(&cursor[t], 1u)] = src;
+            const uint32_t t = src_ids[(uint64_t)(src - s0) * src_stride + slot];
+            if (t < N && t != src && t >= t0 && t < t1)
+                rev[atomicAdd(&cursor[t - t0], 1u)] = src;
         }
+    }
+}
+
+// Copies the first R slots of the local work rows (and their degrees) into
+// rows [v0, v1) of an R-wide edge table, for the all-gather of edge deltas.
+__global__ void pack_work_rows_kernel(const uint32_t *work_ids, const uint32_t *work_deg, uint32_t C, uint32_t R,
+                                      uint32_t v0, uint32_t v1, uint32_t *table, uint32_t *table_deg)
+{
+    const uint64_t total = (uint64_t)(v1 - v0) * R;
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < total;
+         i += (uint64_t)gridDim.x * blockDim.x)
+    {
+        const uint64_t lv = i / R;
+        const uint32_t slot = (uint32_t)(i % R);
+        table[(v0 + lv) * R + slot] = work_ids[lv * C + slot];
+        if (slot == 0)
+            table_deg[v0 + lv] = work_deg[lv];
     }
 }
 
@@ -1016,7 +1039,11 @@ struct MergeParams
     uint32_t heavy_cap, heavy_threshold, heavy_sample;
     uint32_t *heavy_list;
     uint32_t *heavy_count;
-    uint32_t t0, t1;
+    uint32_t *huge_list;
+    uint32_t *huge_count;
+    uint32_t *huge_scratch; // (N+1)/2 words of 16-bit counters per huge-kernel block, all zero
+    uint32_t Cp;            // next_pow2(C), >= 32
+    uint32_t t0, t1;    // targets handled; offsets[] and the work rows are indexed by t - t0
     uint32_t sort_cap;  // light kernel: segments up to this length
     uint32_t per_warp;  // light kernel smem bytes per warp
     unsigned long long *counters; // [3] reverse distance evaluations
@@ -1025,30 +1052,121 @@ struct MergeParams
 constexpr uint32_t kMergeSortCap = 512;
 constexpr uint32_t kHeavySortCap = 16384;
 
-__host__ __device__ __forceinline__ uint32_t merge_smem_per_warp(uint32_t C, uint32_t sort_cap)
+__host__ __device__ __forceinline__ uint32_t merge_smem_per_warp(uint32_t C, uint32_t Cp, uint32_t sort_cap)
 {
-    return align16(4u * sort_cap) + align16(4u * C) + align16(4u * C) + 256u + 256u;
+    return align16(4u * sort_cap) + align16(4u * C) + align16(4u * C) + align16(4u * Cp) + 256u + 256u;
 }
 
-// Reference reverse merge of target t over the sorted source list
-// srcs[0..n) (ascending, duplicates adjacent), executed by one warp.  The
-// row lives in wid/wd (C entries); nl/nd are 64-entry scratch.
-template <int DT, int CPL>
-__device__ void merge_sorted_sources(const MergeParams &p, uint32_t t, const uint32_t *srcs, uint32_t n, uint32_t *wid,
-                                     float *wd, uint32_t *nl, float *nd, int lane, unsigned long long &evals)
+// ---------------------------------------------------------------- merge core
+// The reference merge (src/gpu_vamana_vnew2.cu:1722-1814) walks a target's
+// reverse sources in order: a source already in the row is skipped, the
+// others are appended while the row has fewer than C entries, then each
+// replaces the worst entry (largest distance, lowest slot on ties) when it is
+// strictly closer.  Here the sources are in ascending id order.  A source
+// that was in the row as the search left it, or repeats the previous source,
+// is a no-op in that loop (present, or evicted earlier as the worst and so
+// not closer than the current worst), so the "new" sources are filtered in
+// parallel first; the sequential part then only compares each new source's
+// distance with the cached worst and recomputes the worst after a
+// replacement.
+
+struct MergeState
 {
-    const uint32_t N = p.st.N;
-    const uint32_t C = p.C;
-    const int gl = lane & 7;
+    uint32_t deg; // entries in the row (warp-uniform)
+    float wv;     // current worst distance, valid when ws >= 0
+    int ws;       // its slot, -1 = not computed yet
+};
+
+__device__ __forceinline__ void merge_recompute_worst(const float *wd, uint32_t C, MergeState &ms, int lane)
+{
+    float w = -FLT_MAX;
+    int s = -1;
     for (uint32_t i = lane; i < C; i += 32)
+        if (wd[i] > w)
+        {
+            w = wd[i];
+            s = (int)i;
+        }
+    warp_argmax_lowslot(w, s);
+    ms.wv = w;
+    ms.ws = s;
+}
+
+// Applies m new sources (nl/nd, ascending source order) to the row; one warp.
+__device__ __forceinline__ void merge_apply(uint32_t *wid, float *wd, uint32_t C, const uint32_t *nl, const float *nd,
+                                            int m, MergeState &ms, int lane)
+{
+    int j = 0;
+    if (ms.deg < C)
     {
-        wid[i] = p.work_ids[(uint64_t)t * C + i];
-        wd[i] = p.work_dists[(uint64_t)t * C + i];
+        const int take = min(m, (int)(C - ms.deg));
+        for (int k = lane; k < take; k += 32)
+        {
+            wid[ms.deg + k] = nl[k];
+            wd[ms.deg + k] = nd[k];
+        }
+        ms.deg += (uint32_t)take;
+        j = take;
+        __syncwarp();
     }
-    const uint32_t deg0 = min(p.work_deg[t], C);
-    __syncwarp();
-    uint32_t count = n;
-    bool sampled = false;
+    if (j >= m)
+        return;
+    if (ms.ws < 0)
+        merge_recompute_worst(wd, C, ms, lane);
+    while (j < m)
+    {
+        int k = -1;
+        for (int b = j; b < m; b += 32)
+        {
+            const int idx = b + lane;
+            const unsigned hit = __ballot_sync(kFull, idx < m && nd[idx] < ms.wv);
+            if (hit)
+            {
+                k = b + __ffs(hit) - 1;
+                break;
+            }
+        }
+        if (k < 0)
+            break;
+        if (ms.ws < 0)
+            break; // no slot (C == 0 cannot happen; kept for safety)
+        if (lane == 0)
+        {
+            wid[ms.ws] = nl[k];
+            wd[ms.ws] = nd[k];
+        }
+        __syncwarp();
+        merge_recompute_worst(wd, C, ms, lane);
+        j = k + 1;
+    }
+}
+
+// Binary search in the sorted initial row ids.
+__device__ __forceinline__ bool sorted_contains(const uint32_t *a, int n, uint32_t x)
+{
+    int lo = 0, hi = n;
+    while (lo < hi)
+    {
+        const int mid = (lo + hi) >> 1;
+        if (a[mid] < x)
+            lo = mid + 1;
+        else
+            hi = mid;
+    }
+    return lo < n && a[lo] == x;
+}
+
+// Position in the (optionally heavy-cap sampled) processing list -> index
+// into the sorted source array (reference :1743-1760).
+__device__ __forceinline__ uint32_t merge_list_index(uint32_t k, uint32_t n, uint32_t count, bool sampled)
+{
+    return sampled ? (uint32_t)(((uint64_t)k * n) / count) : k;
+}
+
+__device__ __forceinline__ void merge_list_size(const MergeParams &p, uint32_t n, uint32_t &count, bool &sampled)
+{
+    count = n;
+    sampled = false;
     if (p.heavy_cap && n > p.heavy_threshold)
     {
         count = min(p.heavy_sample, n);
@@ -1056,13 +1174,71 @@ __device__ void merge_sorted_sources(const MergeParams &p, uint32_t t, const uin
             count = 1;
         sampled = count < n;
     }
+}
+
+__device__ __forceinline__ bool merge_is_new(const MergeParams &p, uint32_t t, const uint32_t *srcs, uint32_t n,
+                                             uint32_t count, bool sampled, uint32_t k, const uint32_t *rsorted,
+                                             int deg0, uint32_t &s)
+{
+    s = srcs[merge_list_index(k, n, count, sampled)];
+    if (s >= p.st.N || s == t)
+        return false;
+    if (k > 0 && srcs[merge_list_index(k - 1, n, count, sampled)] == s)
+        return false;
+    return !sorted_contains(rsorted, deg0, s);
+}
+
+// Loads the row of target t into smem (wid/wd) plus a sorted copy of its
+// first deg0 ids (rsorted, Cp >= C entries); one warp.
+__device__ __forceinline__ uint32_t merge_load_row(const MergeParams &p, uint32_t t, uint32_t *wid, float *wd,
+                                                   uint32_t *rsorted, uint32_t Cp, int lane)
+{
+    const uint32_t C = p.C;
+    const uint64_t lt = t - p.t0;
+    const uint32_t deg0 = min(p.work_deg[lt], C);
+    for (uint32_t i = lane; i < Cp; i += 32)
+    {
+        if (i < C)
+        {
+            wid[i] = p.work_ids[lt * C + i];
+            wd[i] = p.work_dists[lt * C + i];
+        }
+        rsorted[i] = i < deg0 ? p.work_ids[lt * C + i] : kInvalid;
+    }
+    __syncwarp();
+    warp_sort_smem_u32(rsorted, (int)Cp, lane);
+    return deg0;
+}
+
+__device__ __forceinline__ void merge_store_row(const MergeParams &p, uint32_t t, const uint32_t *wid, const float *wd,
+                                                uint32_t deg, int lane)
+{
+    const uint32_t C = p.C;
+    const uint64_t lt = t - p.t0;
+    for (uint32_t i = lane; i < C; i += 32)
+    {
+        p.work_ids[lt * C + i] = wid[i];
+        p.work_dists[lt * C + i] = wd[i];
+    }
+    if (lane == 0)
+        p.work_deg[lt] = deg;
+    __syncwarp();
+}
+
+// Whole merge of one target by one warp (sources sorted in srcs[0..n)).
+template <int DT, int CPL>
+__device__ void merge_target_warp(const MergeParams &p, uint32_t t, const uint32_t *srcs, uint32_t n, uint32_t *wid,
+                                  float *wd, uint32_t *rsorted, uint32_t *nl, float *nd, int lane,
+                                  unsigned long long &evals)
+{
+    const int gl = lane & 7;
+    const uint32_t deg0 = merge_load_row(p, t, wid, wd, rsorted, p.Cp, lane);
+    uint32_t count;
+    bool sampled;
+    merge_list_size(p, n, count, sampled);
     uint4 q[CPL];
     load_frag<CPL>(q, p.st.data + (uint64_t)t * p.st.stride, p.st.nchunks, gl);
-    uint32_t deg = deg0;
-    // New sources: valid, not the target, not in the row as the search left
-    // it, and not a repeat of the previous source.  Any other source is a
-    // no-op in the reference loop (present in the row, or evicted earlier as
-    // the worst, hence not closer than the current worst).
+    MergeState ms{deg0, -FLT_MAX, -1};
     for (uint32_t b = 0; b < count; b += 64)
     {
         int m = 0;
@@ -1070,29 +1246,8 @@ __device__ void merge_sorted_sources(const MergeParams &p, uint32_t t, const uin
         for (int h = 0; h < 2; ++h)
         {
             const uint32_t k = b + h * 32 + lane;
-            bool keep = false;
             uint32_t s = kInvalid;
-            if (k < count)
-            {
-                const uint32_t i = sampled ? (uint32_t)(((uint64_t)k * n) / count) : k;
-                s = srcs[i];
-                keep = s < N && s != t;
-                if (keep && k > 0)
-                {
-                    const uint32_t ip = sampled ? (uint32_t)(((uint64_t)(k - 1) * n) / count) : k - 1;
-                    if (srcs[ip] == s)
-                        keep = false;
-                }
-                if (keep)
-                {
-                    for (uint32_t j = 0; j < deg0; ++j)
-                        if (wid[j] == s)
-                        {
-                            keep = false;
-                            break;
-                        }
-                }
-            }
+            const bool keep = k < count && merge_is_new(p, t, srcs, n, count, sampled, k, rsorted, (int)deg0, s);
             const unsigned bm = __ballot_sync(kFull, keep);
             if (keep)
                 nl[m + __popc(bm & ((1u << lane) - 1u))] = s;
@@ -1104,47 +1259,102 @@ __device__ void merge_sorted_sources(const MergeParams &p, uint32_t t, const uin
         eval_candidates<DT, CPL>(p.st.data, p.st.stride, p.st.nchunks, q, nl, nd, m, lane);
         __syncwarp();
         evals += (lane == 0) ? (unsigned long long)m : 0ull;
-        for (int j = 0; j < m; ++j)
+        merge_apply(wid, wd, p.C, nl, nd, m, ms, lane);
+    }
+    merge_store_row(p, t, wid, wd, ms.deg, lane);
+}
+
+// Whole merge of one target by a block of kMergeBlock threads: the filter
+// and the distance evaluations of each chunk of kMergeChunk sources are
+// spread over all warps, warp 0 applies them in order.
+constexpr int kMergeBlock = 256;
+constexpr int kMergeChunk = 1024;
+
+template <int DT, int CPL>
+__device__ void merge_target_block(const MergeParams &p, uint32_t t, const uint32_t *srcs, uint32_t n, uint32_t *wid,
+                                   float *wd, uint32_t *rsorted, uint32_t *nl, float *nd, int *wcount,
+                                   MergeState &ms, unsigned long long &evals)
+{
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    constexpr int W = kMergeBlock / 32;
+    constexpr int PER_WARP = kMergeChunk / W;
+    const int gl = lane & 7;
+    uint32_t deg0 = 0;
+    if (w == 0)
+    {
+        deg0 = merge_load_row(p, t, wid, wd, rsorted, p.Cp, lane);
+        if (lane == 0)
         {
-            const uint32_t s = nl[j];
-            const float d = nd[j];
-            if (deg < C)
-            {
-                if (lane == 0)
-                {
-                    wid[deg] = s;
-                    wd[deg] = d;
-                }
-                ++deg;
-            }
-            else
-            {
-                float w = -FLT_MAX;
-                int ws = -1;
-                for (uint32_t i = lane; i < C; i += 32)
-                    if (wd[i] > w)
-                    {
-                        w = wd[i];
-                        ws = (int)i;
-                    }
-                warp_argmax_lowslot(w, ws);
-                if (lane == 0 && ws >= 0 && d < w)
-                {
-                    wid[ws] = s;
-                    wd[ws] = d;
-                }
-            }
-            __syncwarp();
+            ms.deg = deg0;
+            ms.ws = -1;
+            ms.wv = -FLT_MAX;
         }
     }
-    for (uint32_t i = lane; i < C; i += 32)
+    __syncthreads();
+    deg0 = ms.deg;
+    uint32_t count;
+    bool sampled;
+    merge_list_size(p, n, count, sampled);
+    uint4 q[CPL];
+    load_frag<CPL>(q, p.st.data + (uint64_t)t * p.st.stride, p.st.nchunks, gl);
+    for (uint32_t b = 0; b < count; b += kMergeChunk)
     {
-        p.work_ids[(uint64_t)t * C + i] = wid[i];
-        p.work_dists[(uint64_t)t * C + i] = wd[i];
+        // filter: warp w takes positions [b + w*PER_WARP, b + (w+1)*PER_WARP)
+        int m = 0;
+        uint32_t mine[PER_WARP / 32];
+#pragma unroll
+        for (int h = 0; h < PER_WARP / 32; ++h)
+        {
+            const uint32_t k = b + w * PER_WARP + h * 32 + lane;
+            uint32_t s = kInvalid;
+            const bool keep = k < count && merge_is_new(p, t, srcs, n, count, sampled, k, rsorted, (int)deg0, s);
+            mine[h] = keep ? s : kInvalid;
+            m += __popc(__ballot_sync(kFull, keep));
+        }
+        if (lane == 0)
+            wcount[w] = m;
+        __syncthreads();
+        int off = 0, total = 0;
+        for (int i = 0; i < W; ++i)
+        {
+            if (i < w)
+                off += wcount[i];
+            total += wcount[i];
+        }
+#pragma unroll
+        for (int h = 0; h < PER_WARP / 32; ++h)
+        {
+            const bool keep = mine[h] != kInvalid;
+            const unsigned bm = __ballot_sync(kFull, keep);
+            if (keep)
+                nl[off + __popc(bm & ((1u << lane) - 1u))] = mine[h];
+            off += __popc(bm);
+        }
+        __syncthreads();
+        if (total == 0)
+            continue;
+        // distances: warp w evaluates entries [w*ceil, ...)
+        const int per = (total + W - 1) / W;
+        const int e0 = min(total, w * per), e1 = min(total, e0 + per);
+        if (e1 > e0)
+            eval_candidates<DT, CPL>(p.st.data, p.st.stride, p.st.nchunks, q, nl + e0, nd + e0, e1 - e0, lane);
+        else
+            eval_candidates<DT, CPL>(p.st.data, p.st.stride, p.st.nchunks, q, nl, nd, 0, lane);
+        __syncthreads();
+        if (threadIdx.x == 0)
+            evals += (unsigned long long)total;
+        if (w == 0)
+        {
+            MergeState st = ms;
+            merge_apply(wid, wd, p.C, nl, nd, total, st, lane);
+            if (lane == 0)
+                ms = st;
+        }
+        __syncthreads();
     }
-    if (lane == 0)
-        p.work_deg[t] = deg;
-    __syncwarp();
+    if (w == 0)
+        merge_store_row(p, t, wid, wd, ms.deg, lane);
+    __syncthreads();
 }
 
 template <int DT, int CPL>
@@ -1159,6 +1369,8 @@ __global__ void __launch_bounds__(kBlockThreads) merge_kernel(MergeParams p)
     b += align16(4u * p.C);
     float *wd = reinterpret_cast<float *>(b);
     b += align16(4u * p.C);
+    uint32_t *rsorted = reinterpret_cast<uint32_t *>(b);
+    b += align16(4u * p.Cp);
     uint32_t *nl = reinterpret_cast<uint32_t *>(b);
     b += 256;
     float *nd = reinterpret_cast<float *>(b);
@@ -1166,7 +1378,7 @@ __global__ void __launch_bounds__(kBlockThreads) merge_kernel(MergeParams p)
     for (uint32_t t = p.t0 + blockIdx.x * kWarpsPerBlock + warp_id_in_block(); t < p.t1;
          t += gridDim.x * kWarpsPerBlock)
     {
-        const uint32_t beg = p.offsets[t], end = p.offsets[t + 1];
+        const uint32_t beg = p.offsets[t - p.t0], end = p.offsets[t - p.t0 + 1];
         const uint32_t n = end - beg;
         if (n == 0)
             continue;
@@ -1181,87 +1393,143 @@ __global__ void __launch_bounds__(kBlockThreads) merge_kernel(MergeParams p)
             buf[i] = (uint32_t)i < n ? p.rev[beg + i] : kInvalid;
         __syncwarp();
         warp_sort_smem_u32(buf, n2, lane);
-        merge_sorted_sources<DT, CPL>(p, t, buf, n, wid, wd, nl, nd, lane, evals);
+        merge_target_warp<DT, CPL>(p, t, buf, n, wid, wd, rsorted, nl, nd, lane, evals);
     }
     if (lane == 0 && p.counters)
         atomicAdd(&p.counters[3], evals);
 }
 
-// Heavy targets (more than sort_cap sources): one block per target, sorted
-// in shared memory by the whole block when they fit kHeavySortCap, else
-// sorted in place in global memory by the block (rare: in-degree > 16384).
+__host__ __device__ __forceinline__ uint32_t block_merge_smem_bytes(uint32_t C, uint32_t Cp)
+{
+    return align16(4u * C) * 2 + align16(4u * Cp) + 8u * kMergeChunk + 64u + 32u;
+}
+
+// Carves the block-merge scratch after the sort buffer.
+struct BlockMergeSmem
+{
+    uint32_t *wid, *rsorted, *nl;
+    float *wd, *nd;
+    int *wcount;
+    MergeState *ms;
+};
+
+__device__ __forceinline__ BlockMergeSmem carve_block_merge(uint8_t *b, uint32_t C, uint32_t Cp)
+{
+    BlockMergeSmem m;
+    m.wid = reinterpret_cast<uint32_t *>(b);
+    b += align16(4u * C);
+    m.wd = reinterpret_cast<float *>(b);
+    b += align16(4u * C);
+    m.rsorted = reinterpret_cast<uint32_t *>(b);
+    b += align16(4u * Cp);
+    m.nl = reinterpret_cast<uint32_t *>(b);
+    b += 4u * kMergeChunk;
+    m.nd = reinterpret_cast<float *>(b);
+    b += 4u * kMergeChunk;
+    m.wcount = reinterpret_cast<int *>(b);
+    b += 64u;
+    m.ms = reinterpret_cast<MergeState *>(b);
+    return m;
+}
+
+// Heavy targets (sort_cap < n <= kHeavySortCap sources): one block per
+// target, sources sorted in shared memory by the whole block.  Longer
+// segments are handed to huge_merge_kernel.
 template <int DT, int CPL>
-__global__ void __launch_bounds__(256) heavy_merge_kernel(MergeParams p)
+__global__ void __launch_bounds__(kMergeBlock) heavy_merge_kernel(MergeParams p)
 {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     uint32_t *sbuf = reinterpret_cast<uint32_t *>(smem_raw);
-    uint8_t *b = smem_raw + 4u * kHeavySortCap;
-    uint32_t *wid = reinterpret_cast<uint32_t *>(b);
-    b += align16(4u * p.C);
-    float *wd = reinterpret_cast<float *>(b);
-    b += align16(4u * p.C);
-    uint32_t *nl = reinterpret_cast<uint32_t *>(b);
-    b += 256;
-    float *nd = reinterpret_cast<float *>(b);
-    const int lane = threadIdx.x & 31;
+    BlockMergeSmem sm = carve_block_merge(smem_raw + 4u * kHeavySortCap, p.C, p.Cp);
     const uint32_t nheavy = *p.heavy_count;
     unsigned long long evals = 0;
     for (uint32_t h = blockIdx.x; h < nheavy; h += gridDim.x)
     {
         const uint32_t t = p.heavy_list[h];
-        const uint32_t beg = p.offsets[t], end = p.offsets[t + 1];
+        const uint32_t beg = p.offsets[t - p.t0], end = p.offsets[t - p.t0 + 1];
         const uint32_t n = end - beg;
-        const uint32_t *sorted;
-        if (n <= kHeavySortCap)
+        if (n > kHeavySortCap)
         {
-            const uint32_t n2 = (uint32_t)next_pow2((int)n);
-            for (uint32_t i = threadIdx.x; i < n2; i += blockDim.x)
-                sbuf[i] = i < n ? p.rev[beg + i] : kInvalid;
-            __syncthreads();
-            for (uint32_t size = 2; size <= n2; size <<= 1)
-                for (uint32_t j = size >> 1; j > 0; j >>= 1)
-                {
-                    for (uint32_t i = threadIdx.x; i < n2; i += blockDim.x)
-                    {
-                        const uint32_t l = i ^ j;
-                        if (l > i)
-                        {
-                            const uint32_t x = sbuf[i], y = sbuf[l];
-                            const bool asc = (i & size) == 0;
-                            if (asc ? (x > y) : (x < y))
-                            {
-                                sbuf[i] = y;
-                                sbuf[l] = x;
-                            }
-                        }
-                    }
-                    __syncthreads();
-                }
-            sorted = sbuf;
+            if (threadIdx.x == 0)
+                p.huge_list[atomicAdd(p.huge_count, 1u)] = t;
+            continue;
         }
-        else
-        {
-            // Odd-even transposition sort in place: n rounds, each a
-            // parallel compare-exchange of disjoint neighbours.
-            uint32_t *a = p.rev + beg;
-            for (uint32_t r = 0; r < n; ++r)
+        const uint32_t n2 = (uint32_t)next_pow2((int)n);
+        for (uint32_t i = threadIdx.x; i < n2; i += blockDim.x)
+            sbuf[i] = i < n ? p.rev[beg + i] : kInvalid;
+        __syncthreads();
+        for (uint32_t size = 2; size <= n2; size <<= 1)
+            for (uint32_t j = size >> 1; j > 0; j >>= 1)
             {
-                for (uint32_t i = 2 * threadIdx.x + (r & 1u); i + 1 < n; i += 2 * blockDim.x)
+                for (uint32_t i = threadIdx.x; i < n2; i += blockDim.x)
                 {
-                    const uint32_t x = a[i], y = a[i + 1];
-                    if (x > y)
+                    const uint32_t l = i ^ j;
+                    if (l > i)
                     {
-                        a[i] = y;
-                        a[i + 1] = x;
+                        const uint32_t x = sbuf[i], y = sbuf[l];
+                        const bool asc = (i & size) == 0;
+                        if (asc ? (x > y) : (x < y))
+                        {
+                            sbuf[i] = y;
+                            sbuf[l] = x;
+                        }
                     }
                 }
                 __syncthreads();
             }
-            sorted = a;
+        merge_target_block<DT, CPL>(p, t, sbuf, n, sm.wid, sm.wd, sm.rsorted, sm.nl, sm.nd, sm.wcount, *sm.ms,
+                                    evals);
+    }
+    if (threadIdx.x == 0 && p.counters)
+        atomicAdd(&p.counters[3], evals);
+}
+
+// Huge targets (more than kHeavySortCap sources, e.g. the medoid in the
+// first round, which enters almost every row): the segment is put in
+// ascending order in place by a counting sort over source ids, with 16-bit
+// counters in this block's slice of huge_scratch (kept all-zero between
+// uses), then merged by the block.
+template <int DT, int CPL>
+__global__ void __launch_bounds__(kMergeBlock) huge_merge_kernel(MergeParams p)
+{
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    __shared__ uint32_t s_warp[32];
+    BlockMergeSmem sm = carve_block_merge(smem_raw, p.C, p.Cp);
+    const uint32_t nhuge = *p.huge_count;
+    const uint32_t words = (p.st.N + 1u) / 2u;
+    uint32_t *cnt = p.huge_scratch + (uint64_t)blockIdx.x * words;
+    unsigned long long evals = 0;
+    for (uint32_t h = blockIdx.x; h < nhuge; h += gridDim.x)
+    {
+        const uint32_t t = p.huge_list[h];
+        const uint32_t beg = p.offsets[t - p.t0], end = p.offsets[t - p.t0 + 1];
+        const uint32_t n = end - beg;
+        uint32_t *seg = p.rev + beg;
+        for (uint32_t i = threadIdx.x; i < n; i += blockDim.x)
+        {
+            const uint32_t s = seg[i];
+            atomicAdd(&cnt[s >> 1], 1u << ((s & 1u) * 16u));
         }
-        if (threadIdx.x < 32)
-            merge_sorted_sources<DT, CPL>(p, t, sorted, n, wid, wd, nl, nd, lane, evals);
         __syncthreads();
+        uint32_t base = 0;
+        for (uint32_t w0 = 0; w0 < words; w0 += blockDim.x)
+        {
+            const uint32_t wi = w0 + threadIdx.x;
+            const uint32_t v = wi < words ? cnt[wi] : 0u;
+            const uint32_t c0 = v & 0xFFFFu, c1 = v >> 16;
+            uint32_t total;
+            const uint32_t ex = block_exclusive_scan(c0 + c1, s_warp, total) + base;
+            for (uint32_t r = 0; r < c0; ++r)
+                seg[ex + r] = 2u * wi;
+            for (uint32_t r = 0; r < c1; ++r)
+                seg[ex + c0 + r] = 2u * wi + 1u;
+            if (v)
+                cnt[wi] = 0u;
+            base += total;
+            __syncthreads();
+        }
+        __syncthreads();
+        merge_target_block<DT, CPL>(p, t, seg, n, sm.wid, sm.wd, sm.rsorted, sm.nl, sm.nd, sm.wcount, *sm.ms, evals);
     }
     if (threadIdx.x == 0 && p.counters)
         atomicAdd(&p.counters[3], evals);
@@ -1281,6 +1549,7 @@ struct PruneParams
     float *cur_dists;
     uint32_t *degree;
     uint32_t v0, v1;
+    uint32_t lrow0; // first vertex of the per-rank arrays (work rows, own distance rows)
     uint32_t row_bytes;
     uint32_t per_warp;
     unsigned long long *counters; // [4] pair evaluations
@@ -1324,15 +1593,16 @@ __global__ void __launch_bounds__(kBlockThreads) prune_kernel(PruneParams p)
     for (uint32_t v = p.v0 + blockIdx.x * kWarpsPerBlock + warp_id_in_block(); v < p.v1;
          v += gridDim.x * kWarpsPerBlock)
     {
-        const uint32_t deg = min(p.work_deg[v], C);
+        const uint64_t lv = v - p.lrow0;
+        const uint32_t deg = min(p.work_deg[lv], C);
         // Candidates ordered by (distance, slot): the reference's selection order.
         for (uint32_t i = lane; i < p.Cp; i += 32)
         {
             uint64_t key = kKeyMax;
             if (i < deg)
             {
-                const uint32_t id = p.work_ids[(uint64_t)v * C + i];
-                const float d = p.work_dists[(uint64_t)v * C + i];
+                const uint32_t id = p.work_ids[lv * C + i];
+                const float d = p.work_dists[lv * C + i];
                 rid[i] = id;
                 if (id < N && id != v && d < FLT_MAX)
                     key = ((uint64_t)__float_as_uint(d) << 32) | i;
@@ -1454,7 +1724,7 @@ __global__ void __launch_bounds__(kBlockThreads) prune_kernel(PruneParams p)
         for (uint32_t i = lane; i < p.R; i += 32)
         {
             p.cur_ids[(uint64_t)v * p.R + i] = i < out ? oid[i] : kInvalid;
-            p.cur_dists[(uint64_t)v * p.R + i] = i < out ? od[i] : FLT_MAX;
+            p.cur_dists[lv * p.R + i] = i < out ? od[i] : FLT_MAX;
         }
         if (lane == 0)
             p.degree[v] = out;

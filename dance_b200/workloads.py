@@ -96,39 +96,49 @@ def zipf_partition_labels(n: int, num_labels: int = 100, seed: int = 42) -> np.n
     return rng.choice(num_labels, size=n, p=p).astype(np.uint32)
 
 
-def brute_force_knn(base: torch.Tensor, queries: torch.Tensor, k: int = 10, chunk: int = 2048):
-    """Exact top-k by squared L2 (ties broken by id).  uint8 uses exact integer
-    dot products (float32 sums of integers < 2^24); float uses float64."""
+def brute_force_knn(base: torch.Tensor, queries: torch.Tensor, k: int = 10, qchunk: int = 1024,
+                    bchunk: int = 1 << 20):
+    """Exact top-k by squared L2, ties broken by id.  uint8 uses exact integer
+    dot products (float32 sums of integers below 2^24); float uses float64.
+    Tiled over queries and base so the distance tile stays a few GB."""
     dev = base.device
-    if base.dtype == torch.uint8:
-        B = base.to(torch.float32)
-        Q = queries.to(torch.float32)
-        bn = (B * B).sum(1)
-    else:
-        B = base.to(torch.float64)
-        Q = queries.to(torch.float64)
-        bn = (B * B).sum(1)
-    ids = torch.empty((Q.shape[0], k), dtype=torch.int64, device=dev)
-    ds = torch.empty((Q.shape[0], k), dtype=torch.float64, device=dev)
+    exact_f32 = base.dtype == torch.uint8
+    ct = torch.float32 if exact_f32 else torch.float64
+    kk = min(base.shape[0], k + 16)
     prev = None
-    if B.dtype == torch.float32:
+    if dev.type == "cuda":
         prev = torch.backends.cuda.matmul.allow_tf32
         torch.backends.cuda.matmul.allow_tf32 = False
     try:
-        for b in range(0, Q.shape[0], chunk):
-            q = Q[b:b + chunk]
-            d = bn[None, :] - 2.0 * (q @ B.T) + (q * q).sum(1)[:, None]
-            d = d.to(torch.float64)
-            # stable tie-break by id: sort by (dist, id) among a slightly larger candidate set
-            kk = min(B.shape[0], k + 16)
-            vals, idx = torch.topk(d, kk, dim=1, largest=False)
-            order = torch.argsort(vals * 0 + idx.to(torch.float64), dim=1)  # id order
-            vals2 = torch.gather(vals, 1, order)
-            idx2 = torch.gather(idx, 1, order)
-            o2 = torch.argsort(vals2, dim=1, stable=True)
-            ids[b:b + chunk] = torch.gather(idx2, 1, o2)[:, :k]
-            ds[b:b + chunk] = torch.gather(vals2, 1, o2)[:, :k]
+        out_i = torch.empty((queries.shape[0], k), dtype=torch.int64, device=dev)
+        out_d = torch.empty((queries.shape[0], k), dtype=torch.float64, device=dev)
+        for qb in range(0, queries.shape[0], qchunk):
+            q = queries[qb:qb + qchunk].to(ct)
+            qn = (q * q).sum(1)
+            best_d = None
+            best_i = None
+            for bb in range(0, base.shape[0], bchunk):
+                B = base[bb:bb + bchunk].to(ct)
+                d = (B * B).sum(1)[None, :] - 2.0 * (q @ B.T) + qn[:, None]
+                kc = min(kk, B.shape[0])
+                v, i = torch.topk(d, kc, dim=1, largest=False)
+                v = v.to(torch.float64)
+                i = i + bb
+                if best_d is None:
+                    best_d, best_i = v, i
+                else:
+                    cd = torch.cat([best_d, v], 1)
+                    ci = torch.cat([best_i, i], 1)
+                    v2, j = torch.topk(cd, min(kk, cd.shape[1]), dim=1, largest=False)
+                    best_d, best_i = v2, torch.gather(ci, 1, j)
+            # order the candidates by (distance, id)
+            o = torch.argsort(best_i, dim=1)
+            d2 = torch.gather(best_d, 1, o)
+            i2 = torch.gather(best_i, 1, o)
+            o2 = torch.argsort(d2, dim=1, stable=True)
+            out_i[qb:qb + qchunk] = torch.gather(i2, 1, o2)[:, :k]
+            out_d[qb:qb + qchunk] = torch.gather(d2, 1, o2)[:, :k]
+        return out_i, out_d
     finally:
         if prev is not None:
             torch.backends.cuda.matmul.allow_tf32 = prev
-    return ids, ds

@@ -184,9 +184,10 @@ def _gpu_replay(x, R, C, alpha, ids, ds, deg, eids, eds, ecnt):
     wid = torch.zeros((n, C), dtype=torch.int32, device="cuda")
     wd = torch.zeros((n, C), dtype=torch.float32, device="cuda")
     wdeg = torch.zeros(n, dtype=torch.int32, device="cuda")
-    check(lib.dance_stage_replay(dt, P(s), stride, n, x.shape[1], R, C, ctypes.c_float(alpha), P(dev(ids)),
-                                 P(dev(ds)), P(dev(deg)), P(dev(eids)), P(dev(eds)), P(dev(ecnt)), eids.shape[1],
-                                 P(wid), P(wd), P(wdeg), None))
+    keep = [dev(a) for a in (ids, ds, deg, eids, eds, ecnt)]  # alive until the kernels finish
+    check(lib.dance_stage_replay(dt, P(s), stride, n, x.shape[1], R, C, ctypes.c_float(alpha), *map(P, keep[:6]),
+                                 eids.shape[1], P(wid), P(wd), P(wdeg), None))
+    torch.cuda.synchronize()
     return host(wid, np.uint32), host(wd), host(wdeg, np.uint32)
 
 
@@ -271,8 +272,10 @@ def _gpu_prune(x, R, C, alpha, mindeg, wid, wd, wdeg):
     ids = torch.zeros((n, R), dtype=torch.int32, device="cuda")
     ds = torch.zeros((n, R), dtype=torch.float32, device="cuda")
     deg = torch.zeros(n, dtype=torch.int32, device="cuda")
-    check(lib.dance_stage_prune(dt, P(s), stride, n, x.shape[1], R, C, ctypes.c_float(alpha), mindeg, P(dev(wid)),
-                                P(dev(wd)), P(dev(wdeg)), P(ids), P(ds), P(deg), None))
+    keep = [dev(a) for a in (wid, wd, wdeg)]  # alive until the kernel finishes
+    check(lib.dance_stage_prune(dt, P(s), stride, n, x.shape[1], R, C, ctypes.c_float(alpha), mindeg, *map(P, keep),
+                                P(ids), P(ds), P(deg), None))
+    torch.cuda.synchronize()
     return host(ids, np.uint32), host(ds), host(deg, np.uint32)
 
 
@@ -395,7 +398,8 @@ def test_query_search_matches_oracle_and_recall(dtype):
     R, L, C, S = 32, 64, 48, 32
     g, deg, ds, med = _gpu_build(x, R, L, C, S)
     s, stride, dt = store(x)
-    ids, dd = vamana.search_queries(s, x.shape[1], stride, dev(g), R, med, torch.from_numpy(q).cuda(), 100, 10)
+    gdev = dev(g)
+    ids, dd = vamana.search_queries(s, x.shape[1], stride, gdev, R, med, torch.from_numpy(q).cuda(), 100, 10)
     oi, od = oracle.search_queries(x, g, R, med, q, 100, 10)
     assert np.array_equal(host(ids, np.uint32), oi)
     gt, _ = workloads.brute_force_knn(torch.from_numpy(x).cuda(), torch.from_numpy(q).cuda(), 10)
