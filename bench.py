@@ -380,7 +380,130 @@ def reference_gpu(x, store, stride, our_medoid, args):
 
 
 def run_sharded(args):
-    raise SystemExit("multi-GPU build is not available in this build yet")
+    """N > 1: one graph, vertex batches sharded over the ranks (strong scaling);
+    edge deltas exchanged with NCCL all-gathers inside libdance_b200."""
+    import datetime
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import dance_b200
+    from dance_b200 import vamana, workloads
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                            device_id=torch.device("cuda", local))
+    lib = dance_b200.load()
+    n = args.n
+    R, L, C, S = WORKLOAD["R"], WORKLOAD["L"], WORKLOAD["C"], WORKLOAD["STEPS"]
+    x = make_workload("cuda", n)  # the same seeded vectors on every rank
+    store, stride = vamana.padded_store(x)
+    uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+    if rank == 0:
+        uid.copy_(torch.tensor(list(vamana.nccl_unique_id()), dtype=torch.uint8))
+    dist.broadcast(uid, 0)
+    comm = vamana.Comm(rank, world, bytes(uid.cpu().tolist()), timeout_s=600.0)
+    ws = vamana.sharded_workspace(n, world, R, L, C, S)
+    _, _, chunk = vamana.shard_range(n, world, rank)
+    graph = torch.empty((chunk * world, R), dtype=torch.int32, device="cuda")
+    degree = torch.empty((chunk * world,), dtype=torch.int32, device="cuda")
+    tdeg = torch.empty((chunk * world,), dtype=torch.int32, device="cuda")
+    prm = dance_b200.default_params()
+    stream = torch.cuda.Stream()
+
+    def one_build():
+        with torch.cuda.stream(stream):
+            return vamana.build_sharded(comm, store, WORKLOAD["dim"], stride, R, L, C, S, params=prm, workspace=ws,
+                                        graph=graph, degree=degree, table_degree=tdeg, stream=stream)
+
+    for _ in range(args.warmup):
+        one_build()
+    torch.cuda.synchronize()
+    dist.barrier()
+    clocks = ClockSampler(torch.cuda.current_device()) if rank == 0 else None
+    if clocks:
+        clocks.start()
+    launches0 = lib.dance_kernel_launch_count()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    reports = []
+    torch.cuda.synchronize()
+    ev0.record(stream)
+    for _ in range(args.steps):
+        _, _, medoid = one_build()
+        reports.append(dance_b200.last_build_report())
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    launches = lib.dance_kernel_launch_count() - launches0
+    mine = torch.tensor([ev0.elapsed_time(ev1) * 1e-3], dtype=torch.float64, device="cuda")
+    dist.all_reduce(mine, op=dist.ReduceOp.MAX)
+    elapsed = float(mine.item())
+    clk = clocks.stop() if clocks else None
+    # per-rank search-kernel roofline (max kernel time over ranks, summed bytes)
+    alg = sum(search_algorithmic_bytes(r, 0, stride, R, 0) for r in reports)
+    alg += args.steps * WORKLOAD["iters"] * (n // world) * (stride + R * 8 + 8)
+    kt = torch.tensor([sum(r["search_kernel_seconds"] for r in reports), alg], dtype=torch.float64, device="cuda")
+    kmax = kt.clone()
+    dist.all_reduce(kmax, op=dist.ReduceOp.MAX)
+    ksum = kt.clone()
+    dist.all_reduce(ksum, op=dist.ReduceOp.SUM)
+    # e2e: every rank copies the vectors from pinned host memory, builds, rank 0 reads the graph back
+    e2e = None
+    if not args.no_e2e:
+        hx = x.cpu().pin_memory()
+        hg = torch.empty((n, R), dtype=torch.int32).pin_memory()
+        hd = torch.empty((n,), dtype=torch.int32).pin_memory()
+        dx = torch.empty_like(x)
+        torch.cuda.synchronize()
+        dist.barrier()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            dx.copy_(hx, non_blocking=True)
+            st2, _ = vamana.padded_store(dx)
+            torch.cuda.synchronize()
+            vamana.build_sharded(comm, st2, WORKLOAD["dim"], stride, R, L, C, S, params=prm, workspace=ws,
+                                 graph=graph, degree=degree, table_degree=tdeg)
+            if rank == 0:
+                hg.copy_(graph[:n])
+                hd.copy_(degree[:n])
+            torch.cuda.synchronize()
+        dt = torch.tensor([time.perf_counter() - t0], dtype=torch.float64, device="cuda")
+        dist.all_reduce(dt, op=dist.ReduceOp.MAX)
+        e2e = {"value": n * args.steps / float(dt.item()), "unit": "vectors/s",
+               "h2d_bytes_per_step": int(hx.numel()) * world, "d2h_bytes_per_step": int(hg.numel() * 4 + hd.numel() * 4),
+               "api": "dance_vamana_build_sharded (C ABI) on every rank; vectors copied from pinned host memory "
+                      "on every rank, graph read back on rank 0; wall clock, max over ranks",
+               "warmup": 0}
+    rec = None
+    if rank == 0 and not args.no_recall:
+        q = make_queries("cuda")
+        gt, _ = workloads.brute_force_knn(x, q, 10)
+        ids, _ = vamana.search_queries(store, WORKLOAD["dim"], stride, graph, R, medoid, q, 100, 10)
+        rec = vamana.recall_at_k(ids.cpu().numpy(), gt.cpu().numpy())
+    if rank == 0:
+        peak, peak_kind = measured_peaks()
+        achieved = float(ksum[1].item()) / float(kmax[0].item()) / 1e9
+        line = {
+            "metric": "vamana_build_vectors_per_s", "value": n * args.steps / elapsed, "unit": "vectors/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8",
+            "data": "synthetic (seeded GPU generator, BASELINE.json configs[1] recipe)",
+            "config": dict(config_dict(n), parallelism=f"vertex shards x{world}, NCCL all-gather of edge deltas"),
+            "roofline": {"kernel": "search_kernel", "bound": "hbm", "achieved": achieved, "peak": peak * world,
+                         "unit": "GB/s", "frac": achieved / (peak * world), "peak_source": peak_kind + f" x{world}",
+                         "traffic": None},
+            "gpu_launches": int(launches), "gpu_launches_scope": "rank 0",
+            "clocks": clk,
+        }
+        if e2e:
+            line["e2e"] = e2e
+        if rec is not None:
+            line["recall_at_10"] = {"L_search": 100, "queries": WORKLOAD["queries"], "ours": rec}
+        print(json.dumps(line), flush=True)
+    del ws
+    comm.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
 
 
 def main():

@@ -20,8 +20,8 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libdance_b200.so"
 
-SOURCES = ["vamana_build.cu"]
-HEADERS = ["dance_common.cuh", "vamana_kernels.cuh"]
+SOURCES = ["vamana_build.cu", "vamana_sharded.cu"]
+HEADERS = ["dance_common.cuh", "vamana_kernels.cuh", "host_common.cuh"]
 PUBLIC_HEADERS = ["dance_b200.h", "gpu_vamana_builder.h", "gpu_vamana_config.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -60,7 +60,9 @@ def build(force: bool = False, ptxas_v: bool = False, verbose: bool = False) -> 
            "-I", str(ROOT / "include"), "-o", str(LIB) + ".tmp"]
     if ptxas_v:
         cmd += ["-Xptxas", "-v"]
+    cmd += ["--threads", "2"]
     cmd += [str(CSRC / s) for s in SOURCES]
+    cmd += ["-lnccl"]  # resolves to libnccl.so.2 (the copy torch loads when it is imported first)
     if verbose:
         print(" ".join(cmd), flush=True)
     res = subprocess.run(cmd, capture_output=True, text=True)

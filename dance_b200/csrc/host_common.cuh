@@ -26,6 +26,7 @@ namespace dance
 // ---------------------------------------------------------------- errors
 extern thread_local char g_err[512];
 extern std::atomic<uint64_t> g_launches;
+extern thread_local DanceBuildReport g_report; // last resident or sharded build
 
 inline int fail(int code, const char *fmt, ...)
 {
@@ -350,7 +351,7 @@ using namespace dance;
 struct DanceWorkspace
 {
     int device = 0;
-    uint32_t N = 0, R = 0, L = 0, C = 0, S = 0;
+    uint32_t N = 0, R = 0, L = 0, C = 0, S = 0, Local = 0;
     DevBuf cur_ids, cur_dists, degree;
     DevBuf work_ids, work_dists, work_deg;
     DevBuf exp_ids, exp_dists, exp_count;
@@ -360,32 +361,44 @@ struct DanceWorkspace
     DevBuf med_scores, med_cand, medoid;
     DevBuf counters;
 
-    int reserve(uint32_t n, uint32_t r, uint32_t l, uint32_t c, uint32_t s)
+    // n: vertices of the whole graph; local: vertices whose work rows,
+    // expansion lists and own distance rows live here (n on one GPU, the
+    // shard size when the build is sharded); graph: also allocate the N x R
+    // graph and degrees (the sharded build uses the caller's buffers).
+    int reserve(uint32_t n, uint32_t r, uint32_t l, uint32_t c, uint32_t s, uint32_t local = 0xFFFFFFFFu,
+                bool graph = true)
     {
+        if (local > n)
+            local = n;
         N = n;
         R = r;
         L = l;
         C = c;
         S = s;
-        const uint64_t nr = (uint64_t)n * r, nc = (uint64_t)n * c, ns = (uint64_t)n * s;
-        const uint64_t ntiles = (n + kScanTile - 1) / kScanTile + 1;
-        DANCE_CUDA(cur_ids.ensure(nr * 4));
-        DANCE_CUDA(cur_dists.ensure(nr * 4));
-        DANCE_CUDA(degree.ensure((uint64_t)n * 4));
-        DANCE_CUDA(work_ids.ensure(nc * 4));
-        DANCE_CUDA(work_dists.ensure(nc * 4));
-        DANCE_CUDA(work_deg.ensure((uint64_t)n * 4));
-        DANCE_CUDA(exp_ids.ensure(ns * 4));
-        DANCE_CUDA(exp_dists.ensure(ns * 4));
-        DANCE_CUDA(exp_count.ensure((uint64_t)n * 4));
-        DANCE_CUDA(rev_cnt.ensure((uint64_t)n * 4));
-        DANCE_CUDA(rev_off.ensure(((uint64_t)n + 1) * 4));
-        DANCE_CUDA(rev_cursor.ensure((uint64_t)n * 4));
+        Local = local;
+        const uint64_t nr = (uint64_t)n * r;
+        const uint64_t lr = (uint64_t)local * r, lc = (uint64_t)local * c, ls = (uint64_t)local * s;
+        const uint64_t ntiles = (local + kScanTile - 1) / kScanTile + 1;
+        if (graph)
+        {
+            DANCE_CUDA(cur_ids.ensure(nr * 4));
+            DANCE_CUDA(degree.ensure((uint64_t)n * 4));
+        }
+        DANCE_CUDA(cur_dists.ensure(lr * 4));
+        DANCE_CUDA(work_ids.ensure(lc * 4));
+        DANCE_CUDA(work_dists.ensure(lc * 4));
+        DANCE_CUDA(work_deg.ensure((uint64_t)local * 4));
+        DANCE_CUDA(exp_ids.ensure(ls * 4));
+        DANCE_CUDA(exp_dists.ensure(ls * 4));
+        DANCE_CUDA(exp_count.ensure((uint64_t)local * 4));
+        DANCE_CUDA(rev_cnt.ensure((uint64_t)local * 4));
+        DANCE_CUDA(rev_off.ensure(((uint64_t)local + 1) * 4));
+        DANCE_CUDA(rev_cursor.ensure((uint64_t)local * 4));
         DANCE_CUDA(rev.ensure(nr * 4));
         DANCE_CUDA(tiles.ensure(ntiles * 4));
-        DANCE_CUDA(heavy_list.ensure((uint64_t)n * 4));
+        DANCE_CUDA(heavy_list.ensure((uint64_t)local * 4));
         DANCE_CUDA(heavy_count.ensure(16));
-        DANCE_CUDA(huge_list.ensure((uint64_t)n * 4));
+        DANCE_CUDA(huge_list.ensure((uint64_t)local * 4));
         const uint64_t huge_words = (uint64_t)kHugeBlocks * ((n + 1u) / 2u);
         if (!huge_scratch.p || huge_scratch.bytes < huge_words * 4)
         {

@@ -31,6 +31,7 @@ namespace dance
 {
 thread_local char g_err[512] = "";
 std::atomic<uint64_t> g_launches{0};
+thread_local DanceBuildReport g_report;
 
 static int build_resident_impl(int dtype, const void *d_data, uint64_t stride, uint32_t N, uint32_t dim, uint32_t R,
                                uint32_t L, uint32_t C, uint32_t STEPS, const DanceVamanaParams &prm,
@@ -216,7 +217,6 @@ static int build_resident_impl(int dtype, const void *d_data, uint64_t stride, u
 } // namespace dance
 
 // ====================================================================== additive C ABI
-static thread_local DanceBuildReport g_report;
 
 extern "C" {
 

@@ -295,7 +295,7 @@ __global__ void __launch_bounds__(kBlockThreads) medoid_score_kernel(StoreView s
 }
 
 // Lowest score, first candidate on ties; entry 0 if no finite score.
-__global__ void __launch_bounds__(1024) medoid_argmin_kernel(const float *scores, const uint32_t *cand_ids,
+static __global__ void __launch_bounds__(1024) medoid_argmin_kernel(const float *scores, const uint32_t *cand_ids,
                                                              uint32_t nc, uint32_t *medoid)
 {
     __shared__ float s_v[32];
@@ -871,7 +871,7 @@ __global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
 // Reverse edges: source rows [s0, s1) of an edge table (row stride
 // src_stride, first min(src_deg, R) slots), kept when the target lies in
 // [t0, t1); counts and cursors are indexed by target - t0.
-__global__ void rev_count_kernel(const uint32_t *src_ids, uint64_t src_stride, const uint32_t *src_deg, uint32_t N,
+static __global__ void rev_count_kernel(const uint32_t *src_ids, uint64_t src_stride, const uint32_t *src_deg, uint32_t N,
                                  uint32_t R, uint32_t s0, uint32_t s1, uint32_t t0, uint32_t t1, uint32_t *cnt)
 {
     const uint64_t total = (uint64_t)(s1 - s0) * R;
@@ -889,7 +889,7 @@ __global__ void rev_count_kernel(const uint32_t *src_ids, uint64_t src_stride, c
     }
 }
 
-__global__ void rev_fill_kernel(const uint32_t *src_ids, uint64_t src_stride, const uint32_t *src_deg, uint32_t N,
+static __global__ void rev_fill_kernel(const uint32_t *src_ids, uint64_t src_stride, const uint32_t *src_deg, uint32_t N,
                                 uint32_t R, uint32_t s0, uint32_t s1, uint32_t t0, uint32_t t1, uint32_t *cursor,
                                 uint32_t *rev)
 {
@@ -910,7 +910,7 @@ __global__ void rev_fill_kernel(const uint32_t *src_ids, uint64_t src_stride, co
 
 // Copies the first R slots of the local work rows (and their degrees) into
 // rows [v0, v1) of an R-wide edge table, for the all-gather of edge deltas.
-__global__ void pack_work_rows_kernel(const uint32_t *work_ids, const uint32_t *work_deg, uint32_t C, uint32_t R,
+static __global__ void pack_work_rows_kernel(const uint32_t *work_ids, const uint32_t *work_deg, uint32_t C, uint32_t R,
                                       uint32_t v0, uint32_t v1, uint32_t *table, uint32_t *table_deg)
 {
     const uint64_t total = (uint64_t)(v1 - v0) * R;
@@ -962,7 +962,7 @@ __device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t v, uint32_t *s
     return before + x - v;
 }
 
-__global__ void __launch_bounds__(kScanThreads) scan_tile_sums_kernel(const uint32_t *in, uint32_t n,
+static __global__ void __launch_bounds__(kScanThreads) scan_tile_sums_kernel(const uint32_t *in, uint32_t n,
                                                                       uint32_t *tile_sums)
 {
     __shared__ uint32_t s_warp[32];
@@ -978,7 +978,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_tile_sums_kernel(const uint
         tile_sums[blockIdx.x] = total;
 }
 
-__global__ void __launch_bounds__(kScanThreads) scan_tile_offsets_kernel(uint32_t *tile_sums, uint32_t ntiles)
+static __global__ void __launch_bounds__(kScanThreads) scan_tile_offsets_kernel(uint32_t *tile_sums, uint32_t ntiles)
 {
     __shared__ uint32_t s_warp[32];
     uint32_t carry = 0;
@@ -995,7 +995,7 @@ __global__ void __launch_bounds__(kScanThreads) scan_tile_offsets_kernel(uint32_
     }
 }
 
-__global__ void __launch_bounds__(kScanThreads) scan_apply_kernel(const uint32_t *in, uint32_t n,
+static __global__ void __launch_bounds__(kScanThreads) scan_apply_kernel(const uint32_t *in, uint32_t n,
                                                                   const uint32_t *tile_offsets, uint32_t *out,
                                                                   uint32_t *cursor)
 {

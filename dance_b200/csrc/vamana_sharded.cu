@@ -1,0 +1,425 @@
+// vamana_sharded.cu -- the standard build sharded over the GPUs of one box.
+//
+// The reference has no multi-GPU build of one graph (its only multi-GPU
+// modes are independent shard builds on host threads, integration patch
+// lines 3376-3600, and round-robin merge buckets, src/gpu_merge.cu:643-650).
+// Here one process per GPU owns the contiguous vertex range
+// [rank*chunk, min(N, (rank+1)*chunk)), chunk = ceil(N / world); vectors and
+// the current graph are replicated.  Each round:
+//   search + insert replay of own vertices  (reads the replicated graph)
+//   pack the first R slots of own work rows into rows [v0, v1) of an
+//   N x R edge table, ncclAllGather it (in place) with the work degrees
+//   reverse CSR of the edges that target own vertices + merge (local)
+//   prune own vertices into rows [v0, v1) of the graph, ncclAllGather the
+//   graph and degrees (in place) for the next round.
+// Every rank runs the same kernels as the one-GPU build on the same inputs,
+// so the graph is bit-identical to it.  The communicator is non-blocking:
+// every wait on NCCL or on the build stream is bounded by the communicator's
+// timeout, after which the communicator is aborted and -4 is returned.
+
+#include <nccl.h>
+
+#include <chrono>
+#include <thread>
+
+#include "host_common.cuh"
+
+struct DanceComm
+{
+    ncclComm_t comm = nullptr;
+    int rank = 0, world = 1, device = 0;
+    double timeout_s = 60.0;
+    bool aborted = false;
+};
+
+namespace dance
+{
+
+#define DANCE_NCCL(call)                                                                                      \
+    do                                                                                                        \
+    {                                                                                                         \
+        ncclResult_t r__ = (call);                                                                            \
+        if (r__ != ncclSuccess && r__ != ncclInProgress)                                                      \
+            return fail(-3, "NCCL error %s at %s:%d (%s)", ncclGetErrorString(r__), __FILE__, __LINE__, #call); \
+    } while (0)
+
+using Clock = std::chrono::steady_clock;
+
+// Waits until the communicator has no operation in flight on the host side.
+static int nccl_settle(DanceComm *c, Clock::time_point deadline)
+{
+    while (true)
+    {
+        ncclResult_t st = ncclSuccess;
+        ncclResult_t r = ncclCommGetAsyncError(c->comm, &st);
+        if (r != ncclSuccess)
+            return fail(-3, "ncclCommGetAsyncError: %s", ncclGetErrorString(r));
+        if (st == ncclSuccess)
+            return 0;
+        if (st != ncclInProgress)
+        {
+            ncclCommAbort(c->comm);
+            c->aborted = true;
+            return fail(-3, "NCCL asynchronous error: %s", ncclGetErrorString(st));
+        }
+        if (Clock::now() > deadline)
+        {
+            ncclCommAbort(c->comm);
+            c->aborted = true;
+            return fail(-4, "NCCL operation did not settle within %.1f s; communicator aborted", c->timeout_s);
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(50));
+    }
+}
+
+// Waits for the build stream with the communicator's timeout; a peer that
+// stopped participating leaves a collective pending, which ends in an abort.
+static int stream_wait(DanceComm *c, cudaStream_t s, Clock::time_point deadline)
+{
+    while (true)
+    {
+        const cudaError_t e = cudaStreamQuery(s);
+        if (e == cudaSuccess)
+            return 0;
+        if (e != cudaErrorNotReady)
+            return fail(-2, "CUDA error %s while waiting for the build stream", cudaGetErrorString(e));
+        ncclResult_t st = ncclSuccess;
+        ncclCommGetAsyncError(c->comm, &st);
+        if (st != ncclSuccess && st != ncclInProgress)
+        {
+            ncclCommAbort(c->comm);
+            c->aborted = true;
+            return fail(-3, "NCCL asynchronous error: %s", ncclGetErrorString(st));
+        }
+        if (Clock::now() > deadline)
+        {
+            ncclCommAbort(c->comm);
+            c->aborted = true;
+            return fail(-4, "build stream did not finish within %.1f s; communicator aborted", c->timeout_s);
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(100));
+    }
+}
+
+static Clock::time_point deadline_of(const DanceComm *c)
+{
+    return Clock::now() + std::chrono::duration_cast<Clock::duration>(std::chrono::duration<double>(c->timeout_s));
+}
+
+// In-place all-gather of rows [rank*chunk, (rank+1)*chunk) of a table with
+// `width` uint32 per row.
+static int allgather_rows(DanceComm *c, uint32_t *table, uint64_t chunk, uint64_t width, cudaStream_t s)
+{
+    const uint64_t count = chunk * width;
+    DANCE_NCCL(ncclAllGather(table + (uint64_t)c->rank * count, table, count, ncclUint32, c->comm, s));
+    return nccl_settle(c, deadline_of(c));
+}
+
+} // namespace dance
+
+extern "C" {
+
+DANCE_API void dance_shard_range(uint32_t num_points, int world, int rank, uint32_t *v0, uint32_t *v1, uint32_t *chunk)
+{
+    const uint32_t ch = world > 0 ? (uint32_t)((num_points + (uint32_t)world - 1u) / (uint32_t)world) : num_points;
+    uint64_t a = (uint64_t)ch * (uint32_t)rank;
+    uint64_t b = a + ch;
+    if (a > num_points)
+        a = num_points;
+    if (b > num_points)
+        b = num_points;
+    if (v0)
+        *v0 = (uint32_t)a;
+    if (v1)
+        *v1 = (uint32_t)b;
+    if (chunk)
+        *chunk = ch;
+}
+
+DANCE_API int dance_nccl_unique_id(uint8_t *out, size_t out_bytes)
+{
+    if (!out || out_bytes < sizeof(ncclUniqueId))
+        return fail(-1, "unique id buffer must hold %zu bytes", sizeof(ncclUniqueId));
+    ncclUniqueId id;
+    DANCE_NCCL(ncclGetUniqueId(&id));
+    std::memcpy(out, &id, sizeof(id));
+    return 0;
+}
+
+DANCE_API int dance_comm_create(int rank, int world, const uint8_t *unique_id, size_t id_bytes, double timeout_s,
+                                DanceComm **out)
+{
+    if (!out || !unique_id || id_bytes < sizeof(ncclUniqueId) || world < 1 || rank < 0 || rank >= world ||
+        timeout_s <= 0)
+        return fail(-1, "invalid communicator arguments");
+    DanceComm *c = new DanceComm();
+    c->rank = rank;
+    c->world = world;
+    c->timeout_s = timeout_s;
+    cudaGetDevice(&c->device);
+    ncclUniqueId id;
+    std::memcpy(&id, unique_id, sizeof(id));
+    ncclConfig_t cfg = NCCL_CONFIG_INITIALIZER;
+    cfg.blocking = 0;
+    ncclResult_t r = ncclCommInitRankConfig(&c->comm, world, id, rank, &cfg);
+    if (r != ncclSuccess && r != ncclInProgress)
+    {
+        delete c;
+        return fail(-3, "ncclCommInitRankConfig: %s", ncclGetErrorString(r));
+    }
+    int rc = nccl_settle(c, deadline_of(c));
+    if (rc)
+    {
+        if (!c->aborted && c->comm)
+            ncclCommAbort(c->comm);
+        delete c;
+        return rc;
+    }
+    *out = c;
+    return 0;
+}
+
+DANCE_API void dance_comm_destroy(DanceComm *c)
+{
+    if (!c)
+        return;
+    if (c->comm && !c->aborted)
+    {
+        ncclCommFinalize(c->comm);
+        nccl_settle(c, deadline_of(c));
+        if (!c->aborted)
+            ncclCommDestroy(c->comm);
+    }
+    delete c;
+}
+
+DANCE_API int dance_vamana_build_sharded(DanceComm *comm, int dtype, const void *d_data, uint64_t stride,
+                                         uint32_t N, uint32_t dim, uint32_t R, uint32_t L, uint32_t C,
+                                         uint32_t STEPS, const DanceVamanaParams *params, DanceWorkspace *ws,
+                                         uint32_t *d_graph, uint32_t *d_degree, uint32_t *d_table_degree,
+                                         uint32_t *medoid_out, void *stream)
+{
+    if (!comm || comm->aborted)
+        return fail(-1, "communicator missing or aborted");
+    int rc = check_store(dtype, d_data, stride, N, dim);
+    if (rc)
+        return rc;
+    if (!d_graph || !d_degree || !d_table_degree)
+        return fail(-1, "null graph buffers");
+    if (R == 0 || L == 0 || C == 0 || STEPS == 0 || C < R || C > 1024 || L > 1024)
+        return fail(-1, "invalid parameters: R=%u L=%u C=%u STEPS=%u", R, L, C, STEPS);
+    if (STEPS > L)
+        STEPS = L;
+    DanceVamanaParams prm;
+    if (params)
+        prm = *params;
+    else
+        dance_vamana_default_params(&prm);
+    if (prm.iters == 0 || prm.visited_log2 < 8 || prm.visited_log2 > 16)
+        return fail(-1, "invalid params");
+    uint32_t v0, v1, chunk;
+    dance_shard_range(N, comm->world, comm->rank, &v0, &v1, &chunk);
+    const uint32_t nloc = v1 - v0;
+    DanceWorkspace *own = nullptr;
+    if (!ws)
+    {
+        own = new DanceWorkspace();
+        cudaGetDevice(&own->device);
+        rc = own->reserve(N, R, L, C, std::min(STEPS, L), std::max<uint32_t>(chunk, 1u), false);
+        if (rc)
+        {
+            delete own;
+            return rc;
+        }
+        ws = own;
+    }
+    struct Owner
+    {
+        DanceWorkspace *p;
+        ~Owner() { delete p; }
+    } owner{own};
+    if (ws->N < N || ws->Local < chunk || ws->R != R || ws->C != C || ws->S < std::min(STEPS, L))
+        return fail(-1, "workspace too small for the shard");
+    cudaStream_t s = as_stream(stream);
+    const StoreView st = make_view(d_data, stride, N, dim, dtype);
+    uint32_t *cur_ids = d_graph;   // (world * chunk) x R, replicated
+    uint32_t *degree = d_degree;   // world * chunk, replicated
+    uint32_t *tdeg = d_table_degree; // world * chunk: degrees of the gathered edge table
+    float *cur_dists = ws->cur_dists.as<float>(); // own rows only
+    DANCE_CUDA(cudaMemsetAsync(ws->counters.p, 0, 64, s));
+    // events: build start/end and search-kernel start/end of every round
+    std::vector<cudaEvent_t> ev(2 + 2 * (size_t)prm.iters, nullptr);
+    struct EvGuard
+    {
+        std::vector<cudaEvent_t> &e;
+        ~EvGuard()
+        {
+            for (auto x : e)
+                if (x)
+                    cudaEventDestroy(x);
+        }
+    } guard{ev};
+    for (auto &e : ev)
+        DANCE_CUDA(cudaEventCreate(&e));
+    DANCE_CUDA(cudaEventRecord(ev[0], s));
+
+    // medoid: every rank computes the same entry point
+    const uint32_t nc = std::min<uint32_t>(prm.medoid_candidates, std::min<uint32_t>(N, 4096u));
+    const uint32_t ns = std::min<uint32_t>(prm.medoid_samples, N);
+    uint32_t *d_medoid = ws->medoid.as<uint32_t>();
+    if (nc > 0 && ns > 0)
+    {
+        rc = dispatch<LaunchMedoid>(dtype, st.nchunks, st, nc, ns, ws->med_scores.as<float>(),
+                                    ws->med_cand.as<uint32_t>(), d_medoid, s);
+        if (rc)
+            return rc;
+    }
+    else
+        DANCE_CUDA(cudaMemsetAsync(d_medoid, 0, 4, s));
+    if (nloc)
+    {
+        rc = dispatch<LaunchInit>(dtype, st.nchunks, st, R, cur_ids, cur_dists, degree, v0, v1, v0, s);
+        if (rc)
+            return rc;
+    }
+    if ((rc = allgather_rows(comm, cur_ids, chunk, R, s)) || (rc = allgather_rows(comm, degree, chunk, 1, s)))
+        return rc;
+
+    for (uint32_t it = 0; it < prm.iters; ++it)
+    {
+        const float alpha = (it + 1 >= prm.iters) ? prm.alpha : 1.0f;
+        const uint32_t steps = steps_for_round(it, STEPS, prm);
+        if (nloc)
+        {
+            SearchParams sp{};
+            sp.st = st;
+            sp.R = R;
+            sp.L = L;
+            sp.Lcap = lcap_of(L);
+            sp.steps = steps;
+            sp.seeds = std::min<uint32_t>(prm.init_random_seeds, 31u);
+            sp.log2h = prm.visited_log2;
+            sp.entry_ptr = d_medoid;
+            sp.cur_ids = cur_ids;
+            sp.cur_dists = cur_dists;
+            sp.degree = degree;
+            sp.exp_ids = ws->exp_ids.as<uint32_t>();
+            sp.exp_dists = ws->exp_dists.as<float>();
+            sp.exp_count = ws->exp_count.as<uint32_t>();
+            sp.exp_stride = ws->S;
+            sp.v0 = v0;
+            sp.v1 = v1;
+            sp.lrow0 = v0;
+            sp.counters = ws->counters.as<unsigned long long>();
+            DANCE_CUDA(cudaEventRecord(ev[2 + 2 * it], s));
+            if ((rc = dispatch<LaunchSearch>(dtype, st.nchunks, sp, s)))
+                return rc;
+            DANCE_CUDA(cudaEventRecord(ev[3 + 2 * it], s));
+            ReplayParams rp{};
+            rp.st = st;
+            rp.R = R;
+            rp.C = C;
+            rp.alpha = alpha;
+            rp.cur_ids = cur_ids;
+            rp.cur_dists = cur_dists;
+            rp.degree = degree;
+            rp.exp_ids = sp.exp_ids;
+            rp.exp_dists = sp.exp_dists;
+            rp.exp_count = sp.exp_count;
+            rp.exp_stride = ws->S;
+            rp.work_ids = ws->work_ids.as<uint32_t>();
+            rp.work_dists = ws->work_dists.as<float>();
+            rp.work_deg = ws->work_deg.as<uint32_t>();
+            rp.v0 = v0;
+            rp.v1 = v1;
+            rp.lrow0 = v0;
+            rp.row_bytes = st.nchunks * 16;
+            rp.cache_rows = R + ws->S;
+            rp.counters = sp.counters;
+            if ((rc = dispatch<LaunchReplay>(dtype, st.nchunks, rp, s)))
+                return rc;
+            // own work rows (first R slots) -> rows [v0, v1) of the edge table
+            const uint64_t total = (uint64_t)nloc * R;
+            const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((total + 255) / 256, sm_count() * 16));
+            pack_work_rows_kernel<<<grid, 256, 0, s>>>(rp.work_ids, rp.work_deg, C, R, v0, v1, cur_ids, tdeg);
+            DANCE_LAUNCHED();
+        }
+        if ((rc = allgather_rows(comm, cur_ids, chunk, R, s)) || (rc = allgather_rows(comm, tdeg, chunk, 1, s)))
+            return rc;
+        if (nloc)
+        {
+            rc = reverse_merge_impl(dtype, st, R, C, prm, *ws, cur_ids, R, tdeg, 0, N, ws->work_ids.as<uint32_t>(),
+                                    ws->work_dists.as<float>(), ws->work_deg.as<uint32_t>(), v0, v1, s);
+            if (rc)
+                return rc;
+            PruneParams pp{};
+            pp.st = st;
+            pp.R = R;
+            pp.C = C;
+            pp.alpha = alpha;
+            pp.min_degree = (it + 1 == prm.iters) ? prm.final_min_degree : 0u;
+            pp.work_ids = ws->work_ids.as<uint32_t>();
+            pp.work_dists = ws->work_dists.as<float>();
+            pp.work_deg = ws->work_deg.as<uint32_t>();
+            pp.cur_ids = cur_ids;
+            pp.cur_dists = cur_dists;
+            pp.degree = degree;
+            pp.v0 = v0;
+            pp.v1 = v1;
+            pp.lrow0 = v0;
+            pp.row_bytes = st.nchunks * 16;
+            pp.counters = ws->counters.as<unsigned long long>();
+            if ((rc = dispatch<LaunchPrune>(dtype, st.nchunks, pp, s)))
+                return rc;
+        }
+        if ((rc = allgather_rows(comm, cur_ids, chunk, R, s)) || (rc = allgather_rows(comm, degree, chunk, 1, s)))
+            return rc;
+        if ((rc = stream_wait(comm, s, deadline_of(comm))))
+            return rc;
+    }
+    if (medoid_out)
+        DANCE_CUDA(cudaMemcpyAsync(medoid_out, d_medoid, 4, cudaMemcpyDeviceToHost, s));
+    DANCE_CUDA(cudaEventRecord(ev[1], s));
+    if ((rc = stream_wait(comm, s, deadline_of(comm))))
+        return rc;
+    DanceBuildReport &r = g_report;
+    std::memset(&r, 0, sizeof(r));
+    float a = 0;
+    cudaEventElapsedTime(&a, ev[0], ev[1]);
+    r.total_seconds = a * 1e-3;
+    if (nloc)
+        for (uint32_t it = 0; it < prm.iters; ++it)
+        {
+            cudaEventElapsedTime(&a, ev[2 + 2 * it], ev[3 + 2 * it]);
+            r.search_kernel_seconds += a * 1e-3;
+        }
+    uint64_t ctr[8] = {0};
+    DANCE_CUDA(cudaMemcpy(ctr, ws->counters.p, 64, cudaMemcpyDeviceToHost));
+    r.search_evals = ctr[0];
+    r.expansions = ctr[1];
+    r.replay_pairs = ctr[2];
+    r.reverse_evals = ctr[3];
+    r.prune_pairs = ctr[4];
+    return 0;
+}
+
+DANCE_API int dance_workspace_create_sharded(uint32_t num_points, int world, uint32_t R, uint32_t L, uint32_t C,
+                                             uint32_t STEPS, DanceWorkspace **out)
+{
+    if (!out || num_points == 0 || world < 1 || R == 0 || L == 0 || C == 0 || STEPS == 0 || C < R)
+        return fail(-1, "invalid workspace shape");
+    uint32_t chunk;
+    dance_shard_range(num_points, world, 0, nullptr, nullptr, &chunk);
+    DanceWorkspace *ws = new DanceWorkspace();
+    cudaGetDevice(&ws->device);
+    int rc = ws->reserve(num_points, R, L, C, std::min(STEPS, L), std::max<uint32_t>(chunk, 1u), false);
+    if (rc)
+    {
+        delete ws;
+        return rc;
+    }
+    *out = ws;
+    return 0;
+}
+
+} // extern "C"

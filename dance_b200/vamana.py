@@ -179,3 +179,65 @@ def recall_at_k(found: np.ndarray, truth: np.ndarray, k: int = 10) -> float:
     for f, t in zip(found, truth):
         hits += len(set(f.tolist()) & set(t.tolist()))
     return hits / (k * len(truth))
+
+
+# ----------------------------------------------------------------- sharded build
+def shard_range(N: int, world: int, rank: int):
+    """(v0, v1, chunk) of `rank`: vertices [v0, v1), chunk = ceil(N / world)."""
+    a, b, c = ctypes.c_uint32(), ctypes.c_uint32(), ctypes.c_uint32()
+    load().dance_shard_range(N, world, rank, ctypes.byref(a), ctypes.byref(b), ctypes.byref(c))
+    return a.value, b.value, c.value
+
+
+def nccl_unique_id() -> bytes:
+    buf = (ctypes.c_uint8 * 128)()
+    check(load().dance_nccl_unique_id(buf, 128), "dance_nccl_unique_id")
+    return bytes(buf)
+
+
+class Comm:
+    """NCCL communicator of libdance_b200 (non-blocking, bounded waits)."""
+
+    def __init__(self, rank: int, world: int, unique_id: bytes, timeout_s: float = 120.0):
+        buf = (ctypes.c_uint8 * len(unique_id)).from_buffer_copy(unique_id)
+        self.handle = ctypes.c_void_p()
+        check(load().dance_comm_create(rank, world, buf, len(unique_id), ctypes.c_double(timeout_s),
+                                       ctypes.byref(self.handle)), "dance_comm_create")
+        self.rank, self.world = rank, world
+
+    def close(self):
+        if self.handle:
+            load().dance_comm_destroy(self.handle)
+            self.handle = ctypes.c_void_p()
+
+
+def sharded_workspace(N: int, world: int, R: int, L: int, C: int, STEPS: int) -> Workspace:
+    h = ctypes.c_void_p()
+    check(load().dance_workspace_create_sharded(N, world, R, L, C, STEPS, ctypes.byref(h)),
+          "dance_workspace_create_sharded")
+    return Workspace(h, N, R, L, C, STEPS)
+
+
+def build_sharded(comm: Comm, store, dim: int, stride: int, R: int, L: int, C: int, STEPS: int, params=None,
+                  workspace: Workspace | None = None, graph=None, degree=None, table_degree=None, stream=None):
+    """Sharded build over the communicator's GPUs; every rank returns the
+    whole graph (world*chunk rows, the first N meaningful)."""
+    import torch
+    n = store.shape[0]
+    _, _, chunk = shard_range(n, comm.world, comm.rank)
+    rows = chunk * comm.world
+    dev = store.device
+    if graph is None:
+        graph = torch.empty((rows, R), dtype=torch.int32, device=dev)
+    if degree is None:
+        degree = torch.empty((rows,), dtype=torch.int32, device=dev)
+    if table_degree is None:
+        table_degree = torch.empty((rows,), dtype=torch.int32, device=dev)
+    prm = params or default_params()
+    med = ctypes.c_uint32(0)
+    rc = load().dance_vamana_build_sharded(comm.handle, dtype_code(store), _ptr(store), stride, n, dim, R, L, C,
+                                           STEPS, ctypes.byref(prm), workspace.handle if workspace else None,
+                                           _ptr(graph), _ptr(degree), _ptr(table_degree), ctypes.byref(med),
+                                           _stream(stream))
+    check(rc, "dance_vamana_build_sharded")
+    return graph, degree, int(med.value)

@@ -131,6 +131,32 @@ DANCE_API int dance_stage_prune(int dtype, const void *d_data, uint64_t row_stri
                       const float *d_work_dists, const uint32_t *d_work_deg, uint32_t *d_cur_ids,
                       float *d_cur_dists, uint32_t *d_degree, void *stream);
 
+/* ---- sharded build over the GPUs of one box (one process per GPU) -------- */
+/* Rank r owns vertices [v0, v1) = [r*chunk, min(N, (r+1)*chunk)),
+ * chunk = ceil(N / world).  Graph buffers are world*chunk rows. */
+DANCE_API void dance_shard_range(uint32_t num_points, int world, int rank, uint32_t *v0, uint32_t *v1,
+                                 uint32_t *chunk);
+typedef struct DanceComm DanceComm;
+/* NCCL unique id (rank 0 creates it and shares it with the other ranks). */
+DANCE_API int dance_nccl_unique_id(uint8_t *out, size_t out_bytes);
+/* Non-blocking NCCL communicator on the current device; every wait on it is
+ * bounded by timeout_s, after which it is aborted and the call returns -4. */
+DANCE_API int dance_comm_create(int rank, int world, const uint8_t *unique_id, size_t id_bytes, double timeout_s,
+                                DanceComm **comm);
+DANCE_API void dance_comm_destroy(DanceComm *comm);
+DANCE_API int dance_workspace_create_sharded(uint32_t num_points, int world, uint32_t R, uint32_t L, uint32_t C,
+                                             uint32_t STEPS, DanceWorkspace **ws);
+/* The standard build with vertex batches sharded across the communicator's
+ * ranks; d_data is the full store on every rank.  d_graph (world*chunk x R),
+ * d_degree and d_table_degree (world*chunk) are caller buffers; on return
+ * every rank holds the whole graph, bit-identical to the one-GPU build.
+ * Edge deltas are exchanged with ncclAllGather twice per round. */
+DANCE_API int dance_vamana_build_sharded(DanceComm *comm, int dtype, const void *d_data, uint64_t row_stride_bytes,
+                                         uint32_t num_points, uint32_t dim, uint32_t R, uint32_t L, uint32_t C,
+                                         uint32_t STEPS, const DanceVamanaParams *params, DanceWorkspace *ws,
+                                         uint32_t *d_graph, uint32_t *d_degree, uint32_t *d_table_degree,
+                                         uint32_t *medoid_out, void *stream);
+
 /* ---- query search over a built graph (recall harness) -------------------- */
 /* DiskANN-style best-first search from `start` with list size L_search; the
  * K nearest found per query go to d_out_ids / d_out_dists (nq x K). */
