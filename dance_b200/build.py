@@ -61,6 +61,8 @@ def build(force: bool = False, ptxas_v: bool = False, verbose: bool = False) -> 
     if ptxas_v:
         cmd += ["-Xptxas", "-v"]
     cmd += ["--threads", "2"]
+    # extra defines, e.g. DANCE_NVCC_FLAGS="-DVAMANA_ITERS=3 -DENABLE_FLOAT16_BUILD=1"
+    cmd += os.environ.get("DANCE_NVCC_FLAGS", "").split()
     cmd += [str(CSRC / s) for s in SOURCES]
     cmd += ["-lnccl"]  # resolves to libnccl.so.2 (the copy torch loads when it is imported first)
     if verbose:
