@@ -134,7 +134,8 @@ def load(path: str | os.PathLike | None = None) -> ctypes.CDLL:
     global _lib
     if _lib is not None and path is None:
         return _lib
-    p = Path(path) if path else LIB_PATH
+    env = os.environ.get("DANCE_B200_LIB")
+    p = Path(path) if path else (Path(env) if env else LIB_PATH)
     if not p.exists():
         raise FileNotFoundError(
             f"{p} is missing: build the CUDA library with `python -m dance_b200.build` "

@@ -45,8 +45,8 @@ static int build_resident_impl(int dtype, const void *d_data, uint64_t stride, u
         return fail(-1, "invalid parameters: R=%u L=%u C=%u STEPS=%u", R, L, C, STEPS);
     if (C < R)
         return fail(-1, "invalid parameters: C=%u must be >= R=%u", C, R);
-    if (C > 1024 || L > 1024 || R > 1024)
-        return fail(-1, "R, L and C are limited to 1024 in this build");
+    if (C > 1024 || L > kMaxL || R > 1024)
+        return fail(-1, "R and C are limited to 1024 and L to %d in this build", kMaxL);
     if (STEPS > L)
     {
         fprintf(stderr, "[dance_b200] STEPS=%u is larger than L=%u, clamp STEPS to L.\n", STEPS, L);
@@ -236,7 +236,7 @@ void dance_vamana_default_params(DanceVamanaParams *p)
     p->reverse_heavy_cap = ENABLE_REVERSE_HEAVY_CAP;
     p->reverse_heavy_threshold = REVERSE_HEAVY_THRESHOLD;
     p->reverse_heavy_sample = REVERSE_HEAVY_SAMPLE;
-    p->visited_log2 = 11;
+    p->visited_log2 = 10;
 }
 
 const char *dance_last_error(void) { return dance::g_err; }
@@ -349,7 +349,7 @@ int dance_stage_search(int dtype, const void *d_data, uint64_t stride, uint32_t 
     if (rc)
         return rc;
     steps = std::min(steps, L);
-    if (steps > exp_stride || L == 0 || R == 0 || L > 1024 || visited_log2 < 8 || visited_log2 > 16)
+    if (steps > exp_stride || L == 0 || R == 0 || L > (uint32_t)kMaxL || visited_log2 < 8 || visited_log2 > 16)
         return fail(-1, "invalid search stage arguments");
     SearchParams sp{};
     sp.st = make_view(d_data, stride, N, dim, dtype);
@@ -494,7 +494,7 @@ int dance_search_queries(int dtype, const void *d_data, uint64_t stride, uint32_
     int rc = check_store(dtype, d_data, stride, N, dim);
     if (rc)
         return rc;
-    if (!d_graph || !d_queries || !d_out_ids || !d_out_dists || K == 0 || K > L_search || L_search > 1024 ||
+    if (!d_graph || !d_queries || !d_out_ids || !d_out_dists || K == 0 || K > L_search || L_search > (uint32_t)kMaxL ||
         query_stride % 16 != 0 || visited_log2 < 8 || visited_log2 > 16)
         return fail(-1, "invalid query search arguments");
     QueryParams qp{};

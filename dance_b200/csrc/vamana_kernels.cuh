@@ -24,6 +24,12 @@ namespace dance
 {
 
 constexpr int kWarpsPerBlock = 4;
+constexpr int kMaxL = 256; // search pool capacity limit (8 entries per lane)
+// Resident blocks per SM the search kernels are compiled for (caps their
+// registers; the kernels are latency-bound and gain from more resident warps).
+#ifndef DANCE_SEARCH_MIN_BLOCKS
+#define DANCE_SEARCH_MIN_BLOCKS 8
+#endif
 constexpr int kBlockThreads = kWarpsPerBlock * 32;
 
 struct StoreView
@@ -50,7 +56,8 @@ struct SearchSmem
     uint32_t Lcap;
     uint32_t *bid;  // batch ids (64)
     float *bd;      // batch distances (64)
-    uint64_t *bkey; // sorted, deduplicated batch keys (64)
+    uint64_t *bkey; // survivor keys (64), sorted before the merge
+    uint32_t *bins; // survivors' insertion points in the pool (64)
     uint32_t *vis;  // visited table (1 << log2h ids)
     __device__ __forceinline__ uint64_t *pk(int b) const { return pk0 + (uint32_t)b * Lcap; }
     __device__ __forceinline__ uint8_t *pf(int b) const { return pf0 + (uint32_t)b * Lcap; }
@@ -60,7 +67,7 @@ __host__ __device__ __forceinline__ uint32_t align16(uint32_t x) { return (x + 1
 
 __host__ __device__ __forceinline__ uint32_t search_smem_per_warp(uint32_t Lcap, uint32_t log2h)
 {
-    return align16(16u * Lcap) + align16(2u * Lcap) + 256u + 256u + 512u + align16(4u << log2h);
+    return align16(16u * Lcap) + align16(2u * Lcap) + 256u + 256u + 512u + 256u + align16(4u << log2h);
 }
 
 __device__ __forceinline__ SearchSmem carve_search_smem(uint8_t *base, uint32_t Lcap, uint32_t log2h)
@@ -78,6 +85,8 @@ __device__ __forceinline__ SearchSmem carve_search_smem(uint8_t *base, uint32_t 
     p += 256;
     s.bkey = reinterpret_cast<uint64_t *>(p);
     p += 512;
+    s.bins = reinterpret_cast<uint32_t *>(p);
+    p += 256;
     s.vis = reinterpret_cast<uint32_t *>(p);
     return s;
 }
@@ -86,16 +95,77 @@ __device__ __forceinline__ SearchSmem carve_search_smem(uint8_t *base, uint32_t 
 struct PoolState
 {
     int P;   // entries in the pool
-    int cur; // which pk/pf buffer is current
     int L;   // capacity
+    int lb;  // every entry below lb is expanded
+    int cur; // which key/flag buffer holds the pool
 };
+
+// Number of elements of sorted a[0..n) that are <= x.
+__device__ __forceinline__ int upper_bound_u32(const uint32_t *a, int n, uint32_t x)
+{
+    int lo = 0, hi = n;
+    while (lo < hi)
+    {
+        const int mid = (lo + hi) >> 1;
+        if (a[mid] <= x)
+            lo = mid + 1;
+        else
+            hi = mid;
+    }
+    return lo;
+}
+
+// Merges m2 sorted, distinct survivor keys sm.bkey[0..m2) (whose pool
+// insertion points are sm.bins[0..m2)) with the pool into the other buffer.
+__device__ __forceinline__ void pool_merge(const SearchSmem &sm, PoolState &ps, int m2, int lane)
+{
+    const uint64_t *pk = sm.pk(ps.cur);
+    const uint8_t *pf = sm.pf(ps.cur);
+    const int nxt = ps.cur ^ 1;
+    uint64_t *ok = sm.pk(nxt);
+    uint8_t *of = sm.pf(nxt);
+    for (int i = lane; i < ps.P; i += 32)
+    {
+        int shift;
+        if (m2 <= 8)
+        {
+            shift = 0;
+#pragma unroll 8
+            for (int j = 0; j < 8; ++j)
+                shift += (j < m2) && (sm.bins[j] <= (uint32_t)i);
+        }
+        else
+            shift = upper_bound_u32(sm.bins, m2, (uint32_t)i);
+        const int np = i + shift;
+        if (np < ps.L)
+        {
+            ok[np] = pk[i];
+            of[np] = pf[i];
+        }
+    }
+    for (int j = lane; j < m2; j += 32)
+    {
+        const int np = j + (int)sm.bins[j];
+        if (np < ps.L)
+        {
+            ok[np] = sm.bkey[j];
+            of[np] = 0;
+        }
+    }
+    __syncwarp();
+    ps.lb = min(ps.lb, (int)sm.bins[0]);
+    ps.P = min(ps.P + m2, ps.L);
+    ps.cur = nxt;
+}
 
 // Inserts up to 64 candidates (two per lane; kInvalid = none) into the pool.
 // Candidates already in the visited table are skipped (they were evaluated
 // before, so re-inserting them could not change the pool); the rest are
-// evaluated (unless their distance is given), keyed by (distance, id),
-// sorted, deduplicated and merged so the pool keeps the L smallest keys.
-// Returns the number of distances evaluated.
+// evaluated (unless their distance is given) and keyed by (distance, id).
+// Keys not below the pool's largest key when the pool is full are dropped;
+// the survivors are deduplicated, checked against the pool (the visited
+// table may have forgotten an id that is still pooled), sorted and merged
+// so the pool keeps the L smallest keys.  Returns the distances evaluated.
 template <int DT, int CPL>
 __device__ __forceinline__ int pool_insert_batch(const SearchSmem &sm, PoolState &ps, uint32_t log2h,
                                                  const StoreView &st, const uint4 (&q)[CPL], uint32_t id0,
@@ -143,85 +213,125 @@ __device__ __forceinline__ int pool_insert_batch(const SearchSmem &sm, PoolState
         eval_candidates<DT, CPL>(st.data, st.stride, st.nchunks, q, sm.bid, sm.bd, m, lane);
         __syncwarp();
     }
-    const uint64_t maxk = (ps.P >= ps.L) ? sm.pk(ps.cur)[ps.L - 1] : kKeyMax;
-    const int e0 = 2 * lane, e1 = 2 * lane + 1;
+    const uint64_t *pool = sm.pk(ps.cur);
+    const uint64_t maxk = (ps.P >= ps.L) ? pool[ps.L - 1] : kKeyMax;
+    const int e0 = lane, e1 = lane + 32;
     uint64_t k0 = e0 < m ? make_key(sm.bd[e0], sm.bid[e0]) : kKeyMax;
     uint64_t k1 = e1 < m ? make_key(sm.bd[e1], sm.bid[e1]) : kKeyMax;
     if (k0 >= maxk)
         k0 = kKeyMax;
     if (k1 >= maxk)
         k1 = kKeyMax;
-    const bool any = __any_sync(kFull, (k0 != kKeyMax) || (k1 != kKeyMax));
-    if (!any)
+    const unsigned s0 = __ballot_sync(kFull, k0 != kKeyMax);
+    const unsigned s1 = __ballot_sync(kFull, k1 != kKeyMax);
+    const int k = __popc(s0) + __popc(s1);
+    if (k == 0)
         return m;
-    warp_sort64(k0, k1, lane);
-    const uint64_t prev0 = __shfl_up_sync(kFull, k1, 1);
-    bool keep0 = k0 != kKeyMax && !(lane > 0 && prev0 == k0);
-    bool keep1 = k1 != kKeyMax && k1 != k0;
-    const uint64_t *pool = sm.pk(ps.cur);
-    if (keep0)
+    int m2;
+    if (k <= 32)
     {
-        const int p = lower_bound_u64(pool, ps.P, k0);
-        if (p < ps.P && pool[p] == k0)
-            keep0 = false;
+        // compact the survivors, then rank them by broadcast comparisons
+        __syncwarp();
+        if (k0 != kKeyMax)
+            sm.bkey[__popc(s0 & lt)] = k0;
+        if (k1 != kKeyMax)
+            sm.bkey[__popc(s0) + __popc(s1 & lt)] = k1;
+        __syncwarp();
+        const uint64_t key = lane < k ? sm.bkey[lane] : kKeyMax;
+        bool dup = false;
+#pragma unroll 4
+        for (int i = 0; i < k; ++i)
+        {
+            const uint64_t o = sm.bkey[i];
+            dup |= (i < lane) && (o == key);
+        }
+        bool keep = lane < k && !dup;
+        uint32_t ins = 0;
+        if (keep)
+        {
+            const int p = lower_bound_u64(pool, ps.P, key);
+            keep = !(p < ps.P && pool[p] == key);
+            ins = (uint32_t)p;
+        }
+        const unsigned km = __ballot_sync(kFull, keep);
+        m2 = __popc(km);
+        if (m2 == 0)
+            return m;
+        int rank = 0;
+#pragma unroll 4
+        for (int i = 0; i < k; ++i)
+            rank += ((km >> i) & 1u) && (sm.bkey[i] < key);
+        __syncwarp();
+        if (keep)
+        {
+            sm.bkey[rank] = key;
+            sm.bins[rank] = ins;
+        }
+        __syncwarp();
     }
-    if (keep1)
+    else
     {
-        const int p = lower_bound_u64(pool, ps.P, k1);
-        if (p < ps.P && pool[p] == k1)
-            keep1 = false;
-    }
-    const unsigned c0 = __ballot_sync(kFull, keep0);
-    const unsigned c1 = __ballot_sync(kFull, keep1);
-    const int m2 = __popc(c0) + __popc(c1);
-    if (m2 == 0)
-        return m;
-    {
-        const int before = __popc(c0 & lt) + __popc(c1 & lt);
+        // many survivors (early in the search): full bitonic sort
+        uint64_t a = k0, b = k1;
+        // warp_sort64 wants element 2*lane+s; the layout of the inputs is irrelevant
+        warp_sort64(a, b, lane);
+        const uint64_t prev0 = __shfl_up_sync(kFull, b, 1);
+        bool keep0 = a != kKeyMax && !(lane > 0 && prev0 == a);
+        bool keep1 = b != kKeyMax && b != a;
+        uint32_t ins0 = 0, ins1 = 0;
         if (keep0)
-            sm.bkey[before] = k0;
+        {
+            const int p = lower_bound_u64(pool, ps.P, a);
+            keep0 = !(p < ps.P && pool[p] == a);
+            ins0 = (uint32_t)p;
+        }
         if (keep1)
-            sm.bkey[before + (keep0 ? 1 : 0)] = k1;
-    }
-    __syncwarp();
-    const int nxt = ps.cur ^ 1;
-    for (int i = lane; i < ps.P; i += 32)
-    {
-        const uint64_t key = pool[i];
-        const int pos = i + lower_bound_u64(sm.bkey, m2, key);
-        if (pos < ps.L)
         {
-            sm.pk(nxt)[pos] = key;
-            sm.pf(nxt)[pos] = sm.pf(ps.cur)[i];
+            const int p = lower_bound_u64(pool, ps.P, b);
+            keep1 = !(p < ps.P && pool[p] == b);
+            ins1 = (uint32_t)p;
         }
-    }
-    for (int j = lane; j < m2; j += 32)
-    {
-        const uint64_t key = sm.bkey[j];
-        const int pos = j + lower_bound_u64(pool, ps.P, key);
-        if (pos < ps.L)
+        const unsigned c0 = __ballot_sync(kFull, keep0);
+        const unsigned c1 = __ballot_sync(kFull, keep1);
+        m2 = __popc(c0) + __popc(c1);
+        if (m2 == 0)
+            return m;
+        const int before = __popc(c0 & lt) + __popc(c1 & lt);
+        __syncwarp();
+        if (keep0)
         {
-            sm.pk(nxt)[pos] = key;
-            sm.pf(nxt)[pos] = 0;
+            sm.bkey[before] = a;
+            sm.bins[before] = ins0;
         }
+        if (keep1)
+        {
+            const int j = before + (keep0 ? 1 : 0);
+            sm.bkey[j] = b;
+            sm.bins[j] = ins1;
+        }
+        __syncwarp();
     }
-    __syncwarp();
-    ps.P = min(ps.P + m2, ps.L);
-    ps.cur = nxt;
+    pool_merge(sm, ps, m2, lane);
     return m;
 }
 
-// Index of the first unexpanded pool entry (smallest key), -1 if none.
-__device__ __forceinline__ int pool_select(const SearchSmem &sm, const PoolState &ps, int lane)
+// Index of the first unexpanded pool entry (smallest key), -1 if none;
+// scanning starts at ps.lb, below which everything is expanded.
+__device__ __forceinline__ int pool_select(const SearchSmem &sm, PoolState &ps, int lane)
 {
-    for (int base = 0; base < ps.P; base += 32)
+    for (int base = ps.lb; base < ps.P; base += 32)
     {
         const int i = base + lane;
         const bool u = i < ps.P && sm.pf(ps.cur)[i] == 0;
         const unsigned m = __ballot_sync(kFull, u);
         if (m)
-            return base + __ffs(m) - 1;
+        {
+            const int sel = base + __ffs(m) - 1;
+            ps.lb = sel + 1;
+            return sel;
+        }
     }
+    ps.lb = ps.P;
     return -1;
 }
 
@@ -418,7 +528,7 @@ struct SearchParams
 };
 
 template <int DT, int CPL>
-__global__ void __launch_bounds__(kBlockThreads) search_kernel(SearchParams p)
+__global__ void __launch_bounds__(kBlockThreads, DANCE_SEARCH_MIN_BLOCKS) search_kernel(SearchParams p)
 {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     const int lane = lane_id();
@@ -436,7 +546,7 @@ __global__ void __launch_bounds__(kBlockThreads) search_kernel(SearchParams p)
         uint4 q[CPL];
         load_frag<CPL>(q, st.data + (uint64_t)v * st.stride, st.nchunks, gl);
         clear_visited(sm.vis, p.log2h, lane);
-        PoolState ps{0, 0, (int)p.L};
+        PoolState ps{0, (int)p.L, 0, 0};
 
         // Seeds: entry point and hash seeds (distances computed) ...
         uint32_t sid = kInvalid;
@@ -534,7 +644,7 @@ struct QueryParams
 };
 
 template <int DT, int CPL>
-__global__ void __launch_bounds__(kBlockThreads) query_search_kernel(QueryParams p)
+__global__ void __launch_bounds__(kBlockThreads, DANCE_SEARCH_MIN_BLOCKS) query_search_kernel(QueryParams p)
 {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     const int lane = lane_id();
@@ -547,7 +657,7 @@ __global__ void __launch_bounds__(kBlockThreads) query_search_kernel(QueryParams
         uint4 q[CPL];
         load_frag<CPL>(q, p.queries + (uint64_t)qi * p.qstride, p.st.nchunks, gl);
         clear_visited(sm.vis, p.log2h, lane);
-        PoolState ps{0, 0, (int)p.L};
+        PoolState ps{0, (int)p.L, 0, 0};
         const uint32_t s0 = (lane == 0 && p.start < N) ? p.start : kInvalid;
         pool_insert_batch<DT, CPL>(sm, ps, p.log2h, p.st, q, s0, kInvalid, 0.0f, 0.0f, false, lane);
         while (true)
@@ -609,8 +719,9 @@ struct ReplayParams
 
 __host__ __device__ __forceinline__ uint32_t replay_smem_per_warp(uint32_t C, uint32_t cache_rows, uint32_t row_bytes)
 {
+    const uint32_t Cp = C <= 32 ? 32u : (uint32_t)next_pow2((int)C);
     return cache_rows * row_bytes + align16(4u * cache_rows) + align16(4u * C) + align16(4u * C) + align16(2u * C) +
-           align16(2u * C);
+           2u * align16(2u * C) + align16(8u * Cp);
 }
 
 // Warp argmax over (value, slot) pairs: larger value wins, lower slot on ties.
@@ -630,77 +741,122 @@ __device__ __forceinline__ void warp_argmax_lowslot(float &v, int &s)
     s = __shfl_sync(kFull, s, 0);
 }
 
+// Copies `count` rows (ids[k] -> slot k of cache) with 8-lane groups.
+template <int CPL>
+__device__ __forceinline__ void gather_rows_grouped(const uint8_t *__restrict__ data, uint64_t stride,
+                                                    uint32_t nchunks, const uint32_t *ids, int count, uint8_t *cache,
+                                                    uint32_t row_bytes, int lane)
+{
+    const int g = lane >> 3, gl = lane & 7;
+    for (int r = g; r < count; r += 4)
+    {
+        const uint4 *src = reinterpret_cast<const uint4 *>(data + (uint64_t)ids[r] * stride);
+        uint4 *dst = reinterpret_cast<uint4 *>(cache + (uint32_t)r * row_bytes);
+#pragma unroll
+        for (int t = 0; t < CPL; ++t)
+        {
+            const uint32_t c = (uint32_t)(gl + 8 * t);
+            if (c < nchunks)
+                dst[c] = ldg_chunk(src + c);
+        }
+    }
+}
+
+// Order key of a work-row slot: descending distance, then ascending slot --
+// the reference's preference for the victim and the worst entry
+// (src/gpu_vamana_vnew2.cu:816-846, strict '>' scans in slot order).
+__device__ __forceinline__ uint64_t order_key(float d, uint32_t slot)
+{
+    return ((uint64_t)(~__float_as_uint(d)) << 32) | slot;
+}
+
+// Online RobustInsert replay (reference dynamic_robust_insert_C_warp,
+// src/gpu_vamana_vnew2.cu:759-877) of each vertex's recorded expansion
+// sequence into its C-wide work row.  One warp per vertex; the row's
+// vectors (initial neighbours and expanded nodes) are cached in shared
+// memory, and the valid slots are kept in ord[] sorted by order_key, so
+//  - occlusion is tested from the nearest kept neighbour outwards and stops
+//    at the first occluder,
+//  - the victim is the first qualifying slot from the far end,
+//  - the worst slot is ord[0].
 template <int DT, int CPL>
 __global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
 {
     extern __shared__ __align__(16) uint8_t smem_raw[];
     const int lane = lane_id();
     const int g = lane >> 3, gl = lane & 7;
+    const uint32_t C = p.C;
+    const uint32_t Cp = C <= 32 ? 32u : (uint32_t)next_pow2((int)C);
     uint8_t *base = smem_raw + warp_id_in_block() * p.per_warp;
     uint8_t *cache = base;
     uint8_t *q = cache + p.cache_rows * p.row_bytes;
     uint32_t *gid = reinterpret_cast<uint32_t *>(q);
     q += align16(4u * p.cache_rows);
     uint32_t *wid = reinterpret_cast<uint32_t *>(q);
-    q += align16(4u * p.C);
+    q += align16(4u * C);
     float *wd = reinterpret_cast<float *>(q);
-    q += align16(4u * p.C);
+    q += align16(4u * C);
     uint16_t *wu = reinterpret_cast<uint16_t *>(q);
-    q += align16(2u * p.C);
-    uint16_t *lst = reinterpret_cast<uint16_t *>(q);
-    q += align16(2u * p.C);
+    q += align16(2u * C);
+    uint16_t *ordb = reinterpret_cast<uint16_t *>(q); // two buffers of C slots
+    const uint32_t ordstride = align16(2u * C) / 2u;
+    q += 2u * align16(2u * C);
+    uint64_t *okeys = reinterpret_cast<uint64_t *>(q); // Cp, initial sort
     const uint32_t N = p.st.N;
-    const uint32_t C = p.C;
     unsigned long long pairs = 0;
 
     for (uint32_t v = p.v0 + blockIdx.x * kWarpsPerBlock + warp_id_in_block(); v < p.v1;
          v += gridDim.x * kWarpsPerBlock)
     {
+        const uint64_t lv = v - p.lrow0;
         const uint32_t deg_self = min(p.degree[v], p.R);
-        for (uint32_t i = lane; i < C; i += 32)
+        for (uint32_t i = lane; i < Cp; i += 32)
         {
             uint32_t nb = kInvalid;
             float d = FLT_MAX;
             uint16_t u = 0xFFFFu;
+            uint64_t ok = kKeyMax;
             if (i < deg_self)
             {
                 nb = p.cur_ids[(uint64_t)v * p.R + i];
                 if (nb < N && nb != v)
                 {
-                    d = p.cur_dists[(uint64_t)(v - p.lrow0) * p.R + i];
+                    d = p.cur_dists[lv * p.R + i];
                     u = (uint16_t)i;
+                    ok = order_key(d, i);
                 }
                 else
                     nb = kInvalid;
             }
-            wid[i] = nb;
-            wd[i] = d;
-            wu[i] = u;
+            if (i < C)
+            {
+                wid[i] = nb;
+                wd[i] = d;
+                wu[i] = u;
+            }
+            okeys[i] = ok;
         }
-        const uint64_t lv = v - p.lrow0;
         const uint32_t cnt = min(p.exp_count[lv], p.exp_stride);
         for (uint32_t i = lane; i < p.R + cnt; i += 32)
         {
             uint32_t id;
             if (i < p.R)
-            {
                 id = i < deg_self ? p.cur_ids[(uint64_t)v * p.R + i] : v;
-                if (id >= N)
-                    id = v;
-            }
             else
-            {
                 id = p.exp_ids[lv * p.exp_stride + (i - p.R)];
-                if (id >= N)
-                    id = v;
-            }
-            gid[i] = id;
+            gid[i] = id < N ? id : v;
         }
         __syncwarp();
-        // rows [0, deg_self) and [R, R + cnt) of the cache
-        gather_rows_to_smem(p.st.data, p.st.stride, p.st.nchunks, gid, (int)deg_self, cache, p.row_bytes, lane);
-        gather_rows_to_smem(p.st.data, p.st.stride, p.st.nchunks, gid + p.R, (int)cnt, cache + p.R * p.row_bytes,
-                            p.row_bytes, lane);
+        warp_sort_smem_u64(okeys, (int)Cp, lane);
+        int nv = 0;
+        for (uint32_t b = 0; b < Cp; b += 32)
+            nv += __popc(__ballot_sync(kFull, okeys[b + lane] != kKeyMax));
+        int ob = 0;
+        for (int j = lane; j < nv; j += 32)
+            ordb[j] = (uint16_t)(okeys[j] & 0xFFFFu);
+        gather_rows_grouped<CPL>(p.st.data, p.st.stride, p.st.nchunks, gid, (int)deg_self, cache, p.row_bytes, lane);
+        gather_rows_grouped<CPL>(p.st.data, p.st.stride, p.st.nchunks, gid + p.R, (int)cnt,
+                                 cache + p.R * p.row_bytes, p.row_bytes, lane);
         __syncwarp();
         uint32_t wdeg = deg_self;
 
@@ -723,33 +879,25 @@ __global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
             }
             if (present)
                 continue;
+            const uint16_t *ord = ordb + ob * ordstride;
+            // ord[0, ngt) have d(v,y) > d(v,x); ord[ngt, nv) have d(v,y) <= d(v,x)
+            int ngt = 0;
+            for (int b = 0; b < nv; b += 32)
+            {
+                const int j = b + lane;
+                ngt += __popc(__ballot_sync(kFull, j < nv && wd[ord[j]] > dx));
+            }
             uint4 xf[CPL];
             load_frag_smem<CPL>(xf, cache + (p.R + k) * p.row_bytes, p.st.nchunks, gl);
-
-            // Occlusion: some kept y with d(v,y) <= d(v,x) and alpha*d(y,x) <= d(v,x).
-            int na = 0;
-            for (uint32_t b = 0; b < deg; b += 32)
-            {
-                const uint32_t i = b + lane;
-                bool in = false;
-                if (i < deg)
-                {
-                    const uint32_t y = wid[i];
-                    in = y < N && y != v && wd[i] <= dx;
-                }
-                const unsigned bm = __ballot_sync(kFull, in);
-                if (in)
-                    lst[na + __popc(bm & ((1u << lane) - 1u))] = (uint16_t)i;
-                na += __popc(bm);
-            }
-            __syncwarp();
+            // occlusion: nearest kept neighbours first
             bool occluded = false;
-            for (int b = 0; b < na; b += 4)
+            for (int b = nv - 1; b >= ngt; b -= 4)
             {
-                const int idx = b + g;
+                const int j = b - g;
                 uint4 c[CPL];
-                if (idx < na)
-                    load_frag_smem<CPL>(c, cache + (uint32_t)wu[lst[idx]] * p.row_bytes, p.st.nchunks, gl);
+                const bool act = j >= ngt;
+                if (act)
+                    load_frag_smem<CPL>(c, cache + (uint32_t)wu[ord[j]] * p.row_bytes, p.st.nchunks, gl);
                 else
                 {
 #pragma unroll
@@ -757,10 +905,9 @@ __global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
                         c[t] = make_uint4(0u, 0u, 0u, 0u);
                 }
                 const float d = GroupDist<DT, CPL>::eval(xf, c, p.st.nchunks, gl);
-                const bool hit = idx < na && gl == 0 && __fmul_rn(p.alpha, d) <= dx;
                 if (lane == 0)
-                    pairs += (uint32_t)min(4, na - b);
-                if (__any_sync(kFull, hit))
+                    pairs += (unsigned long long)min(4, b - ngt + 1);
+                if (__any_sync(kFull, act && gl == 0 && __fmul_rn(p.alpha, d) <= dx))
                 {
                     occluded = true;
                     break;
@@ -768,45 +915,15 @@ __global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
             }
             if (occluded)
                 continue;
-
-            // Worst kept entry and the victim (farthest y with d(v,y) > d(v,x) and
-            // alpha*d(x,y) <= d(v,y)); both lowest slot on ties.
-            float wv = -FLT_MAX;
-            int ws = -1;
-            int nb_ = 0;
-            for (uint32_t b = 0; b < deg; b += 32)
+            // victim: the first slot from the far end with alpha*d(x,y) <= d(v,y)
+            int vj = -1;
+            for (int b = 0; b < ngt; b += 4)
             {
-                const uint32_t i = b + lane;
-                bool in = false;
-                if (i < deg)
-                {
-                    const uint32_t y = wid[i];
-                    if (y < N && y != v)
-                    {
-                        const float dy = wd[i];
-                        if (dy > wv)
-                        {
-                            wv = dy;
-                            ws = (int)i;
-                        }
-                        in = dy > dx;
-                    }
-                }
-                const unsigned bm = __ballot_sync(kFull, in);
-                if (in)
-                    lst[nb_ + __popc(bm & ((1u << lane) - 1u))] = (uint16_t)i;
-                nb_ += __popc(bm);
-            }
-            warp_argmax_lowslot(wv, ws);
-            __syncwarp();
-            float vv = -FLT_MAX;
-            int vs = -1;
-            for (int b = 0; b < nb_; b += 4)
-            {
-                const int idx = b + g;
+                const int j = b + g;
                 uint4 c[CPL];
-                if (idx < nb_)
-                    load_frag_smem<CPL>(c, cache + (uint32_t)wu[lst[idx]] * p.row_bytes, p.st.nchunks, gl);
+                const bool act = j < ngt;
+                if (act)
+                    load_frag_smem<CPL>(c, cache + (uint32_t)wu[ord[j]] * p.row_bytes, p.st.nchunks, gl);
                 else
                 {
 #pragma unroll
@@ -815,43 +932,57 @@ __global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
                 }
                 const float d = GroupDist<DT, CPL>::eval(xf, c, p.st.nchunks, gl);
                 if (lane == 0)
-                    pairs += (uint32_t)min(4, nb_ - b);
-                if (idx < nb_ && gl == 0)
+                    pairs += (unsigned long long)min(4, ngt - b);
+                const unsigned hit = __ballot_sync(kFull, act && gl == 0 && __fmul_rn(p.alpha, d) <= wd[ord[j]]);
+                if (hit)
                 {
-                    const int slot = lst[idx];
-                    const float dy = wd[slot];
-                    if (__fmul_rn(p.alpha, d) <= dy && (vs < 0 || dy > vv || (dy == vv && slot < vs)))
-                    {
-                        vv = dy;
-                        vs = slot;
-                    }
+                    vj = b + ((__ffs(hit) - 1) >> 3);
+                    break;
                 }
             }
-            warp_argmax_lowslot(vv, vs);
+            int slot = -1, pr = -1;
+            if (vj >= 0)
+            {
+                slot = ord[vj];
+                pr = vj;
+            }
+            else if (deg < C)
+            {
+                slot = (int)deg;
+                wdeg = deg + 1;
+            }
+            else if (nv > 0 && dx < wd[ord[0]])
+            {
+                slot = ord[0];
+                pr = 0;
+            }
+            if (slot < 0)
+                continue;
+            // new order: drop position pr, insert the slot at its key
+            const uint64_t kn = order_key(dx, (uint32_t)slot);
+            int pn = 0;
+            for (int b = 0; b < nv; b += 32)
+            {
+                const int j = b + lane;
+                pn += __popc(__ballot_sync(kFull, j < nv && j != pr && order_key(wd[ord[j]], ord[j]) < kn));
+            }
+            uint16_t *nord = ordb + (ob ^ 1) * ordstride;
+            for (int j = lane; j < nv; j += 32)
+            {
+                if (j == pr)
+                    continue;
+                const int j1 = j - ((pr >= 0 && j > pr) ? 1 : 0);
+                nord[j1 + (j1 >= pn ? 1 : 0)] = ord[j];
+            }
             if (lane == 0)
             {
-                const uint16_t ux = (uint16_t)(p.R + k);
-                if (vs >= 0)
-                {
-                    wid[vs] = x;
-                    wd[vs] = dx;
-                    wu[vs] = ux;
-                }
-                else if (deg < C)
-                {
-                    wid[deg] = x;
-                    wd[deg] = dx;
-                    wu[deg] = ux;
-                }
-                else if (ws >= 0 && dx < wv)
-                {
-                    wid[ws] = x;
-                    wd[ws] = dx;
-                    wu[ws] = ux;
-                }
+                nord[pn] = (uint16_t)slot;
+                wid[slot] = x;
+                wd[slot] = dx;
+                wu[slot] = (uint16_t)(p.R + k);
             }
-            if (vs < 0 && deg < C)
-                wdeg = deg + 1;
+            nv += (pr >= 0) ? 0 : 1;
+            ob ^= 1;
             __syncwarp();
         }
         for (uint32_t i = lane; i < C; i += 32)

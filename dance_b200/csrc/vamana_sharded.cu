@@ -206,7 +206,7 @@ DANCE_API int dance_vamana_build_sharded(DanceComm *comm, int dtype, const void 
         return rc;
     if (!d_graph || !d_degree || !d_table_degree)
         return fail(-1, "null graph buffers");
-    if (R == 0 || L == 0 || C == 0 || STEPS == 0 || C < R || C > 1024 || L > 1024)
+    if (R == 0 || L == 0 || C == 0 || STEPS == 0 || C < R || C > 1024 || L > (uint32_t)kMaxL)
         return fail(-1, "invalid parameters: R=%u L=%u C=%u STEPS=%u", R, L, C, STEPS);
     if (STEPS > L)
         STEPS = L;

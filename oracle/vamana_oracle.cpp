@@ -922,7 +922,7 @@ void oracle_default_params(DanceVamanaParams *p)
     p->reverse_heavy_cap = 0;
     p->reverse_heavy_threshold = 256;
     p->reverse_heavy_sample = 256;
-    p->visited_log2 = 11;
+    p->visited_log2 = 10;
 }
 
 void oracle_reset_counters(void)

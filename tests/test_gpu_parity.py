@@ -412,3 +412,22 @@ def test_kernel_launches_counted():
     x = make(np.uint8, 1000)
     _gpu_build(x, 16, 32, 24, 16)
     assert lib.dance_kernel_launch_count() > before
+
+
+def test_search_large_pool_and_degree():
+    # 8 pool entries per lane (L=256) and rows wider than one 64-candidate batch (R=96)
+    x = make(np.float32, 5000)
+    R, L, S = 96, 256, 80
+    m, ids, ds, deg = _round_inputs(x, R, 1, C=112, L=L, S=S)
+    ge, gd, gc = _gpu_search(x, R, L, S, m, ids, ds, deg, S)
+    oe, od, oc = oracle.search(x, R, L, S, m, 8, ids, ds, deg, S)
+    assert np.array_equal(gc, oc)
+    mask = np.arange(S)[None, :] < oc[:, None]
+    assert np.array_equal(ge[mask], oe[mask]) and np.array_equal(gd[mask], od[mask])
+
+
+def test_pool_capacity_limit_is_an_error():
+    from dance_b200 import DanceError
+    x = make(np.uint8, 500)
+    with pytest.raises(DanceError):
+        _gpu_build(x, 16, 300, 24, 16)
