@@ -113,6 +113,9 @@ SIGNATURES = {
     "dance_stage_prune": (_I, [_I, _P, _U64, _U32, _U32, _U32, _U32, _F, _U32, _P, _P, _P, _P, _P, _P, _P]),
     "dance_search_queries": (_I, [_I, _P, _U64, _U32, _U32, _P, _U32, _U32, _P, _U64, _U32, _U32, _U32, _U32, _P,
                                   _P, _P]),
+    "dance_merge_shards_gpu": (_I, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, _U64, _U32,
+                                    ctypes.c_char_p, ctypes.c_char_p]),
+    "dance_merge_edges_device": (_I, [_P, _P, _U64, _U32, _U32, _U32, _U64, _P, _P, _P]),
     "dance_shard_range": (None, [_U32, _I, _I, _PU32, _PU32, _PU32]),
     "dance_nccl_unique_id": (_I, [_P, ctypes.c_size_t]),
     "dance_comm_create": (_I, [_I, _I, _P, ctypes.c_size_t, ctypes.c_double, _P]),

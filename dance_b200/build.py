@@ -20,9 +20,9 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libdance_b200.so"
 
-SOURCES = ["vamana_build.cu", "vamana_sharded.cu"]
+SOURCES = ["vamana_build.cu", "vamana_sharded.cu", "gpu_merge.cu"]
 HEADERS = ["dance_common.cuh", "vamana_kernels.cuh", "host_common.cuh"]
-PUBLIC_HEADERS = ["dance_b200.h", "gpu_vamana_builder.h", "gpu_vamana_config.h"]
+PUBLIC_HEADERS = ["dance_b200.h", "gpu_vamana_builder.h", "gpu_vamana_config.h", "gpu_merge.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -157,6 +157,18 @@ DANCE_API int dance_vamana_build_sharded(DanceComm *comm, int dtype, const void 
                                          uint32_t *d_graph, uint32_t *d_degree, uint32_t *d_table_degree,
                                          uint32_t *medoid_out, void *stream);
 
+/* ---- shard merge (C form of diskann::merge_shards_gpu, include/gpu_merge.h) */
+DANCE_API int dance_merge_shards_gpu(const char *vamana_prefix, const char *vamana_suffix, const char *idmaps_prefix,
+                                     const char *idmaps_suffix, uint64_t nshards, uint32_t max_degree,
+                                     const char *output_vamana, const char *medoids_file);
+/* Device core of the merge for sources [node_begin, node_begin + node_count):
+ * edges (d_src[i] -> d_dst[i]) in global ids without self loops; writes
+ * each source's first max_degree distinct destinations in hash rank order
+ * to d_out_neighbors (node_count x max_degree) and d_out_degrees. */
+DANCE_API int dance_merge_edges_device(const uint32_t *d_src, const uint32_t *d_dst, uint64_t n_edges,
+                                       uint32_t node_begin, uint32_t node_count, uint32_t max_degree, uint64_t seed,
+                                       uint32_t *d_out_neighbors, uint32_t *d_out_degrees, void *stream);
+
 /* ---- query search over a built graph (recall harness) -------------------- */
 /* DiskANN-style best-first search from `start` with list size L_search; the
  * K nearest found per query go to d_out_ids / d_out_dists (nq x K). */

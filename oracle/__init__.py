@@ -28,6 +28,8 @@ _SIGS = {
     "oracle_distance": (_F, [_I, _P, _P, _U32]),
     "oracle_float_to_half": (None, [_P, _P, _U64]),
     "oracle_hash_u32": (_U32, [_U32]),
+    "oracle_hash_edge32": (_U32, [_U32, _U32, _U64]),
+    "oracle_merge_edges": (_I, [_P, _P, _U64, _U32, _U32, _U64, _P, _P]),
     "oracle_det_neighbor": (_U32, [_U32, _U32, _U32]),
     "oracle_medoid": (_U32, [_I, _P, _U64, _U32, _U32, _U32, _U32, _P, _P, _I]),
     "oracle_init": (_I, [_I, _P, _U64, _U32, _U32, _U32, _P, _P, _P, _I]),
@@ -222,6 +224,16 @@ def search_queries(data, graph, R, start, queries, L, K):
     load().oracle_search_queries(dt, _p(d), stride, n, dim, _p(np.ascontiguousarray(graph, np.uint32)), R, start,
                                  _p(q), qstride, nq, L, K, _p(ids), _p(ds), threads())
     return ids, ds
+
+
+def merge_edges(src, dst, nnodes, max_degree, seed=0x9e3779b97f4a7c15):
+    """Reference shard-merge rule on global edges -> (rows nnodes x max_degree, degrees)."""
+    src = np.ascontiguousarray(src, np.uint32)
+    dst = np.ascontiguousarray(dst, np.uint32)
+    rows = np.zeros((nnodes, max_degree), np.uint32)
+    deg = np.zeros(nnodes, np.uint32)
+    load().oracle_merge_edges(_p(src), _p(dst), len(src), nnodes, max_degree, seed, _p(rows), _p(deg))
+    return rows, deg
 
 
 def counters():

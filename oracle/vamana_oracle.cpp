@@ -968,6 +968,45 @@ void oracle_float_to_half(const float *src, uint16_t *dst, uint64_t n)
 }
 
 uint32_t oracle_hash_u32(uint32_t x) { return hash_u32(x); }
+
+// Shard-merge rank hash (reference src/gpu_merge.cu:92-101).
+uint32_t oracle_hash_edge32(uint32_t src, uint32_t dst, uint64_t seed)
+{
+    uint64_t x = ((uint64_t)src << 32) ^ (uint64_t)dst ^ seed;
+    x ^= x >> 33;
+    x *= 0xff51afd7ed558ccdULL;
+    x ^= x >> 33;
+    x *= 0xc4ceb9fe1a85ec53ULL;
+    x ^= x >> 33;
+    return (uint32_t)(x ^ (x >> 32));
+}
+
+// Merge of global edges (reference merge_shards_gpu pass 2, :586-731):
+// per source, distinct destinations other than itself, ranked by
+// (hash_edge32, destination), first max_degree kept.
+int oracle_merge_edges(const uint32_t *src, const uint32_t *dst, uint64_t n, uint32_t nnodes, uint32_t max_degree,
+                       uint64_t seed, uint32_t *out_rows, uint32_t *out_deg)
+{
+    std::vector<std::vector<uint32_t>> adj(nnodes);
+    for (uint64_t i = 0; i < n; ++i)
+        if (src[i] < nnodes && src[i] != dst[i])
+            adj[src[i]].push_back(dst[i]);
+    for (uint32_t v = 0; v < nnodes; ++v)
+    {
+        auto &a = adj[v];
+        std::sort(a.begin(), a.end());
+        a.erase(std::unique(a.begin(), a.end()), a.end());
+        std::vector<std::pair<uint32_t, uint32_t>> k;
+        for (uint32_t d : a)
+            k.emplace_back(oracle_hash_edge32(v, d, seed), d);
+        std::sort(k.begin(), k.end());
+        const uint32_t keep = std::min<uint32_t>((uint32_t)k.size(), max_degree);
+        out_deg[v] = keep;
+        for (uint32_t j = 0; j < max_degree; ++j)
+            out_rows[(size_t)v * max_degree + j] = j < keep ? k[j].second : kInvalid;
+    }
+    return 0;
+}
 uint32_t oracle_det_neighbor(uint32_t node, uint32_t k, uint32_t N) { return det_neighbor(node, k, N); }
 
 uint32_t oracle_medoid(int dtype, const void *data, uint64_t stride, uint32_t N, uint32_t dim, uint32_t nc,
