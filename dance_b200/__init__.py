@@ -73,6 +73,22 @@ class DanceBuildReport(ctypes.Structure):
         ("reserved", ctypes.c_uint64 * 3)]
 
 
+class DanceStitchedStats(ctypes.Structure):
+    """Mirror of ``DanceStitchedStats`` in include/dance_b200.h."""
+    _fields_ = [(n, ctypes.c_uint32) for n in (
+        "num_labels", "npts_per_label_min", "npts_per_label_max", "max_degree")] + [
+        ("npts_per_label_mean", ctypes.c_double)] + [(n, ctypes.c_uint64) for n in (
+            "total_label_memberships", "processed_label_memberships", "remap_invalid_local_ids", "remap_self_loops",
+            "remap_duplicate_edges", "output_edges")] + [(n, ctypes.c_double) for n in (
+                "label_data_materialization_seconds", "per_label_gpu_build_sum_seconds",
+                "per_label_gpu_build_max_seconds", "label_build_wall_seconds", "local_to_global_remap_seconds",
+                "total_seconds", "peak_gpu_mem_gb")] + [
+        ("streams", ctypes.c_uint32), ("reserved0", ctypes.c_uint32), ("reserved", ctypes.c_uint64 * 4)]
+
+    def as_dict(self) -> dict:
+        return {k: getattr(self, k) for k, _ in self._fields_ if not k.startswith("reserved")}
+
+
 _P = ctypes.c_void_p
 _U32 = ctypes.c_uint32
 _U64 = ctypes.c_uint64
@@ -116,6 +132,11 @@ SIGNATURES = {
     "dance_merge_shards_gpu": (_I, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, _U64, _U32,
                                     ctypes.c_char_p, ctypes.c_char_p]),
     "dance_merge_edges_device": (_I, [_P, _P, _U64, _U32, _U32, _U32, _U64, _P, _P, _P]),
+    "dance_stitched_build": (_I, [_I, _P, _U32, _U32, _U32, _P, _P, _U32, _U32, _U32, _U32, _U32, _P, _U32, _P, _P,
+                                  _U64, _P, _P]),
+    "dance_stitched_label_graphs": (_I, [_I, _P, _U64, _U32, _U32, _U32, _P, _P, _P, _U32, _U32, _U32, _U32, _P,
+                                         _U32, _P, _P, _P, _P]),
+    "dance_stitched_remap": (_I, [_U32, _U32, _P, _P, _P, _P, _U32, _U32, _P, _P, _U64, _P, _P]),
     "dance_shard_range": (None, [_U32, _I, _I, _PU32, _PU32, _PU32]),
     "dance_nccl_unique_id": (_I, [_P, ctypes.c_size_t]),
     "dance_comm_create": (_I, [_I, _I, _P, ctypes.c_size_t, ctypes.c_double, _P]),

@@ -20,7 +20,7 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libdance_b200.so"
 
-SOURCES = ["vamana_build.cu", "vamana_sharded.cu", "gpu_merge.cu"]
+SOURCES = ["vamana_build.cu", "vamana_sharded.cu", "gpu_merge.cu", "stitched.cu"]
 HEADERS = ["dance_common.cuh", "vamana_kernels.cuh", "host_common.cuh"]
 PUBLIC_HEADERS = ["dance_b200.h", "gpu_vamana_builder.h", "gpu_vamana_config.h", "gpu_merge.h"]
 

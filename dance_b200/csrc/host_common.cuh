@@ -343,6 +343,17 @@ inline StoreView make_view(const void *d_data, uint64_t stride, uint32_t N, uint
 
 inline uint32_t lcap_of(uint32_t L) { return (L + 31u) & ~31u; }
 
+// Float entry points store the vectors as fp16 when ENABLE_FLOAT16_BUILD is
+// set at build time, or DANCE_FLOAT16_BUILD=0|1 at run time (the run-time
+// variable wins), mirroring the reference's FAST profiles.
+inline bool float16_build_enabled()
+{
+    const char *e = std::getenv("DANCE_FLOAT16_BUILD");
+    if (e && *e)
+        return std::atoi(e) != 0;
+    return ENABLE_FLOAT16_BUILD != 0;
+}
+
 } // namespace dance
 
 using namespace dance;
@@ -491,5 +502,9 @@ struct StageTimes
 };
 
 // The whole build on resident vectors.  graph_out/dists_out/degree_out may
-// alias the workspace's own buffers.
+// alias the workspace's own buffers.  Defined in vamana_build.cu.
+int build_resident_impl(int dtype, const void *d_data, uint64_t stride, uint32_t N, uint32_t dim, uint32_t R,
+                        uint32_t L, uint32_t C, uint32_t STEPS, const DanceVamanaParams &prm, DanceWorkspace &ws,
+                        uint32_t *graph_out, uint32_t *degree_out, float *dists_out, uint32_t *medoid_out,
+                        cudaStream_t s, StageTimes *times, uint64_t *counters_out);
 } // namespace dance

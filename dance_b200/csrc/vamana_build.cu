@@ -33,10 +33,10 @@ thread_local char g_err[512] = "";
 std::atomic<uint64_t> g_launches{0};
 thread_local DanceBuildReport g_report;
 
-static int build_resident_impl(int dtype, const void *d_data, uint64_t stride, uint32_t N, uint32_t dim, uint32_t R,
-                               uint32_t L, uint32_t C, uint32_t STEPS, const DanceVamanaParams &prm,
-                               DanceWorkspace &ws, uint32_t *graph_out, uint32_t *degree_out, float *dists_out,
-                               uint32_t *medoid_out, cudaStream_t s, StageTimes *times, uint64_t *counters_out)
+int build_resident_impl(int dtype, const void *d_data, uint64_t stride, uint32_t N, uint32_t dim, uint32_t R,
+                        uint32_t L, uint32_t C, uint32_t STEPS, const DanceVamanaParams &prm, DanceWorkspace &ws,
+                        uint32_t *graph_out, uint32_t *degree_out, float *dists_out, uint32_t *medoid_out,
+                        cudaStream_t s, StageTimes *times, uint64_t *counters_out)
 {
     int rc = check_store(dtype, d_data, stride, N, dim);
     if (rc)
@@ -529,14 +529,6 @@ double now_sec()
     return std::chrono::duration<double>(std::chrono::steady_clock::now().time_since_epoch()).count();
 }
 
-bool float16_build()
-{
-    const char *e = std::getenv("DANCE_FLOAT16_BUILD");
-    if (e && *e)
-        return std::atoi(e) != 0;
-    return ENABLE_FLOAT16_BUILD != 0;
-}
-
 __global__ void f32_to_f16_rows(const float *src, uint32_t dim, __half *dst, uint64_t dst_stride_elems, uint64_t n)
 {
     for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
@@ -567,7 +559,7 @@ int host_build(int in_dtype, const void *h_data, uint32_t N, uint32_t dim, uint3
         fprintf(stderr, "[gpu_vamana_build] STEPS=%u is larger than L=%u, clamp STEPS to L.\n", STEPS, L);
         STEPS = L;
     }
-    const int store_dtype = (in_dtype == kF32 && float16_build()) ? kF16 : in_dtype;
+    const int store_dtype = (in_dtype == kF32 && float16_build_enabled()) ? kF16 : in_dtype;
     const int in_es = elem_size(in_dtype);
     const int st_es = elem_size(store_dtype);
     const uint64_t in_row = (uint64_t)dim * in_es;

@@ -169,6 +169,74 @@ DANCE_API int dance_merge_edges_device(const uint32_t *d_src, const uint32_t *d_
                                        uint32_t node_begin, uint32_t node_count, uint32_t max_degree, uint64_t seed,
                                        uint32_t *d_out_neighbors, uint32_t *d_out_degrees, void *stream);
 
+/* ---- GPU-StitchedVamana (apps/utils/gpu_stitched_vamana_index.cpp:241-428) */
+/* Labels are given as a CSR: label l (0-based here; the sidecar files number
+ * it l + 1) holds the points label_points[label_offsets[l] ..
+ * label_offsets[l + 1]), in the order the label file lists them.  Every
+ * label's points form one independent vnew2 graph (Rsmall, Lsmall, C,
+ * steps); a point's output row is the concatenation over its labels, in
+ * label order, of the first min(local degree, Rstitched) local neighbours
+ * mapped to global ids, skipping invalid ids and self loops and not
+ * repeating an id (:276-341).  Rstitched below Rsmall is raised to Rsmall,
+ * as the reference app does (:86-87).  The global label-aware prune that the
+ * reference runs for multi-label rows (:353-372) is not part of this call. */
+typedef struct DanceStitchedStats
+{
+    uint32_t num_labels;
+    uint32_t npts_per_label_min;
+    uint32_t npts_per_label_max;
+    uint32_t max_degree; /* largest output row */
+    double npts_per_label_mean;
+    uint64_t total_label_memberships;
+    uint64_t processed_label_memberships;
+    uint64_t remap_invalid_local_ids;
+    uint64_t remap_self_loops;
+    uint64_t remap_duplicate_edges;
+    uint64_t output_edges;
+    double label_data_materialization_seconds; /* upload + label-major gather */
+    double per_label_gpu_build_sum_seconds;    /* summed over labels */
+    double per_label_gpu_build_max_seconds;
+    double label_build_wall_seconds;           /* all labels, streams overlapped */
+    double local_to_global_remap_seconds;
+    double total_seconds;
+    double peak_gpu_mem_gb;
+    uint32_t streams; /* label builds in flight at once */
+    uint32_t reserved0;
+    uint64_t reserved[4];
+} DanceStitchedStats;
+
+/* Host in, host out.  dtype DANCE_U8 or DANCE_F32 (fp16 storage when the
+ * float build is configured so, as for gpu_vamana_vnew2_build_float).
+ * row_offsets has N + 1 entries; row_ids needs at most
+ * label_offsets[num_labels] * Rsmall entries (error -3 when
+ * row_ids_capacity is smaller than the result).  label_medoids[l] is the
+ * global id of label l's medoid.  streams = 0 picks 4. */
+DANCE_API int dance_stitched_build(int dtype, const void *h_data, uint32_t num_points, uint32_t dim,
+                                   uint32_t num_labels, const uint64_t *label_offsets, const uint32_t *label_points,
+                                   uint32_t r_small, uint32_t l_small, uint32_t r_stitched, uint32_t C,
+                                   uint32_t steps, const DanceVamanaParams *params, uint32_t streams,
+                                   uint64_t *row_offsets, uint32_t *row_ids, uint64_t row_ids_capacity,
+                                   uint32_t *label_medoids, DanceStitchedStats *stats);
+/* Device-resident first half, for label-parallel multi-GPU builds: builds
+ * the labels with label_mask[l] != 0 (all when label_mask is NULL) from the
+ * padded store d_data into d_local_graph (memberships x Rsmall, membership m
+ * of label l at row label_offsets[l] + local index) and d_local_degree, and
+ * writes label l's local medoid index to label_medoids_local[l] (host).  Rows
+ * and medoids of unselected labels are left untouched. */
+DANCE_API int dance_stitched_label_graphs(int dtype, const void *d_data, uint64_t row_stride_bytes,
+                                          uint32_t num_points, uint32_t dim, uint32_t num_labels,
+                                          const uint64_t *label_offsets, const uint32_t *label_points,
+                                          const uint8_t *label_mask, uint32_t r_small, uint32_t l_small, uint32_t C,
+                                          uint32_t steps, const DanceVamanaParams *params, uint32_t streams,
+                                          uint32_t *d_local_graph, uint32_t *d_local_degree,
+                                          uint32_t *label_medoids_local, DanceStitchedStats *stats);
+/* Second half: local graphs (device) to the stitched CSR graph (host). */
+DANCE_API int dance_stitched_remap(uint32_t num_points, uint32_t num_labels, const uint64_t *label_offsets,
+                                   const uint32_t *label_points, const uint32_t *d_local_graph,
+                                   const uint32_t *d_local_degree, uint32_t r_small, uint32_t r_stitched,
+                                   uint64_t *row_offsets, uint32_t *row_ids, uint64_t row_ids_capacity,
+                                   DanceStitchedStats *stats, void *stream);
+
 /* ---- query search over a built graph (recall harness) -------------------- */
 /* DiskANN-style best-first search from `start` with list size L_search; the
  * K nearest found per query go to d_out_ids / d_out_dists (nq x K). */

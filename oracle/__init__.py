@@ -245,3 +245,45 @@ def counters():
 
 def reset_counters():
     load().oracle_reset_counters()
+
+
+def stitched_remap(rows, ids, local_graph, local_degree, r_small, r_out, counters):
+    """One label's rows appended to the global rows by the reference rule
+    (apps/utils/gpu_stitched_vamana_index.cpp:316-341): the first
+    min(deg, Rstitched) local neighbours, invalid ids and self loops skipped,
+    ids already in the row not repeated."""
+    n = len(ids)
+    for i in range(n):
+        row = rows[ids[i]]
+        deg = min(int(local_degree[i]), r_out)
+        for j in range(deg):
+            nb = int(local_graph[i * r_small + j]) if local_graph.ndim == 1 else int(local_graph[i, j])
+            if nb == 0xFFFFFFFF or nb >= n:
+                counters["remap_invalid_local_ids"] += 1
+                continue
+            if ids[nb] == ids[i]:
+                counters["remap_self_loops"] += 1
+                continue
+            g = int(ids[nb])
+            if g not in row:
+                row.append(g)
+            else:
+                counters["remap_duplicate_edges"] += 1
+
+
+def stitched(data, label_points, r_small, l_small, r_out, C, steps, prm=None):
+    """Reference label loop (:276-341) over oracle builds of each label's
+    points; returns (rows: list of lists, label medoids, counters)."""
+    r_out = max(r_out, r_small)
+    rows = [[] for _ in range(data.shape[0])]
+    medoids = []
+    counters = dict(remap_invalid_local_ids=0, remap_self_loops=0, remap_duplicate_edges=0)
+    for ids in label_points:
+        ids = [int(i) for i in ids]
+        if not ids:
+            medoids.append(0)
+            continue
+        g, deg, _, med = build_graph(np.ascontiguousarray(data[ids]), r_small, l_small, C, steps, prm)
+        medoids.append(ids[med] if med < len(ids) else ids[0])
+        stitched_remap(rows, ids, g, deg, r_small, r_out, counters)
+    return rows, medoids, counters
