@@ -132,6 +132,7 @@ SIGNATURES = {
     "dance_merge_shards_gpu": (_I, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, _U64, _U32,
                                     ctypes.c_char_p, ctypes.c_char_p]),
     "dance_merge_edges_device": (_I, [_P, _P, _U64, _U32, _U32, _U32, _U64, _P, _P, _P]),
+    "dance_merge_edges_device_noalloc": (_I, [_P, _P, _U64, _U32, _U32, _U32, _U64, _P, _P, _P]),
     "dance_stitched_build": (_I, [_I, _P, _U32, _U32, _U32, _P, _P, _U32, _U32, _U32, _U32, _U32, _P, _U32, _P, _P,
                                   _U64, _P, _P]),
     "dance_stitched_label_graphs": (_I, [_I, _P, _U64, _U32, _U32, _U32, _P, _P, _P, _U32, _U32, _U32, _U32, _P,

@@ -333,6 +333,133 @@ extern "C" DANCE_API int dance_merge_edges_device(const uint32_t *d_src, const u
                                d_out_degrees, as_stream(stream));
 }
 
+// ---------------------------------------------------------------- no-alloc variant
+// dance_merge_edges_device_noalloc runs the same kernels as
+// dance_merge_edges_device, but its scratch (per-source counts, offsets and
+// cursors, scan tile sums, the long-segment list, two status words and the
+// source-sorted edge array) lives in one fixed array in the library's device
+// memory instead of buffers allocated per call.  The array holds
+// kNoAllocMaxNodes sources and kNoAllocMaxEdges edges, about 4.3 MiB; larger
+// requests are refused before anything is launched.
+namespace dance
+{
+constexpr uint32_t kNoAllocMaxNodes = 16384;
+constexpr uint32_t kNoAllocMaxEdges = 1u << 20;
+constexpr uint32_t kNoAllocTiles = (kNoAllocMaxNodes + kScanTile - 1) / kScanTile;
+
+constexpr uint32_t na_align(uint32_t words) { return (words + 63u) & ~63u; } // 256-byte sub-buffers
+constexpr uint32_t kNaCnt = 0;
+constexpr uint32_t kNaOff = kNaCnt + na_align(kNoAllocMaxNodes);
+constexpr uint32_t kNaCursor = kNaOff + na_align(kNoAllocMaxNodes + 1);
+constexpr uint32_t kNaTiles = kNaCursor + na_align(kNoAllocMaxNodes);
+constexpr uint32_t kNaLong = kNaTiles + na_align(kNoAllocTiles + 1);
+constexpr uint32_t kNaMisc = kNaLong + na_align(kNoAllocMaxNodes);
+constexpr uint32_t kNaSeg = kNaMisc + na_align(4);
+constexpr uint32_t kNaWords = kNaSeg + na_align(kNoAllocMaxEdges);
+
+static __device__ __align__(256) uint32_t g_merge_noalloc_scratch[kNaWords];
+
+// Address of this device's copy of the scratch array, looked up once per
+// device (cudaGetSymbolAddress loads the module on first use).
+static int merge_noalloc_scratch(uint32_t **out)
+{
+    static std::mutex mu;
+    static uint32_t *addr[64] = {};
+    int dev = 0;
+    DANCE_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64)
+        return fail(-1, "device ordinal %d out of range for the merge scratch table", dev);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[dev])
+    {
+        void *p = nullptr;
+        DANCE_CUDA(cudaGetSymbolAddress(&p, g_merge_noalloc_scratch));
+        addr[dev] = static_cast<uint32_t *>(p);
+    }
+    *out = addr[dev];
+    return 0;
+}
+
+static int merge_bucket_noalloc(const uint32_t *d_src, const uint32_t *d_dst, uint64_t n_edges, uint32_t begin,
+                                uint32_t count, uint32_t max_degree, uint64_t seed, uint32_t *d_out_neighbors,
+                                uint32_t *d_out_degrees, cudaStream_t s)
+{
+    if (count == 0)
+        return 0;
+    uint32_t *base = nullptr;
+    int rc = merge_noalloc_scratch(&base);
+    if (rc)
+        return rc;
+    uint32_t *cnt = base + kNaCnt, *off = base + kNaOff, *cursor = base + kNaCursor, *tiles = base + kNaTiles;
+    uint32_t *longl = base + kNaLong, *misc = base + kNaMisc, *seg = base + kNaSeg;
+    const uint32_t ntiles = (count + kScanTile - 1) / kScanTile;
+    // The counts and the two status words (long-segment count, error) must
+    // start at zero; everything else is written before it is read.
+    DANCE_CUDA(cudaMemsetAsync(cnt, 0, (uint64_t)count * 4, s));
+    DANCE_CUDA(cudaMemsetAsync(misc, 0, 16, s));
+    const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((n_edges + 255) / 256, sm_count() * 16ull));
+    if (n_edges)
+    {
+        mrg_count_kernel<<<grid, 256, 0, s>>>(d_src, n_edges, begin, count, cnt);
+        DANCE_LAUNCHED();
+    }
+    scan_tile_sums_kernel<<<ntiles, kScanThreads, 0, s>>>(cnt, count, tiles);
+    DANCE_LAUNCHED();
+    scan_tile_offsets_kernel<<<1, kScanThreads, 0, s>>>(tiles, ntiles);
+    DANCE_LAUNCHED();
+    scan_apply_kernel<<<ntiles, kScanThreads, 0, s>>>(cnt, count, tiles, off, cursor);
+    DANCE_LAUNCHED();
+    if (n_edges)
+    {
+        mrg_fill_kernel<<<grid, 256, 0, s>>>(d_src, d_dst, n_edges, begin, count, cursor, seg);
+        DANCE_LAUNCHED();
+    }
+    MergeSelectParams mp{};
+    mp.offsets = off;
+    mp.seg = seg;
+    mp.begin = begin;
+    mp.count = count;
+    mp.max_degree = max_degree;
+    mp.seed = seed;
+    mp.out_neighbors = d_out_neighbors;
+    mp.out_degrees = d_out_degrees;
+    mp.long_list = longl;
+    mp.long_count = misc;
+    mp.error = misc + 1;
+    int per_sm = 0;
+    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, mrg_select_kernel, 128, 0);
+    const int g2 = (int)std::max<uint64_t>(1, std::min<uint64_t>((count + 3) / 4, (uint64_t)std::max(per_sm, 1) *
+                                                                                       sm_count()));
+    mrg_select_kernel<<<g2, 128, 0, s>>>(mp);
+    DANCE_LAUNCHED();
+    const size_t lsmem = 12u * kMergeBlockCap;
+    DANCE_CUDA(allow_smem(mrg_select_long_kernel, lsmem));
+    mrg_select_long_kernel<<<sm_count(), 256, lsmem, s>>>(mp);
+    DANCE_LAUNCHED();
+    uint32_t err = 0;
+    DANCE_CUDA(cudaMemcpyAsync(&err, mp.error, 4, cudaMemcpyDeviceToHost, s));
+    DANCE_CUDA(cudaStreamSynchronize(s));
+    if (err)
+        return fail(-20, "a source has %u merged edges, more than the %u supported per source", err, kMergeBlockCap);
+    return 0;
+}
+} // namespace dance
+
+extern "C" DANCE_API int dance_merge_edges_device_noalloc(const uint32_t *d_src, const uint32_t *d_dst,
+                                                          uint64_t n_edges, uint32_t node_begin, uint32_t node_count,
+                                                          uint32_t max_degree, uint64_t seed,
+                                                          uint32_t *d_out_neighbors, uint32_t *d_out_degrees,
+                                                          void *stream)
+{
+    if ((n_edges && (!d_src || !d_dst)) || !d_out_neighbors || !d_out_degrees || max_degree == 0)
+        return fail(-1, "invalid merge arguments");
+    if (node_count > kNoAllocMaxNodes || n_edges > kNoAllocMaxEdges)
+        return fail(-5, "no-alloc merge holds at most %u sources and %u edges (asked for %u and %llu)",
+                    kNoAllocMaxNodes, kNoAllocMaxEdges, node_count, (unsigned long long)n_edges);
+    return merge_bucket_noalloc(d_src, d_dst, n_edges, node_begin, node_count, max_degree, seed, d_out_neighbors,
+                                d_out_degrees, as_stream(stream));
+}
+
 namespace
 {
 struct ShardMeta

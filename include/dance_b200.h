@@ -168,6 +168,25 @@ DANCE_API int dance_merge_shards_gpu(const char *vamana_prefix, const char *vama
 DANCE_API int dance_merge_edges_device(const uint32_t *d_src, const uint32_t *d_dst, uint64_t n_edges,
                                        uint32_t node_begin, uint32_t node_count, uint32_t max_degree, uint64_t seed,
                                        uint32_t *d_out_neighbors, uint32_t *d_out_degrees, void *stream);
+/* Same merge and same results as dance_merge_edges_device, without any
+ * device allocation.  No counterpart in the reference: its merge always
+ * allocates.  For callers that cannot allocate device memory on this path:
+ * a process whose memory is owned by another allocator (a framework's
+ * caching pool that has reserved the free memory, so cudaMalloc fails), or a
+ * loop that keeps other streams busy, where cudaMalloc/cudaFree would stall
+ * them because cudaFree waits for the whole device.
+ * Scratch is one fixed array in the library's device memory (about 4.3 MiB
+ * per device): at most 16384 sources (node_count) and 1048576 edges
+ * (n_edges); larger requests return -5 before any work is issued.  The
+ * first call on a device looks the array up (cudaGetSymbolAddress); if the
+ * calls are to be made inside stream capture, make one call on that device
+ * before capture begins.  All calls on one device share the array, so calls
+ * that overlap in time (from several host threads, or on several streams)
+ * race on it and give wrong results: run them one after another. */
+DANCE_API int dance_merge_edges_device_noalloc(const uint32_t *d_src, const uint32_t *d_dst, uint64_t n_edges,
+                                               uint32_t node_begin, uint32_t node_count, uint32_t max_degree,
+                                               uint64_t seed, uint32_t *d_out_neighbors, uint32_t *d_out_degrees,
+                                               void *stream);
 
 /* ---- GPU-StitchedVamana (apps/utils/gpu_stitched_vamana_index.cpp:241-428) */
 /* Labels are given as a CSR: label l (0-based here; the sidecar files number
