@@ -54,6 +54,9 @@ def parse():
     ap.add_argument("--no-recall", action="store_true")
     ap.add_argument("--ref-gpu", action="store_true",
                     help="also time the reference's own GPU builder (oracle/_ref, sm_100a) once on the workload")
+    ap.add_argument("--workload", choices=["cfg1_u8_10M", "cfg3_stitched"], default="cfg1_u8_10M",
+                    help="cfg1_u8_10M: the headline standard build; cfg3_stitched: the per-label stitched build "
+                         "of BASELINE.json configs[3]")
     return ap.parse_args()
 
 
@@ -506,8 +509,319 @@ def run_sharded(args):
     return 0
 
 
+# ------------------------------------------------------------------ stitched
+STITCHED = dict(name="cfg3_stitched_f32_1M", N=1_000_000, dim=96, centroids=1000, sigma=0.3, labels=100,
+                r_small=32, l_small=100, r_stitched=64, C=96, steps=64, alpha=1.2, seed=42, queries=10_000)
+STITCHED_CPU_SAMPLE = 20_000  # label memberships built by the oracle for cpu_baseline
+
+
+def stitched_inputs(n):
+    import numpy as np
+    from dance_b200 import stitched, workloads
+    x = workloads.gaussian_mixture_f32(n, STITCHED["dim"], STITCHED["centroids"], STITCHED["sigma"],
+                                       seed=STITCHED["seed"], device="cuda")
+    assign = workloads.zipf_partition_labels(n, STITCHED["labels"], seed=STITCHED["seed"])
+    label_points = stitched.labels_from_assignment(assign, STITCHED["labels"])
+    offs, pts = stitched.labels_csr(label_points)
+    return x, assign, label_points, offs, pts
+
+
+def stitched_recall(x, store, stride, assign, offs, pts, row_offsets, row_ids, medoids):
+    """Recall@10 at L=100 of single-label queries searched from their label's
+    medoid; every stitched edge stays inside its label, so the unfiltered
+    beam search is the filtered one.  Ground truth: brute force inside the label."""
+    import numpy as np
+    import torch
+    from dance_b200 import vamana, workloads
+    nq = STITCHED["queries"]
+    q = workloads.gaussian_mixture_f32(nq, STITCHED["dim"], STITCHED["centroids"], STITCHED["sigma"],
+                                       seed=STITCHED["seed"], device="cuda", stream_offset=1)
+    qlab = workloads.zipf_partition_labels(nq, STITCHED["labels"], seed=STITCHED["seed"] + 1)
+    n = x.shape[0]
+    deg = np.diff(row_offsets.astype(np.int64))
+    R = int(deg.max())
+    padded = np.full((n, R), 0xFFFFFFFF, np.uint32)
+    mask = np.arange(R)[None, :] < deg[:, None]
+    padded[mask] = row_ids
+    g = torch.from_numpy(padded.view(np.int32)).cuda()
+    hits = 0
+    for l in range(len(offs) - 1):
+        qi = np.nonzero(qlab == l)[0]
+        if len(qi) == 0:
+            continue
+        members = torch.from_numpy(pts[int(offs[l]):int(offs[l + 1])].astype(np.int64)).cuda()
+        ql = q[torch.from_numpy(qi).cuda()]
+        gt_local, _ = workloads.brute_force_knn(x[members], ql, 10)
+        gt = members[gt_local.long()].cpu().numpy()
+        ids, _ = vamana.search_queries(store, STITCHED["dim"], stride, g, R, int(medoids[l]), ql, 100, 10)
+        ids = ids.cpu().numpy()
+        hits += sum(len(set(a.tolist()) & set(b.tolist())) for a, b in zip(ids, gt))
+    return hits / (nq * 10)
+
+
+def reference_gpu_stitched(hx, label_points):
+    """The reference app's label loop (apps/utils/gpu_stitched_vamana_index.cpp:276-341):
+    per label, host gather, gpu_vamana_vnew2_build_float of the reference's
+    own library (DANCE src/gpu_vamana_vnew2.cu built for sm_100a, QUALITY
+    profile), medoid; remap done here with numpy.  Times the per-label build
+    calls and the host gathers like the app's timing keys."""
+    import numpy as np
+    lib_path = ROOT / "oracle" / "_ref" / "libref_vnew2_quality.so"
+    if not lib_path.exists():
+        return {"unavailable": f"{lib_path.name} not built"}
+    lib = ctypes.CDLL(str(lib_path))
+    f = lib.gpu_vamana_vnew2_build_float
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.c_void_p] + [ctypes.c_uint32] * 6 + [ctypes.c_void_p] * 2
+    lib.gpu_vamana_vnew2_get_last_medoid.restype = ctypes.c_uint32
+    rs, ls, C, st = STITCHED["r_small"], STITCHED["l_small"], STITCHED["C"], STITCHED["steps"]
+    n, dim = hx.shape
+    point_of, counts, flats = [], [], []
+    medoids = []
+    build_s = mat_s = 0.0
+    t0 = time.perf_counter()
+    for ids in label_points:
+        ids = np.asarray(ids, dtype=np.int64)
+        tm = time.perf_counter()
+        local = np.ascontiguousarray(hx[ids])
+        mat_s += time.perf_counter() - tm
+        g = np.full((len(ids), rs), 0xFFFFFFFF, np.uint32)
+        d = np.zeros(len(ids), np.uint32)
+        tb = time.perf_counter()
+        rc = f(ctypes.c_void_p(local.ctypes.data), len(ids), dim, rs, ls, C, st, ctypes.c_void_p(g.ctypes.data),
+               ctypes.c_void_p(d.ctypes.data))
+        build_s += time.perf_counter() - tb
+        if rc != 0:
+            return {"unavailable": f"reference build returned {rc}"}
+        med = int(lib.gpu_vamana_vnew2_get_last_medoid())
+        medoids.append(int(ids[med if med < len(ids) else 0]))
+        # remap (single-label rows: no duplicates across labels), vectorised
+        k = np.minimum(d, STITCHED["r_stitched"]).astype(np.int64)
+        valid = ((np.arange(rs)[None, :] < k[:, None]) & (g < len(ids))
+                 & (g != np.arange(len(ids), dtype=np.uint32)[:, None]))
+        point_of.append(ids)
+        counts.append(valid.sum(1))
+        flats.append(ids[g[valid].astype(np.int64)])
+    total = time.perf_counter() - t0
+    point_of = np.concatenate(point_of)
+    counts = np.concatenate(counts).astype(np.int64)
+    flat = np.concatenate(flats).astype(np.uint32)
+    src_start = np.concatenate([[0], np.cumsum(counts)[:-1]])
+    order = np.argsort(point_of, kind="stable")
+    offs = np.zeros(n + 1, np.uint64)
+    per_point = np.zeros(n, np.int64)
+    per_point[point_of] = counts
+    np.cumsum(per_point, out=offs[1:])
+    c_sorted = counts[order]
+    gather = np.repeat(src_start[order] - np.concatenate([[0], np.cumsum(c_sorted)[:-1]]), c_sorted) + np.arange(
+        int(c_sorted.sum()))
+    return {"rows": (offs, flat[gather]), "medoids": medoids,
+            "per_label_gpu_build_sum_seconds": build_s, "label_data_materialization_seconds": mat_s,
+            "loop_seconds": total, "e2e_vectors_per_s": n / total,
+            "build": "DANCE vnew2 QUALITY profile via gpu_vamana_vnew2_build_float, nvcc 12.9 sm_100a"}
+
+
+def run_stitched(args):
+    import numpy as np
+    import torch
+    import dance_b200
+    from dance_b200 import stitched, vamana
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    lib = dance_b200.load()
+    n = args.n if args.n != WORKLOAD["N"] else STITCHED["N"]
+    rs, ls, rst, C, steps = (STITCHED[k] for k in ("r_small", "l_small", "r_stitched", "C", "steps"))
+    x, assign, label_points, offs, pts = stitched_inputs(n)
+    store, stride = vamana.padded_store(x)
+    dim = STITCHED["dim"]
+    M = int(offs[-1])
+    nl = len(offs) - 1
+    prm = dance_b200.default_params()
+    lgraph = torch.zeros(M * rs, dtype=torch.int32, device="cuda")
+    ldeg = torch.zeros(M, dtype=torch.int32, device="cuda")
+    med_local = np.zeros(nl, np.uint32)
+    row_offsets = np.zeros(n + 1, np.uint64)
+    row_ids = np.zeros(M * rs, np.uint32)
+    P = stitched._ptr
+
+    def one_step():
+        st = dance_b200.DanceStitchedStats()
+        rc = lib.dance_stitched_label_graphs(dance_b200.DANCE_F32, P(store), stride, n, dim, nl, P(offs), P(pts),
+                                             None, rs, ls, C, steps, ctypes.byref(prm), 4, P(lgraph), P(ldeg),
+                                             P(med_local), ctypes.byref(st))
+        dance_b200.check(rc, "dance_stitched_label_graphs")
+        st2 = dance_b200.DanceStitchedStats()
+        rc = lib.dance_stitched_remap(n, nl, P(offs), P(pts), P(lgraph), P(ldeg), rs, rst, P(row_offsets),
+                                      P(row_ids), M * rs, ctypes.byref(st2), None)
+        dance_b200.check(rc, "dance_stitched_remap")
+        return st, st2
+
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    launches0 = lib.dance_kernel_launch_count()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    stats = []
+    ev0.record()
+    for _ in range(args.steps):
+        stats.append(one_step())
+    ev1.record()
+    torch.cuda.synchronize()
+    launches = lib.dance_kernel_launch_count() - launches0
+    clk = clocks.stop()
+    elapsed = ev0.elapsed_time(ev1) * 1e-3
+    medoids = [int(pts[int(offs[l]) + int(med_local[l])]) for l in range(nl)]
+    peak, peak_kind = measured_peaks()
+    rep = {"search_evals": sum(a.search_evals for a, _ in stats), "expansions": sum(a.search_expansions
+                                                                                   for a, _ in stats)}
+    alg = search_algorithmic_bytes(rep, M * len(stats), stride, rs, 4)
+    ksec = sum(a.search_kernel_seconds for a, _ in stats)
+    launches_per_step = 4 * nl
+    achieved = alg / ksec / 1e9
+    s0, s1 = stats[-1]
+    line = {
+        "metric": "stitched_build_vectors_per_s", "value": n * args.steps / elapsed, "unit": "vectors/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded GPU generator, BASELINE.json configs[3] recipe)",
+        "config": {"workload": STITCHED["name"], "N": n, "dim": dim, "labels": nl, "Rsmall": rs, "Lsmall": ls,
+                   "Rstitched": rst, "C": C, "steps": steps, "alpha": STITCHED["alpha"], "seed": STITCHED["seed"],
+                   "label_sizes": {"min": s0.npts_per_label_min, "max": s0.npts_per_label_max},
+                   "l2": "inputs larger than L2 (384 MB vectors + label-major copy), no flush",
+                   "timed": "dance_stitched_label_graphs (device-resident store) + dance_stitched_remap"},
+        "roofline": {"kernel": "search_kernel", "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_source": peak_kind, "traffic": None,
+                     "algorithmic_bytes_per_launch": alg / (len(stats) * launches_per_step),
+                     "avg_launch_ms": ksec / (len(stats) * launches_per_step) * 1e3,
+                     "note": "label builds overlap on 4 streams, so launch durations overlap"},
+        "gpu_launches": int(launches),
+        "clocks": clk,
+        "stage_seconds": {"label_build_wall": s0.label_build_wall_seconds,
+                          "per_label_build_sum": s0.per_label_gpu_build_sum_seconds,
+                          "per_label_build_max": s0.per_label_gpu_build_max_seconds,
+                          "gather": s0.label_data_materialization_seconds,
+                          "remap": s1.local_to_global_remap_seconds},
+        "graph": {"edges": int(s1.output_edges), "max_degree": int(s1.max_degree),
+                  "remap_invalid_local_ids": int(s1.remap_invalid_local_ids),
+                  "remap_self_loops": int(s1.remap_self_loops),
+                  "remap_duplicate_edges": int(s1.remap_duplicate_edges)},
+    }
+    hx = x.cpu().numpy()
+    if not args.no_e2e:
+        hxp = torch.from_numpy(hx).pin_memory()
+        e_off = np.zeros(n + 1, np.uint64)
+        e_ids = np.zeros(M * rs, np.uint32)
+        e_med = np.zeros(nl, np.uint32)
+
+        def e2e_call():
+            st = dance_b200.DanceStitchedStats()
+            rc = lib.dance_stitched_build(dance_b200.DANCE_F32, ctypes.c_void_p(hxp.data_ptr()), n, dim, nl, P(offs),
+                                          P(pts), rs, ls, rst, C, steps, ctypes.byref(prm), 4, P(e_off), P(e_ids),
+                                          M * rs, P(e_med), ctypes.byref(st))
+            dance_b200.check(rc, "dance_stitched_build")
+
+        e2e_call()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e2e_call()
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        line["e2e"] = {"value": n * args.steps / dt, "unit": "vectors/s", "h2d_bytes_per_step": int(hx.nbytes + pts.nbytes
+                                                                                                    + offs.nbytes),
+                       "d2h_bytes_per_step": int(e_off.nbytes + 4 * int(e_off[-1]) + e_med.nbytes),
+                       "api": "dance_stitched_build (host in, host CSR out), pinned vectors, wall clock",
+                       "matches_resident_path": bool(np.array_equal(e_off, row_offsets)
+                                                     and np.array_equal(e_ids[:int(e_off[-1])],
+                                                                        row_ids[:int(row_offsets[-1])])
+                                                     and e_med.tolist() == medoids)}
+    E = int(row_offsets[-1])
+    if not args.no_recall:
+        line["recall_at_10"] = {"L_search": 100, "queries": STITCHED["queries"],
+                                "ours": stitched_recall(x, store, stride, assign, offs, pts, row_offsets,
+                                                        row_ids[:E], medoids)}
+    if not args.no_cpu_baseline:
+        import oracle
+        # smallest labels first until the sample holds STITCHED_CPU_SAMPLE memberships
+        sizes = np.diff(offs.astype(np.int64))
+        chosen, tot = [], 0
+        for l in np.argsort(sizes, kind="stable"):
+            if tot >= STITCHED_CPU_SAMPLE:
+                break
+            chosen.append(int(l))
+            tot += int(sizes[l])
+        threads = os.cpu_count() or 1
+        t0 = time.perf_counter()
+        oracle.stitched(hx, [label_points[l] for l in chosen], rs, ls, rst, C, steps)
+        secs = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": tot / secs, "unit": "vectors/s", "cores": threads, "kind": "port",
+                                "sample": f"the {len(chosen)} smallest labels ({tot} points), per-label builds and "
+                                          f"remap ({secs:.1f} s)"}
+    if args.ref_gpu:
+        ref = reference_gpu_stitched(hx, label_points)
+        if "rows" in ref:
+            roffs, rids = ref.pop("rows")
+            ref["recall_at_10"] = stitched_recall(x, store, stride, assign, offs, pts, roffs, rids, ref["medoids"])
+            ref["graph_equals_ours"] = bool(np.array_equal(roffs, row_offsets) and np.array_equal(rids,
+                                                                                               row_ids[:E]))
+            ref["medoids_equal_ours"] = ref.pop("medoids") == medoids
+        line["reference_gpu"] = ref
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_stitched_reference(args, n):
+    """--impl reference for the stitched workload: the oracle port of the
+    app's label loop on the host cores, a bounded sample (smallest labels
+    first) per step."""
+    import numpy as np
+    import oracle
+    from dance_b200 import stitched, workloads
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    x = workloads.gaussian_mixture_f32(n, STITCHED["dim"], STITCHED["centroids"], STITCHED["sigma"],
+                                       seed=STITCHED["seed"], device="cpu").numpy()
+    assign = workloads.zipf_partition_labels(n, STITCHED["labels"], seed=STITCHED["seed"])
+    label_points = stitched.labels_from_assignment(assign, STITCHED["labels"])
+    sizes = np.array([len(p) for p in label_points])
+    chosen, tot = [], 0
+    for l in np.argsort(sizes, kind="stable"):
+        if tot >= STITCHED_CPU_SAMPLE:
+            break
+        chosen.append(int(l))
+        tot += int(sizes[l])
+    sample = [label_points[l] for l in chosen]
+    args_t = (STITCHED["r_small"], STITCHED["l_small"], STITCHED["r_stitched"], STITCHED["C"], STITCHED["steps"])
+    for _ in range(args.warmup):
+        oracle.stitched(x, sample[:1], *args_t)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.stitched(x, sample, *args_t)
+    dt = time.perf_counter() - t0
+    v = tot * args.steps / dt
+    threads = os.cpu_count() or 1
+    print(json.dumps({
+        "impl": "reference", "metric": "stitched_build_vectors_per_s", "value": v, "unit": "vectors/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (BASELINE.json configs[3] recipe)",
+        "config": {"workload": STITCHED["name"], "N": n, "labels": STITCHED["labels"]},
+        "cpu_baseline": {"value": v, "unit": "vectors/s", "cores": threads, "kind": "port",
+                         "sample": f"the {len(chosen)} smallest labels ({tot} points) per step"},
+        "e2e": {"value": v, "unit": "vectors/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}), flush=True)
+    return 0
+
+
 def main():
     args = parse()
+    if args.workload == "cfg3_stitched":
+        if args.impl == "reference":
+            return run_stitched_reference(args, args.n if args.n != WORKLOAD["N"] else STITCHED["N"])
+        return run_stitched(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

@@ -82,7 +82,8 @@ class DanceStitchedStats(ctypes.Structure):
             "remap_duplicate_edges", "output_edges")] + [(n, ctypes.c_double) for n in (
                 "label_data_materialization_seconds", "per_label_gpu_build_sum_seconds",
                 "per_label_gpu_build_max_seconds", "label_build_wall_seconds", "local_to_global_remap_seconds",
-                "total_seconds", "peak_gpu_mem_gb")] + [
+                "total_seconds", "peak_gpu_mem_gb", "search_kernel_seconds")] + [
+        ("search_evals", ctypes.c_uint64), ("search_expansions", ctypes.c_uint64),
         ("streams", ctypes.c_uint32), ("reserved0", ctypes.c_uint32), ("reserved", ctypes.c_uint64 * 4)]
 
     def as_dict(self) -> dict:

@@ -224,7 +224,8 @@ struct Worker
 {
     int rc = 0;
     std::string err;
-    double busy = 0, max_label = 0;
+    double busy = 0, max_label = 0, search_kernel = 0;
+    uint64_t search_evals = 0, expansions = 0;
 };
 
 // Builds every selected label's graph into the label-major arrays.
@@ -298,6 +299,9 @@ int build_label_graphs(int dtype, const uint8_t *d_seg, uint64_t stride, uint32_
                 const double dt = wall() - lt0;
                 w.busy += dt;
                 w.max_label = std::max(w.max_label, dt);
+                w.search_kernel += tm.search_kernel;
+                w.search_evals += ctr[0];
+                w.expansions += ctr[1];
                 label_medoids_local[l] = med < n ? med : 0u;
             }
             cudaStreamDestroy(s);
@@ -316,6 +320,9 @@ int build_label_graphs(int dtype, const uint8_t *d_seg, uint64_t stride, uint32_
         {
             st->per_label_gpu_build_sum_seconds += w.busy;
             st->per_label_gpu_build_max_seconds = std::max(st->per_label_gpu_build_max_seconds, w.max_label);
+            st->search_kernel_seconds += w.search_kernel;
+            st->search_evals += w.search_evals;
+            st->search_expansions += w.expansions;
         }
         st->streams = nthreads;
         size_t fr = 0, tot = 0;

@@ -219,6 +219,9 @@ typedef struct DanceStitchedStats
     double local_to_global_remap_seconds;
     double total_seconds;
     double peak_gpu_mem_gb;
+    double search_kernel_seconds; /* GreedySearch kernel time summed over labels */
+    uint64_t search_evals;        /* GreedySearch distance evaluations, all labels */
+    uint64_t search_expansions;
     uint32_t streams; /* label builds in flight at once */
     uint32_t reserved0;
     uint64_t reserved[4];
