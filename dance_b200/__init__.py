@@ -73,6 +73,39 @@ class DanceBuildReport(ctypes.Structure):
         ("reserved", ctypes.c_uint64 * 3)]
 
 
+class GPUFilteredVamanaStats(ctypes.Structure):
+    """Mirror of ``GPUFilteredVamanaStats`` in include/gpu_vamana_filtered.h."""
+    _fields_ = ([(n, ctypes.c_double) for n in (
+        "gpu_build_seconds", "label_h2d_seconds", "graph_build_seconds", "diagnostics_seconds", "d2h_seconds",
+        "peak_gpu_mem_gb", "backbone_seconds", "task_generation_seconds", "filtered_search_seconds",
+        "ordinary_search_seconds", "merge_seconds", "forward_prune_seconds", "csr_reverse_seconds",
+        "reverse_prune_seconds", "compaction_seconds")]
+        + [(n, ctypes.c_uint64) for n in (
+            "filtered_search_distance_count", "unfiltered_search_distance_count", "label_check_count",
+            "label_reject_count", "filtered_candidate_count", "unfiltered_candidate_count", "merged_candidate_count",
+            "active_rows", "original_neighbor_count", "filtered_seed_count", "filtered_visited_count",
+            "filtered_visited_reserved_count", "filtered_top_reserved_count", "bridge_reserved_count",
+            "unfiltered_reserved_count", "filtered_reserved_count", "label_occlusion_blocked_count",
+            "geometry_occluded_count", "candidate_rejected_by_label_count", "refill_count",
+            "filtered_prune_reject_count", "universal_label_pass_count", "final_prune_rows", "reverse_edges",
+            "reverse_touched_rows", "filtered_reverse_edges", "filtered_reverse_touched_rows",
+            "filtered_reverse_candidates_kept", "filtered_reverse_pruned_rows")]
+        + [(n, ctypes.c_double) for n in (
+            "avg_common_label_out_degree", "common_label_degree_before_avg", "common_label_degree_after_avg",
+            "active_rows_frac")]
+        + [(n, ctypes.c_uint32) for n in (
+            "low_common_label_degree_count", "low_common_before", "low_common_after", "out_degree_min",
+            "out_degree_max")]
+        + [("out_degree_avg", ctypes.c_double)]
+        + [(n, ctypes.c_uint32) for n in (
+            "common_label_degree_min", "common_label_degree_max", "invalid_neighbor_count", "self_loop_count")]
+        + [("prune_output_degree_avg", ctypes.c_double)]
+        + [(n, ctypes.c_uint32) for n in ("filtered_seed_source", "semantic_stage", "semantic_complete")])
+
+    def as_dict(self) -> dict:
+        return {k: getattr(self, k) for k, _ in self._fields_}
+
+
 class DanceStitchedStats(ctypes.Structure):
     """Mirror of ``DanceStitchedStats`` in include/dance_b200.h."""
     _fields_ = [(n, ctypes.c_uint32) for n in (
@@ -111,7 +144,19 @@ SIGNATURES = {
     "gpu_vamana_get_last_stats": (None, [_P]),
     "gpu_vamana_vnew2_get_last_medoid": (_U32, []),
     "gpu_vamana_vnew2_get_last_stats": (None, [_P]),
+    # reference filtered C ABI (include/gpu_vamana_filtered.h)
+    "gpu_vamana_filtered_build_uint8": (_I, [_P, _U32, _U32, _U32, _U32, _U32, _U32, _U32, _F, _P, _P, _U32, _P,
+                                             _U32, _U32, _U32, _P, _P, _U32, _P, _P]),
+    "gpu_vamana_filtered_build_float": (_I, [_P, _U32, _U32, _U32, _U32, _U32, _U32, _U32, _F, _P, _P, _U32, _P,
+                                             _U32, _U32, _U32, _P, _P, _U32, _P, _P]),
+    "gpu_vamana_filtered_get_last_stats": (None, [_P]),
     # additive C ABI (include/dance_b200.h)
+    "dance_filtered_build_resident": (_I, [_I, _P, _U64, _U32, _U32, _U32, _U32, _U32, _U32, _U32, _F, _P, _P, _P,
+                                           _U32, _U32, _U32, _P, _P, _U32, _P, _P, _P, _P]),
+    "dance_filtered_random_graph": (_I, [_U32, _U32, _U32, _U32, _P, _P, _P]),
+    "dance_filtered_stage_round": (_I, [_I, _P, _U64, _U32, _U32, _U32, _U32, _U32, _U32, _U32, _F, _P, _P, _P,
+                                        _U32, _U32, _U32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P, _P,
+                                        _P]),
     "dance_vamana_default_params": (None, [_P]),
     "dance_last_error": (ctypes.c_char_p, []),
     "dance_kernel_launch_count": (_U64, []),

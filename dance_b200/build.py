@@ -20,9 +20,10 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libdance_b200.so"
 
-SOURCES = ["vamana_build.cu", "vamana_sharded.cu", "gpu_merge.cu", "stitched.cu"]
-HEADERS = ["dance_common.cuh", "vamana_kernels.cuh", "host_common.cuh"]
-PUBLIC_HEADERS = ["dance_b200.h", "gpu_vamana_builder.h", "gpu_vamana_config.h", "gpu_merge.h"]
+SOURCES = ["vamana_build.cu", "vamana_sharded.cu", "gpu_merge.cu", "stitched.cu", "filtered.cu"]
+HEADERS = ["dance_common.cuh", "vamana_kernels.cuh", "host_common.cuh", "filtered_kernels.cuh"]
+PUBLIC_HEADERS = ["dance_b200.h", "gpu_vamana_builder.h", "gpu_vamana_config.h", "gpu_merge.h",
+                  "gpu_vamana_filtered.h"]
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 

@@ -28,6 +28,8 @@
 #endif
 #include <stddef.h>
 
+#include "gpu_vamana_filtered.h"
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -258,6 +260,46 @@ DANCE_API int dance_stitched_remap(uint32_t num_points, uint32_t num_labels, con
                                    const uint32_t *d_local_degree, uint32_t r_small, uint32_t r_stitched,
                                    uint64_t *row_offsets, uint32_t *row_ids, uint64_t row_ids_capacity,
                                    DanceStitchedStats *stats, void *stream);
+
+/* ---- GPU-FilteredVamana on resident vectors ------------------------------- */
+/* The canonical filtered build of gpu_vamana_filtered.h on a padded store
+ * already in device memory: dtype DANCE_U8 or DANCE_F16 (the float entry
+ * point searches in fp16); work_C is the work width itself (no min(C, 128)
+ * clamp here; it must lie in [2R, 128]).  Label arrays are host arrays as in
+ * gpu_vamana_filtered.h.  d_init_graph/d_init_degree (N x R) replace the
+ * random initial graph when given; rounds = 3 is the reference's schedule.
+ * Status 1 when work_C < 2R. */
+DANCE_API int dance_filtered_build_resident(int dtype, const void *d_data, uint64_t row_stride_bytes,
+                                            uint32_t num_points, uint32_t dim, uint32_t R, uint32_t L,
+                                            uint32_t filtered_L, uint32_t work_C, uint32_t STEPS, float alpha,
+                                            const uint32_t *point_label_offsets, const uint32_t *point_labels,
+                                            const uint32_t *label_to_start_id, uint32_t num_labels,
+                                            uint32_t universal_label_id, uint32_t global_start_id,
+                                            const uint32_t *d_init_graph, const uint32_t *d_init_degree,
+                                            uint32_t rounds, uint32_t *d_graph, uint32_t *d_degree,
+                                            GPUFilteredVamanaStats *stats, void *stream);
+/* The reference's deterministic random initial graph (min(R, initial_degree,
+ * N-1) distinct hashed neighbours per point, INVALID padded). */
+DANCE_API int dance_filtered_random_graph(uint32_t num_points, uint32_t R, uint32_t initial_degree, uint32_t seed,
+                                          uint32_t *d_graph, uint32_t *d_degree, void *stream);
+/* One round from (d_graph_in, d_degree_in) with its intermediates copied out
+ * (parity tests): per-(point, label) search outputs (total labels x
+ * min(min(filtered_L, 32), 8)), union search outputs (N x min(R, L)), merged
+ * work rows (N x work_C) with distances and lengths, the forward-pruned graph
+ * and the reverse-repaired graph (N x R).  Any output but the last two may
+ * be NULL. */
+DANCE_API int dance_filtered_stage_round(int dtype, const void *d_data, uint64_t row_stride_bytes,
+                                         uint32_t num_points, uint32_t dim, uint32_t R, uint32_t L,
+                                         uint32_t filtered_L, uint32_t work_C, uint32_t STEPS, float alpha,
+                                         const uint32_t *point_label_offsets, const uint32_t *point_labels,
+                                         const uint32_t *label_to_start_id, uint32_t num_labels,
+                                         uint32_t universal_label_id, uint32_t global_start_id,
+                                         const uint32_t *d_graph_in, const uint32_t *d_degree_in,
+                                         uint32_t *d_task_ids, float *d_task_dists, uint32_t *d_union_ids,
+                                         float *d_union_dists, uint32_t *d_work_ids, float *d_work_dists,
+                                         uint32_t *d_work_degree, uint32_t *d_forward_graph,
+                                         uint32_t *d_forward_degree, uint32_t *d_graph_out, uint32_t *d_degree_out,
+                                         void *stream);
 
 /* ---- query search over a built graph (recall harness) -------------------- */
 /* DiskANN-style best-first search from `start` with list size L_search; the

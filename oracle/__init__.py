@@ -42,6 +42,17 @@ _SIGS = {
     "oracle_build": (_I, [_I, _P, _U64, _U32, _U32, _U32, _U32, _U32, _U32, _P, _I, _I, _P, _P, _P, _P]),
     "oracle_search_queries": (_I, [_I, _P, _U64, _U32, _U32, _P, _U32, _U32, _P, _U64, _U32, _U32, _U32, _P, _P,
                                    _I]),
+    "oracle_filtered_random_graph": (None, [_U32, _U32, _U32, _U32, _P, _P]),
+    "oracle_filtered_round": (_I, [_I, _P, _U64, _U32, _U32, _U32, _U32, _U32, _U32, _U32, _F, _P, _P, _P, _U32,
+                                   _U32, _U32, _P, _P, _P, _P, _P, _P, _P, _P, _P, _I]),
+    "oracle_filtered_build": (_I, [_I, _P, _U64, _U32, _U32, _U32, _U32, _U32, _U32, _U32, _F, _P, _P, _P, _U32,
+                                   _U32, _U32, _P, _P, _U32, _I, _P, _P]),
+    "oracle_filtered_task_search": (_I, [_I, _P, _U64, _U32, _U32, _U32, _U32, _U32, _P, _P, _P, _U32, _U32, _P,
+                                         _P, _P, _P, _I]),
+    "oracle_filtered_ordinary_search": (_I, [_I, _P, _U64, _U32, _U32, _U32, _U32, _U32, _U32, _P, _P, _P, _U32,
+                                             _U32, _U32, _P, _P, _P, _P, _I]),
+    "oracle_filtered_prune_lists": (_I, [_I, _P, _U64, _U32, _U32, _U32, _F, _P, _P, _U32, _P, _U32, _P, _P, _P,
+                                         _P, _P]),
 }
 
 _lib = None
@@ -287,3 +298,106 @@ def stitched(data, label_points, r_small, l_small, r_out, C, steps, prm=None):
         medoids.append(ids[med] if med < len(ids) else ids[0])
         stitched_remap(rows, ids, g, deg, r_small, r_out, counters)
     return rows, medoids, counters
+
+
+# ---------------------------------------------------------------- GPU-FilteredVamana
+class FilteredLabels:
+    """Per-point label CSR (each row strictly increasing) + per-label start ids."""
+
+    def __init__(self, offsets, labels, starts, num_labels, universal=0xFFFFFFFF, global_start=0xFFFFFFFF):
+        self.offsets = np.ascontiguousarray(offsets, np.uint32)
+        self.labels = np.ascontiguousarray(labels, np.uint32)
+        self.starts = np.ascontiguousarray(starts, np.uint32)
+        self.num_labels = int(num_labels)
+        self.universal = int(universal)
+        self.global_start = int(global_start)
+
+
+def filtered_random_graph(n, R, initial_degree=16, seed=42):
+    g = np.zeros((n, R), np.uint32)
+    d = np.zeros(n, np.uint32)
+    load().oracle_filtered_random_graph(n, R, initial_degree, seed, _p(g), _p(d))
+    return g, d
+
+
+def filtered_work_width(C):
+    """The reference's GPU work width: min(C, 128) (src/gpu_vamana_filtered.cu:6563-6567)."""
+    return min(int(C), 128)
+
+
+def filtered_round(data, lab: FilteredLabels, R, L, FL, C, STEPS, alpha, graph, degree):
+    """One canonical round; C is the work width.  Returns dict of graph, degree,
+    work rows (ids, dists, lengths) and the forward-pruned graph."""
+    d, stride, dt = _store(data)
+    n, dim = data.shape
+    out = dict(graph=np.zeros((n, R), np.uint32), degree=np.zeros(n, np.uint32),
+               work=np.zeros((n, C), np.uint32), work_d=np.zeros((n, C), np.float32),
+               work_deg=np.zeros(n, np.uint32), fwd=np.zeros((n, R), np.uint32), fwd_deg=np.zeros(n, np.uint32))
+    rc = load().oracle_filtered_round(dt, _p(d), stride, n, dim, R, L, FL, C, STEPS, alpha, _p(lab.offsets),
+                                      _p(lab.labels), _p(lab.starts), lab.num_labels, lab.universal,
+                                      lab.global_start, _p(np.ascontiguousarray(graph, np.uint32)),
+                                      _p(np.ascontiguousarray(degree, np.uint32)), _p(out["graph"]),
+                                      _p(out["degree"]), _p(out["work"]), _p(out["work_d"]), _p(out["work_deg"]),
+                                      _p(out["fwd"]), _p(out["fwd_deg"]), threads())
+    assert rc == 0
+    return out
+
+
+def filtered_build(data, lab: FilteredLabels, R, L, FL, C, STEPS, alpha, graph=None, degree=None, rounds=3):
+    """Canonical filtered build; C is the caller's C (clamped to 128 here)."""
+    d, stride, dt = _store(data)
+    n, dim = data.shape
+    g = np.zeros((n, R), np.uint32)
+    deg = np.zeros(n, np.uint32)
+    gi = None if graph is None else np.ascontiguousarray(graph, np.uint32)
+    di = None if degree is None else np.ascontiguousarray(degree, np.uint32)
+    rc = load().oracle_filtered_build(dt, _p(d), stride, n, dim, R, L, FL, filtered_work_width(C), STEPS, alpha,
+                                      _p(lab.offsets), _p(lab.labels), _p(lab.starts), lab.num_labels,
+                                      lab.universal, lab.global_start, _p(gi), _p(di), rounds, threads(), _p(g),
+                                      _p(deg))
+    assert rc == 0
+    return g, deg
+
+
+def filtered_task_search(data, lab: FilteredLabels, R, FL, STEPS, graph, degree):
+    d, stride, dt = _store(data)
+    n, dim = data.shape
+    keep = min(min(FL, 32), 8)
+    T = int(lab.offsets[-1])
+    ids = np.zeros((T, keep), np.uint32)
+    ds = np.zeros((T, keep), np.float32)
+    load().oracle_filtered_task_search(dt, _p(d), stride, n, dim, R, FL, STEPS, _p(lab.offsets), _p(lab.labels),
+                                       _p(lab.starts), lab.num_labels, lab.universal,
+                                       _p(np.ascontiguousarray(graph, np.uint32)),
+                                       _p(np.ascontiguousarray(degree, np.uint32)), _p(ids), _p(ds), threads())
+    return ids, ds
+
+
+def filtered_ordinary_search(data, lab: FilteredLabels, R, L, FL, STEPS, graph, degree):
+    d, stride, dt = _store(data)
+    n, dim = data.shape
+    keep = min(R, L)
+    ids = np.zeros((n, keep), np.uint32)
+    ds = np.zeros((n, keep), np.float32)
+    load().oracle_filtered_ordinary_search(dt, _p(d), stride, n, dim, R, L, FL, STEPS, _p(lab.offsets),
+                                           _p(lab.labels), _p(lab.starts), lab.num_labels, lab.universal,
+                                           lab.global_start, _p(np.ascontiguousarray(graph, np.uint32)),
+                                           _p(np.ascontiguousarray(degree, np.uint32)), _p(ids), _p(ds), threads())
+    return ids, ds
+
+
+def filtered_prune_lists(data, lab: FilteredLabels, R, alpha, rows, lists, dists):
+    """FilteredRobustPrune of explicit candidate lists (one per row in `rows`)."""
+    d, stride, dt = _store(data)
+    n, dim = data.shape
+    rows = np.ascontiguousarray(rows, np.uint32)
+    off = np.zeros(len(rows) + 1, np.uint64)
+    np.cumsum([len(x) for x in lists], out=off[1:])
+    ids = np.ascontiguousarray(np.concatenate(lists) if len(lists) else np.zeros(0), np.uint32)
+    ds = np.ascontiguousarray(np.concatenate(dists) if len(dists) else np.zeros(0), np.float32)
+    g = np.zeros((len(rows), R), np.uint32)
+    deg = np.zeros(len(rows), np.uint32)
+    load().oracle_filtered_prune_lists(dt, _p(d), stride, n, dim, R, alpha, _p(lab.offsets), _p(lab.labels),
+                                       lab.num_labels, _p(rows), len(rows), _p(off), _p(ids), _p(ds), _p(g),
+                                       _p(deg))
+    return g, deg

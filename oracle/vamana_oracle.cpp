@@ -39,6 +39,7 @@
 #include <cmath>
 #include <cstdint>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <vector>
 
@@ -1238,6 +1239,670 @@ int oracle_search_queries(int dtype, const void *data, uint64_t stride, uint32_t
                 }
             }
         }
+    }
+    return 0;
+}
+
+} // extern "C"
+
+// ====================================================================== GPU-FilteredVamana
+// Restatement of the reference's canonical filtered builder
+// (src/gpu_vamana_filtered.cu): deterministic random initial graph
+// (:716-744), then three rounds of label-masked per-(row, label) search
+// (:4266-4426), union-label search (:4530-4670), fixed-order merge with label
+// quotas (:4672-4842), missing work distances (:4845-4871), FilteredRobustPrune
+// (:4877-4994) and the exact CSR reverse repair (:4996-5230), driven as in
+// canonical_round0_from_host_backbone_typed (:5663-6300).  Pools are the
+// reference's unsorted slot arrays (insert_top_l_state_warp :4187-4233,
+// select_next_unexpanded_size_warp :4235-4263), restated literally.
+//
+// One deliberate difference: a row with reverse sources gets the list (its
+// forward row, then the new reverse sources).  The reference's fill kernel
+// (:5071-5105) also writes the forward rows of rows WITHOUT reverse sources,
+// at the start of the next row's list range, so the list of a row that
+// follows such a row depends on which concurrent store lands last; those
+// rows cannot be reproduced and follow the rule above instead.
+namespace
+{
+struct LabelSets
+{
+    const uint32_t *off;
+    const uint32_t *lab;
+    uint32_t num_labels;
+    uint32_t universal;
+    // point_has_exact_label_device (:557-571): labels of a point ascend.
+    bool has(uint32_t p, uint32_t l) const
+    {
+        for (uint32_t i = off[p]; i < off[p + 1]; ++i)
+        {
+            if (lab[i] == l)
+                return true;
+            if (lab[i] > l)
+                break;
+        }
+        return false;
+    }
+    // has_common_label_device (:495-529) with no universal label
+    bool common(uint32_t a, uint32_t b) const
+    {
+        uint32_t i = off[a], j = off[b];
+        while (i < off[a + 1] && j < off[b + 1])
+        {
+            if (lab[i] == lab[j])
+                return true;
+            if (lab[i] < lab[j])
+                ++i;
+            else
+                ++j;
+        }
+        return false;
+    }
+    // filtered_selected_covers_common_labels (include/filtered_label_coverage.cuh:8-45)
+    bool covers(uint32_t target, uint32_t selected, uint32_t cand) const
+    {
+        uint32_t t = off[target], c = off[cand];
+        while (t < off[target + 1] && c < off[cand + 1])
+        {
+            if (lab[t] < lab[c])
+                ++t;
+            else if (lab[c] < lab[t])
+                ++c;
+            else
+            {
+                bool found = false;
+                for (uint32_t s = off[selected]; s < off[selected + 1]; ++s)
+                {
+                    if (lab[s] == lab[t])
+                    {
+                        found = true;
+                        break;
+                    }
+                    if (lab[s] > lab[t])
+                        break;
+                }
+                if (!found)
+                    return false;
+                ++t;
+                ++c;
+            }
+        }
+        return true;
+    }
+};
+
+uint32_t fhash(uint32_t x) { return hash_u32(x); } // filtered_hash_u32 (:694-702) is the same finaliser
+
+struct FSlotPool
+{
+    uint32_t cap, count = 0;
+    std::vector<uint32_t> ids;
+    std::vector<float> d;
+    std::vector<uint8_t> exp;
+    explicit FSlotPool(uint32_t c) : cap(c), ids(c, kInvalid), d(c, FLT_MAX), exp(c, 0) {}
+    static bool greater(float da, uint32_t ia, float db, uint32_t ib) { return da > db || (da == db && ia > ib); }
+    void insert(uint32_t id, float dist)
+    {
+        if (id == kInvalid)
+            return;
+        for (uint32_t p = 0; p < count; ++p)
+            if (ids[p] == id)
+            {
+                if (dist < d[p])
+                {
+                    d[p] = dist;
+                    exp[p] = 0;
+                }
+                return;
+            }
+        if (count < cap)
+        {
+            ids[count] = id;
+            d[count] = dist;
+            exp[count] = 0;
+            ++count;
+            return;
+        }
+        int w = -1;
+        for (uint32_t p = 0; p < count; ++p)
+            if (w < 0 || greater(d[p], ids[p], d[w], ids[w]))
+                w = (int)p;
+        if (w >= 0 && (dist < d[w] || (dist == d[w] && id < ids[w])))
+        {
+            ids[w] = id;
+            d[w] = dist;
+            exp[w] = 0;
+        }
+    }
+    int select() const
+    {
+        int b = -1;
+        for (uint32_t p = 0; p < count; ++p)
+            if (!exp[p] && (b < 0 || d[p] < d[b] || (d[p] == d[b] && ids[p] < ids[b])))
+                b = (int)p;
+        return b;
+    }
+};
+
+struct FilteredCtx
+{
+    Store st;
+    uint32_t N, R;
+    LabelSets ls;
+    const uint32_t *starts;
+    std::vector<uint32_t> lp_off, lp; // label -> points (ascending)
+    void build_postings()
+    {
+        lp_off.assign((size_t)ls.num_labels + 1, 0);
+        for (uint32_t p = 0; p < N; ++p)
+            for (uint32_t i = ls.off[p]; i < ls.off[p + 1]; ++i)
+                if (ls.lab[i] < ls.num_labels)
+                    ++lp_off[ls.lab[i] + 1];
+        for (uint32_t l = 0; l < ls.num_labels; ++l)
+            lp_off[l + 1] += lp_off[l];
+        lp.assign(lp_off[ls.num_labels], kInvalid);
+        std::vector<uint32_t> cur(lp_off.begin(), lp_off.end() - 1);
+        for (uint32_t p = 0; p < N; ++p)
+            for (uint32_t i = ls.off[p]; i < ls.off[p + 1]; ++i)
+                if (ls.lab[i] < ls.num_labels)
+                    lp[cur[ls.lab[i]]++] = p;
+    }
+};
+
+// filtered_deterministic_random_graph_kernel (:716-744)
+void filtered_random_graph(uint32_t N, uint32_t R, uint32_t initial_degree, uint32_t seed, uint32_t *graph,
+                           uint32_t *degrees)
+{
+    const uint32_t target = std::min(std::min(R, initial_degree), N > 0 ? N - 1 : 0u);
+    for (uint32_t row = 0; row < N; ++row)
+    {
+        uint32_t *g = graph + (size_t)row * R;
+        uint32_t deg = 0, attempt = 0;
+        while (deg < target && attempt < (1u << 24))
+        {
+            const uint32_t c = fhash(row * 0x9e3779b1u ^ seed * 0x85ebca6bu ^ attempt * 0xc2b2ae35u) % N;
+            ++attempt;
+            if (c == row)
+                continue;
+            bool dup = false;
+            for (uint32_t i = 0; i < deg; ++i)
+                dup |= g[i] == c;
+            if (!dup)
+                g[deg++] = c;
+        }
+        for (uint32_t i = deg; i < R; ++i)
+            g[i] = kInvalid;
+        degrees[row] = deg;
+    }
+}
+
+// canonical_filtered_task_search (:4266-4426) for task p (row, label at
+// label position p); label_seed_count 16, no posting anchor.
+void task_search(const FilteredCtx &cx, uint32_t p, uint32_t row, const uint32_t *graph, const uint32_t *deg,
+                 uint32_t pool_cap, uint32_t keep, uint32_t steps, uint32_t *out_ids, float *out_d)
+{
+    const uint32_t N = cx.N, R = cx.R;
+    const uint32_t label = cx.ls.lab[p];
+    for (uint32_t i = 0; i < keep; ++i)
+    {
+        out_ids[i] = kInvalid;
+        out_d[i] = FLT_MAX;
+    }
+    if (row >= N || label >= cx.ls.num_labels || label == cx.ls.universal)
+        return;
+    FSlotPool pool(pool_cap);
+    const uint32_t start = cx.starts[label];
+    if (start < N && start != row)
+        pool.insert(start, dist(cx.st, row, start));
+    const uint32_t pb = cx.lp_off[label], pc = cx.lp_off[label + 1] - pb;
+    const uint32_t nseed = std::min(16u, pc);
+    for (uint32_t s = 0; s < nseed; ++s)
+    {
+        const uint32_t seed = cx.lp[pb + fhash(row + s * 7919u + label * 17u) % pc];
+        if (seed >= N || seed == row)
+            continue;
+        pool.insert(seed, dist(cx.st, row, seed));
+    }
+    auto scan = [&](uint32_t x) {
+        const uint32_t dx = std::min(deg[x], R);
+        for (uint32_t j = 0; j < dx; ++j)
+        {
+            const uint32_t c = graph[(size_t)x * R + j];
+            if (c >= N || c == row || !cx.ls.has(c, label))
+                continue;
+            pool.insert(c, dist(cx.st, row, c));
+        }
+    };
+    scan(row);
+    for (uint32_t step = 0; step < steps; ++step)
+    {
+        const int e = pool.select();
+        if (e < 0)
+            break;
+        pool.exp[e] = 1;
+        scan(pool.ids[e]);
+    }
+    for (uint32_t i = 0; i < keep && i < pool.count; ++i)
+    {
+        out_ids[i] = pool.ids[i];
+        out_d[i] = pool.d[i];
+    }
+}
+
+// canonical_ordinary_search (:4530-4670), label_seed_count 64, restricted
+// traversal, all slots output.
+void ordinary_search(const FilteredCtx &cx, uint32_t row, uint32_t global_start, const uint32_t *graph,
+                     const uint32_t *deg, uint32_t pool_cap, uint32_t keep, uint32_t steps, uint32_t *out_ids,
+                     float *out_d)
+{
+    const uint32_t N = cx.N, R = cx.R;
+    const LabelSets &ls = cx.ls;
+    FSlotPool pool(pool_cap);
+    auto compatible = [&](uint32_t c) {
+        for (uint32_t p = ls.off[row]; p < ls.off[row + 1]; ++p)
+            if (ls.has(c, ls.lab[p]))
+                return true;
+        return false;
+    };
+    for (uint32_t p = ls.off[row]; p < ls.off[row + 1]; ++p)
+    {
+        const uint32_t label = ls.lab[p];
+        if (label >= ls.num_labels)
+            continue;
+        const uint32_t start = cx.starts[label];
+        if (start < N && start != row)
+            pool.insert(start, dist(cx.st, row, start));
+        const uint32_t pb = cx.lp_off[label], pc = cx.lp_off[label + 1] - pb;
+        const uint32_t nseed = std::min(64u, pc);
+        for (uint32_t s = 0; s < nseed; ++s)
+        {
+            const uint32_t seed = cx.lp[pb + fhash(row + s * 7919u + label * 17u) % pc];
+            if (seed >= N || seed == row)
+                continue;
+            pool.insert(seed, dist(cx.st, row, seed));
+        }
+    }
+    if (global_start < N && global_start != row && compatible(global_start))
+        pool.insert(global_start, dist(cx.st, row, global_start));
+    auto scan = [&](uint32_t x) {
+        const uint32_t dx = std::min(deg[x], R);
+        for (uint32_t j = 0; j < dx; ++j)
+        {
+            const uint32_t c = graph[(size_t)x * R + j];
+            if (c >= N || c == row || !compatible(c))
+                continue;
+            pool.insert(c, dist(cx.st, row, c));
+        }
+    };
+    scan(row);
+    for (uint32_t step = 0; step < steps; ++step)
+    {
+        const int e = pool.select();
+        if (e < 0)
+            break;
+        pool.exp[e] = 1;
+        scan(pool.ids[e]);
+    }
+    for (uint32_t i = 0; i < keep; ++i)
+    {
+        out_ids[i] = i < pool.count ? pool.ids[i] : kInvalid;
+        out_d[i] = i < pool.count ? pool.d[i] : FLT_MAX;
+    }
+}
+
+// canonical_merge_candidates (:4703-4842) without the unrestricted-round
+// options, then canonical_compute_work_distances (:4845-4871).
+uint32_t merge_row(const FilteredCtx &cx, uint32_t row, uint32_t C, uint32_t per_label_keep, uint32_t ord_keep,
+                   const uint32_t *graph, const uint32_t *deg, const uint32_t *task_ids, const float *task_d,
+                   const uint32_t *ord_ids, const float *ord_d, uint32_t *w, float *wd)
+{
+    const uint32_t N = cx.N, R = cx.R;
+    const LabelSets &ls = cx.ls;
+    for (uint32_t i = 0; i < C; ++i)
+    {
+        w[i] = kInvalid;
+        wd[i] = FLT_MAX;
+    }
+    uint32_t count = 0;
+    auto add = [&](uint32_t c, float d) {
+        if (c >= N || c == row || count >= C)
+            return;
+        for (uint32_t i = 0; i < count; ++i)
+            if (w[i] == c)
+            {
+                if (d < wd[i])
+                    wd[i] = d;
+                return;
+            }
+        w[count] = c;
+        wd[count] = d;
+        ++count;
+    };
+    for (uint32_t p = ls.off[row]; p < ls.off[row + 1]; ++p)
+        for (uint32_t i = 0; i < per_label_keep; ++i)
+            add(task_ids[(size_t)p * per_label_keep + i], task_d[(size_t)p * per_label_keep + i]);
+    const uint32_t dr = std::min(deg[row], R);
+    for (uint32_t i = 0; i < dr; ++i)
+    {
+        const uint32_t c = graph[(size_t)row * R + i];
+        if (c < N && c != row && ls.common(row, c))
+            add(c, FLT_MAX);
+    }
+    for (uint32_t i = 0; i < ord_keep; ++i)
+        add(ord_ids[i], ord_d[i]);
+    const uint32_t nl = ls.off[row + 1] - ls.off[row];
+    if (nl > 0 && nl <= 16)
+    {
+        uint32_t assigned[16] = {};
+        uint32_t quota = (R + nl - 1) / nl;
+        if (quota < per_label_keep)
+            quota = per_label_keep;
+        uint32_t kept = 0;
+        for (uint32_t i = 0; i < count; ++i)
+        {
+            const uint32_t c = w[i];
+            uint32_t bq = kInvalid, bcard = kInvalid;
+            for (uint32_t q = 0; q < nl; ++q)
+            {
+                const uint32_t label = ls.lab[ls.off[row] + q];
+                if (assigned[q] >= quota || !ls.has(c, label))
+                    continue;
+                const uint32_t card = cx.lp_off[label + 1] - cx.lp_off[label];
+                if (bq == kInvalid || card < bcard || (card == bcard && label < ls.lab[ls.off[row] + bq]))
+                {
+                    bq = q;
+                    bcard = card;
+                }
+            }
+            if (bq == kInvalid)
+                continue;
+            w[kept] = c;
+            wd[kept] = wd[i];
+            ++assigned[bq];
+            ++kept;
+        }
+        for (uint32_t i = kept; i < count; ++i)
+        {
+            w[i] = kInvalid;
+            wd[i] = FLT_MAX;
+        }
+        count = kept;
+    }
+    for (uint32_t i = 0; i < count; ++i)
+        if (wd[i] == FLT_MAX)
+            wd[i] = dist(cx.st, row, w[i]);
+    return count;
+}
+
+// canonical_exact_prune (:4877-4994) / canonical_exact_prune_csr (:5131-5230):
+// select the least (distance, id); drop q iff the selection covers every
+// label q shares with the row and 0 < alpha * d(sel, q) <= d(row, q).
+uint32_t filtered_prune(const FilteredCtx &cx, uint32_t row, float alpha, const uint32_t *cand, const float *cd,
+                        uint32_t n, uint32_t *out)
+{
+    std::vector<uint8_t> removed(n, 0);
+    uint32_t sel = 0;
+    while (sel < cx.R)
+    {
+        int b = -1;
+        for (uint32_t i = 0; i < n; ++i)
+        {
+            if (removed[i])
+                continue;
+            if (b < 0 || cd[i] < cd[b] || (cd[i] == cd[b] && cand[i] < cand[b]))
+                b = (int)i;
+        }
+        if (b < 0)
+            break;
+        const uint32_t best = cand[b];
+        out[sel++] = best;
+        removed[b] = 1;
+        for (uint32_t i = 0; i < n; ++i)
+        {
+            if (removed[i] || !cx.ls.covers(row, best, cand[i]))
+                continue;
+            const float pd = dist(cx.st, best, cand[i]);
+            g_pair_evals.fetch_add(1, std::memory_order_relaxed);
+            if (pd > 0.0f && alpha * pd <= cd[i])
+                removed[i] = 1;
+        }
+    }
+    return sel;
+}
+
+struct FilteredCounters
+{
+    uint64_t tasks = 0, reverse_edges = 0, touched = 0;
+};
+
+struct RoundOut
+{
+    std::vector<uint32_t> *work, *work_deg, *fwd, *fwd_deg;
+    std::vector<float> *work_d;
+};
+
+// One canonical round: graph_a -> graph_b (forward prune, then exact CSR reverse repair).
+void filtered_round(const FilteredCtx &cx, uint32_t C, uint32_t L, uint32_t FL, uint32_t steps, float alpha,
+                    uint32_t global_start, const std::vector<uint32_t> &ga, const std::vector<uint32_t> &da,
+                    std::vector<uint32_t> &gb, std::vector<uint32_t> &db, int threads, FilteredCounters &fc,
+                    const RoundOut *ro)
+{
+    const uint32_t N = cx.N, R = cx.R;
+    const uint32_t plp = std::min(FL, 32u), plk = std::min(plp, 8u);
+    const uint32_t ord_keep = std::min(R, L), ord_pool = std::min(64u, FL);
+    const uint32_t T = cx.ls.off[N];
+    std::vector<uint32_t> tids((size_t)T * plk);
+    std::vector<float> td((size_t)T * plk);
+#pragma omp parallel for schedule(dynamic, 64) num_threads(threads)
+    for (int64_t row = 0; row < (int64_t)N; ++row)
+        for (uint32_t p = cx.ls.off[row]; p < cx.ls.off[row + 1]; ++p)
+            task_search(cx, p, (uint32_t)row, ga.data(), da.data(), plp, plk, steps, &tids[(size_t)p * plk],
+                        &td[(size_t)p * plk]);
+    fc.tasks += T;
+    std::vector<uint32_t> w((size_t)N * C);
+    std::vector<float> wd((size_t)N * C);
+    std::vector<uint32_t> wdeg(N);
+#pragma omp parallel num_threads(threads)
+    {
+        std::vector<uint32_t> oid(ord_keep);
+        std::vector<float> od(ord_keep);
+#pragma omp for schedule(dynamic, 64)
+        for (int64_t row = 0; row < (int64_t)N; ++row)
+        {
+            ordinary_search(cx, (uint32_t)row, global_start, ga.data(), da.data(), ord_pool, ord_keep, steps,
+                            oid.data(), od.data());
+            wdeg[row] = merge_row(cx, (uint32_t)row, C, plk, ord_keep, ga.data(), da.data(), tids.data(), td.data(),
+                                  oid.data(), od.data(), &w[(size_t)row * C], &wd[(size_t)row * C]);
+        }
+    }
+    gb.assign((size_t)N * R, kInvalid);
+    db.assign(N, 0);
+#pragma omp parallel for schedule(dynamic, 64) num_threads(threads)
+    for (int64_t row = 0; row < (int64_t)N; ++row)
+        db[row] = filtered_prune(cx, (uint32_t)row, alpha, &w[(size_t)row * C], &wd[(size_t)row * C], wdeg[row],
+                                 &gb[(size_t)row * R]);
+    if (ro)
+    {
+        *ro->work = w;
+        *ro->work_d = wd;
+        *ro->work_deg = wdeg;
+        *ro->fwd = gb;
+        *ro->fwd_deg = db;
+    }
+    // exact CSR reverse repair on the forward-pruned graph
+    std::vector<std::vector<uint32_t>> rev(N);
+    for (uint32_t s = 0; s < N; ++s)
+        for (uint32_t i = 0; i < std::min(db[s], R); ++i)
+        {
+            const uint32_t t = gb[(size_t)s * R + i];
+            if (t < N && t != s)
+                rev[t].push_back(s);
+        }
+    std::vector<uint32_t> fwd_b = gb, fdeg_b = db;
+    uint64_t edges = 0, touched = 0;
+#pragma omp parallel for schedule(dynamic, 16) num_threads(threads) reduction(+ : edges, touched)
+    for (int64_t row = 0; row < (int64_t)N; ++row)
+    {
+        if (rev[row].empty())
+            continue;
+        edges += rev[row].size();
+        ++touched;
+        const uint32_t dr = std::min(fdeg_b[row], R);
+        std::vector<uint32_t> cand(fwd_b.begin() + (size_t)row * R, fwd_b.begin() + (size_t)row * R + dr);
+        for (uint32_t s : rev[row])
+        {
+            bool dup = s >= N || s == (uint32_t)row;
+            for (uint32_t i = 0; !dup && i < dr; ++i)
+                dup = fwd_b[(size_t)row * R + i] == s;
+            if (!dup)
+                cand.push_back(s);
+        }
+        std::vector<float> cd(cand.size());
+        for (size_t i = 0; i < cand.size(); ++i)
+            cd[i] = dist(cx.st, (uint32_t)row, cand[i]);
+        uint32_t *out = &gb[(size_t)row * R];
+        for (uint32_t i = 0; i < R; ++i)
+            out[i] = kInvalid;
+        db[row] = filtered_prune(cx, (uint32_t)row, alpha, cand.data(), cd.data(), (uint32_t)cand.size(), out);
+    }
+    fc.reverse_edges += edges;
+    fc.touched += touched;
+}
+
+FilteredCtx make_ctx(int dtype, const void *data, uint64_t stride, uint32_t N, uint32_t dim, uint32_t R,
+                     const uint32_t *offsets, const uint32_t *labels, const uint32_t *starts, uint32_t num_labels,
+                     uint32_t universal)
+{
+    FilteredCtx cx{Store{dtype, static_cast<const uint8_t *>(data), stride, dim}, N, R,
+                   LabelSets{offsets, labels, num_labels, universal}, starts, {}, {}};
+    cx.build_postings();
+    return cx;
+}
+
+} // namespace
+
+extern "C" {
+
+void oracle_filtered_random_graph(uint32_t N, uint32_t R, uint32_t initial_degree, uint32_t seed, uint32_t *graph,
+                                  uint32_t *degrees)
+{
+    filtered_random_graph(N, R, initial_degree, seed, graph, degrees);
+}
+
+// One round from a given graph; optional work rows (N x C) and forward graph (N x R).
+int oracle_filtered_round(int dtype, const void *data, uint64_t stride, uint32_t N, uint32_t dim, uint32_t R,
+                          uint32_t L, uint32_t FL, uint32_t C, uint32_t STEPS, float alpha, const uint32_t *offsets,
+                          const uint32_t *labels, const uint32_t *starts, uint32_t num_labels, uint32_t universal,
+                          uint32_t global_start, const uint32_t *graph_in, const uint32_t *degree_in,
+                          uint32_t *graph_out, uint32_t *degree_out, uint32_t *work_ids, float *work_dists,
+                          uint32_t *work_deg, uint32_t *fwd_graph, uint32_t *fwd_deg, int threads)
+{
+    const FilteredCtx cx = make_ctx(dtype, data, stride, N, dim, R, offsets, labels, starts, num_labels, universal);
+    std::vector<uint32_t> ga(graph_in, graph_in + (size_t)N * R), da(degree_in, degree_in + N), gb, db;
+    FilteredCounters fc;
+    std::vector<uint32_t> w, wdeg, fg, fd;
+    std::vector<float> wd;
+    RoundOut ro{&w, &wdeg, &fg, &fd, &wd};
+    filtered_round(cx, C, L, FL, STEPS, alpha, global_start, ga, da, gb, db, threads, fc, &ro);
+    std::copy(gb.begin(), gb.end(), graph_out);
+    std::copy(db.begin(), db.end(), degree_out);
+    if (work_ids)
+    {
+        std::copy(w.begin(), w.end(), work_ids);
+        std::copy(wd.begin(), wd.end(), work_dists);
+        std::copy(wdeg.begin(), wdeg.end(), work_deg);
+    }
+    if (fwd_graph)
+    {
+        std::copy(fg.begin(), fg.end(), fwd_graph);
+        std::copy(fd.begin(), fd.end(), fwd_deg);
+    }
+    return 0;
+}
+
+// Whole canonical build from a given initial graph (NULL: the random graph
+// of degree min(16, R), seed 42), `rounds` rounds (the reference runs 3).
+// C is the work width after the reference's min(C, 128) clamp.
+int oracle_filtered_build(int dtype, const void *data, uint64_t stride, uint32_t N, uint32_t dim, uint32_t R,
+                          uint32_t L, uint32_t FL, uint32_t C, uint32_t STEPS, float alpha, const uint32_t *offsets,
+                          const uint32_t *labels, const uint32_t *starts, uint32_t num_labels, uint32_t universal,
+                          uint32_t global_start, const uint32_t *graph_in, const uint32_t *degree_in,
+                          uint32_t rounds, int threads, uint32_t *graph_out, uint32_t *degree_out)
+{
+    const FilteredCtx cx = make_ctx(dtype, data, stride, N, dim, R, offsets, labels, starts, num_labels, universal);
+    std::vector<uint32_t> ga((size_t)N * R), da(N), gb, db;
+    if (graph_in)
+    {
+        std::copy(graph_in, graph_in + (size_t)N * R, ga.begin());
+        std::copy(degree_in, degree_in + N, da.begin());
+    }
+    else
+        filtered_random_graph(N, R, 16u, 42u, ga.data(), da.data());
+    FilteredCounters fc;
+    const bool trace = std::getenv("ORACLE_FILTERED_TRACE") != nullptr;
+    for (uint32_t round = 0; round < rounds; ++round)
+    {
+        const FilteredCounters before = fc;
+        filtered_round(cx, C, L, FL, STEPS, alpha, global_start, ga, da, gb, db, threads, fc, nullptr);
+        if (trace)
+            fprintf(stderr, "[oracle_filtered] round=%u touched=%llu reverse_proposals=%llu\n", round,
+                    (unsigned long long)(fc.touched - before.touched),
+                    (unsigned long long)(fc.reverse_edges - before.reverse_edges));
+        std::swap(ga, gb);
+        std::swap(da, db);
+    }
+    std::copy(ga.begin(), ga.end(), graph_out);
+    std::copy(da.begin(), da.end(), degree_out);
+    return 0;
+}
+
+// Task search outputs of every (row, label position) on a given graph (T x keep).
+int oracle_filtered_task_search(int dtype, const void *data, uint64_t stride, uint32_t N, uint32_t dim, uint32_t R,
+                                uint32_t FL, uint32_t STEPS, const uint32_t *offsets, const uint32_t *labels,
+                                const uint32_t *starts, uint32_t num_labels, uint32_t universal,
+                                const uint32_t *graph, const uint32_t *degree, uint32_t *out_ids, float *out_d,
+                                int threads)
+{
+    const FilteredCtx cx = make_ctx(dtype, data, stride, N, dim, R, offsets, labels, starts, num_labels, universal);
+    const uint32_t plp = std::min(FL, 32u), plk = std::min(plp, 8u);
+#pragma omp parallel for schedule(dynamic, 64) num_threads(threads)
+    for (int64_t row = 0; row < (int64_t)N; ++row)
+        for (uint32_t p = offsets[row]; p < offsets[row + 1]; ++p)
+            task_search(cx, p, (uint32_t)row, graph, degree, plp, plk, STEPS, out_ids + (size_t)p * plk,
+                        out_d + (size_t)p * plk);
+    return 0;
+}
+
+// Union-label search outputs of every row (N x min(R, L)).
+int oracle_filtered_ordinary_search(int dtype, const void *data, uint64_t stride, uint32_t N, uint32_t dim,
+                                    uint32_t R, uint32_t L, uint32_t FL, uint32_t STEPS, const uint32_t *offsets,
+                                    const uint32_t *labels, const uint32_t *starts, uint32_t num_labels,
+                                    uint32_t universal, uint32_t global_start, const uint32_t *graph,
+                                    const uint32_t *degree, uint32_t *out_ids, float *out_d, int threads)
+{
+    const FilteredCtx cx = make_ctx(dtype, data, stride, N, dim, R, offsets, labels, starts, num_labels, universal);
+    const uint32_t keep = std::min(R, L), pool = std::min(64u, FL);
+#pragma omp parallel for schedule(dynamic, 64) num_threads(threads)
+    for (int64_t row = 0; row < (int64_t)N; ++row)
+        ordinary_search(cx, (uint32_t)row, global_start, graph, degree, pool, keep, STEPS,
+                        out_ids + (size_t)row * keep, out_d + (size_t)row * keep);
+    return 0;
+}
+
+// Per-row FilteredRobustPrune of candidate lists given as CSR (tests).
+int oracle_filtered_prune_lists(int dtype, const void *data, uint64_t stride, uint32_t N, uint32_t dim, uint32_t R,
+                                float alpha, const uint32_t *offsets, const uint32_t *labels, uint32_t num_labels,
+                                const uint32_t *rows, uint32_t nrows, const uint64_t *list_off,
+                                const uint32_t *list_ids, const float *list_d, uint32_t *graph_out,
+                                uint32_t *degree_out)
+{
+    const FilteredCtx cx = make_ctx(dtype, data, stride, N, dim, R, offsets, labels, nullptr, num_labels, kInvalid);
+    for (uint32_t r = 0; r < nrows; ++r)
+    {
+        uint32_t *out = graph_out + (size_t)r * R;
+        for (uint32_t i = 0; i < R; ++i)
+            out[i] = kInvalid;
+        degree_out[r] = filtered_prune(cx, rows[r], alpha, list_ids + list_off[r], list_d + list_off[r],
+                                       (uint32_t)(list_off[r + 1] - list_off[r]), out);
     }
     return 0;
 }

@@ -13,6 +13,8 @@ REFERENCE_SYMBOLS = [
     "gpu_vamana_build", "gpu_vamana_build_float", "gpu_vamana_vnew2_build", "gpu_vamana_vnew2_build_float",
     "gpu_vamana_vnew2_build_device", "gpu_vamana_vnew2_build_device_float", "gpu_vamana_get_last_medoid",
     "gpu_vamana_get_last_stats", "gpu_vamana_vnew2_get_last_medoid", "gpu_vamana_vnew2_get_last_stats",
+    # DANCE include/gpu_vamana_filtered.h:79-123
+    "gpu_vamana_filtered_build_uint8", "gpu_vamana_filtered_build_float", "gpu_vamana_filtered_get_last_stats",
 ]
 
 
