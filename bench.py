@@ -54,9 +54,9 @@ def parse():
     ap.add_argument("--no-recall", action="store_true")
     ap.add_argument("--ref-gpu", action="store_true",
                     help="also time the reference's own GPU builder (oracle/_ref, sm_100a) once on the workload")
-    ap.add_argument("--workload", choices=["cfg1_u8_10M", "cfg3_stitched"], default="cfg1_u8_10M",
-                    help="cfg1_u8_10M: the headline standard build; cfg3_stitched: the per-label stitched build "
-                         "of BASELINE.json configs[3]")
+    ap.add_argument("--workload", choices=["cfg1_u8_10M", "cfg2_filtered", "cfg3_stitched"], default="cfg1_u8_10M",
+                    help="cfg1_u8_10M: the headline standard build; cfg2_filtered: the GPU-FilteredVamana build of "
+                         "BASELINE.json configs[2]; cfg3_stitched: the per-label stitched build of configs[3]")
     return ap.parse_args()
 
 
@@ -816,8 +816,283 @@ def run_stitched_reference(args, n):
     return 0
 
 
+# ------------------------------------------------------------------ filtered
+FILTERED = dict(name="cfg2_filtered_f32_1M", N=1_000_000, dim=96, centroids=1000, sigma=0.3, vocab=1000, min_labels=1,
+                max_labels=5, R=64, L=100, FL=100, C=128, STEPS=64, alpha=1.2, seed=42, queries=10_000)
+FILTERED_CPU_SAMPLE = 6_000  # points built by the oracle for cpu_baseline
+
+
+def filtered_label_starts(x, offs, labs, vocab):
+    """Start point of each label: the member nearest to the label's mean (a
+    stand-in for DiskANN's label start selection, which lives outside the
+    reference); the global start is the point nearest to the overall mean."""
+    import numpy as np
+    import torch
+    n = x.shape[0]
+    rows = torch.from_numpy(np.repeat(np.arange(n), np.diff(offs.astype(np.int64)))).cuda()
+    lab = torch.from_numpy(labs.astype(np.int64)).cuda()
+    xf = x.float()
+    sums = torch.zeros((vocab, x.shape[1]), dtype=torch.float64, device="cuda")
+    sums.index_add_(0, lab, xf[rows].double())
+    cnt = torch.bincount(lab, minlength=vocab).clamp(min=1).double()
+    mean = (sums / cnt[:, None]).float()
+    d = ((xf[rows] - mean[lab]) ** 2).sum(1)
+    key = d.double()
+    best = torch.full((vocab,), float("inf"), dtype=torch.float64, device="cuda")
+    best.scatter_reduce_(0, lab, key, reduce="amin")
+    hit = key == best[lab]
+    starts = torch.full((vocab,), n, dtype=torch.int64, device="cuda")
+    starts.scatter_reduce_(0, lab[hit], rows[hit], reduce="amin")
+    starts = starts.cpu().numpy()
+    starts[starts >= n] = 0xFFFFFFFF
+    g = int(((xf - xf.mean(0)) ** 2).sum(1).argmin())
+    return starts.astype(np.uint32), g
+
+
+def filtered_recall(x, store, stride, offs, labs, graph, starts, R, queries, qlabels, L_search=100, K=10):
+    """Recall@10 of label-filtered queries searched from their label's start;
+    ground truth is brute force among the points carrying the label."""
+    import numpy as np
+    import torch
+    from dance_b200 import vamana, workloads
+    n = x.shape[0]
+    rows = np.repeat(np.arange(n), np.diff(offs.astype(np.int64)))
+    order = np.argsort(labs, kind="stable")
+    lab_sorted = labs[order]
+    d_off = torch.from_numpy(offs.view(np.int32)).cuda()
+    d_lab = torch.from_numpy(labs.view(np.int32)).cuda()
+    qs = torch.from_numpy(starts[qlabels].view(np.int32)).cuda()
+    ql = torch.from_numpy(qlabels.astype(np.uint32).view(np.int32)).cuda()
+    # queries in the store's element type (the fp16 store searches fp16 queries)
+    ids, _ = vamana.search_queries_filtered(store, x.shape[1], stride, graph, R, d_off, d_lab, ql, qs,
+                                            queries.to(store.dtype), L_search, K)
+    ids = ids.cpu().numpy().view(np.uint32)
+    hits = total = 0
+    for l in np.unique(qlabels):
+        qi = np.nonzero(qlabels == l)[0]
+        a, b = np.searchsorted(lab_sorted, [l, l + 1])
+        members = torch.from_numpy(rows[order[a:b]].astype(np.int64)).cuda()
+        k = min(K, len(members))
+        gt_local, _ = workloads.brute_force_knn(x[members], queries[torch.from_numpy(qi).cuda()], k)
+        gt = members[gt_local.long()].cpu().numpy()
+        for j, q in enumerate(qi):
+            hits += len(set(ids[q, :k].tolist()) & set(gt[j].tolist()))
+            total += k
+    return hits / total
+
+
+def filtered_inputs(n):
+    import numpy as np
+    from dance_b200 import workloads
+    F = FILTERED
+    x = workloads.gaussian_mixture_f32(n, F["dim"], F["centroids"], F["sigma"], seed=F["seed"], device="cuda")
+    offs, labs = workloads.zipf_multilabels(n, F["vocab"], F["min_labels"], F["max_labels"], seed=F["seed"])
+    starts, gstart = filtered_label_starts(x, offs, labs, F["vocab"])
+    q = workloads.gaussian_mixture_f32(F["queries"], F["dim"], F["centroids"], F["sigma"], seed=F["seed"],
+                                       device="cuda", stream_offset=1)
+    rng = np.random.default_rng(F["seed"] + 1)
+    pz = 1.0 / np.arange(1, F["vocab"] + 1)
+    qlabels = rng.choice(F["vocab"], size=F["queries"], p=pz / pz.sum()).astype(np.int64)
+    return x, offs, labs, starts, gstart, q, qlabels
+
+
+def run_filtered(args):
+    import numpy as np
+    import torch
+    import dance_b200
+    from dance_b200 import filtered, vamana
+    F = FILTERED
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    lib = dance_b200.load()
+    n = args.n if args.n != WORKLOAD["N"] else F["N"]
+    x, offs, labs, starts, gstart, q, qlabels = filtered_inputs(n)
+    store, stride = vamana.padded_store(x.half())
+    R, L, FL, C, S, alpha = F["R"], F["L"], F["FL"], F["C"], F["STEPS"], F["alpha"]
+    graph = torch.empty((n, R), dtype=torch.int32, device="cuda")
+    degree = torch.empty(n, dtype=torch.int32, device="cuda")
+
+    def one_build():
+        return filtered.build_resident(store, F["dim"], stride, R, L, FL, min(C, 128), S, alpha, offs, labs, starts,
+                                       F["vocab"], 0xFFFFFFFF, gstart, graph=graph, degree=degree)
+
+    for _ in range(args.warmup):
+        one_build()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    launches0 = lib.dance_kernel_launch_count()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    stats = []
+    ev0.record()
+    for _ in range(args.steps):
+        stats.append(one_build()[2])
+    ev1.record()
+    torch.cuda.synchronize()
+    launches = lib.dance_kernel_launch_count() - launches0
+    clk = clocks.stop()
+    elapsed = ev0.elapsed_time(ev1) * 1e-3
+    peak, peak_kind = measured_peaks()
+    st = stats[-1]
+    # roofline of the union-label search (the largest stage): one gathered
+    # fp16 row per distance evaluation over its kernel time (3 launches per build)
+    alg = st["unfiltered_search_distance_count"] * stride
+    ksec = st["ordinary_search_seconds"]
+    achieved = alg / ksec / 1e9 if ksec else 0.0
+    stage = {k: st[k] for k in ("filtered_search_seconds", "ordinary_search_seconds", "merge_seconds",
+                                "forward_prune_seconds", "csr_reverse_seconds", "reverse_prune_seconds")}
+    line = {
+        "metric": "filtered_build_vectors_per_s", "value": n * args.steps / elapsed, "unit": "vectors/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded generators, BASELINE.json configs[2] recipe)",
+        "config": {"workload": F["name"], "N": n, "dim": F["dim"], "labels": F["vocab"],
+                   "label_memberships": int(offs[-1]), "R": R, "L": L, "FilteredL": FL, "C": C, "STEPS": S,
+                   "alpha": alpha, "rounds": 3, "pools": [min(FL, 32), min(FL, 32, 8), min(64, FL)],
+                   "l2": "inputs larger than L2 (192 MB fp16 vectors + graphs), no flush",
+                   "label_starts": "member nearest to the label mean (stand-in for DiskANN's selection)"},
+        "roofline": {"kernel": "fl_union_search_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
+                     "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind, "traffic": None,
+                     "algorithmic_bytes_per_launch": alg / 3, "avg_launch_ms": ksec / 3 * 1e3},
+        "gpu_launches": int(launches),
+        "clocks": clk,
+        "stage_seconds": stage,
+        "counters_per_build": {"task_search_evals": st["filtered_search_distance_count"],
+                               "union_search_evals": st["unfiltered_search_distance_count"],
+                               "reverse_edges": st["reverse_edges"], "reverse_touched_rows": st["reverse_touched_rows"]},
+    }
+    hx = x.cpu().numpy()
+    if not args.no_e2e:
+        hxp = torch.from_numpy(hx).pin_memory()
+        hg = np.zeros((n, R), np.uint32)
+        hd = np.zeros(n, np.uint32)
+        P = lambda a: ctypes.c_void_p(a.ctypes.data)  # noqa: E731
+
+        def e2e_call():
+            rc = lib.gpu_vamana_filtered_build_float(ctypes.c_void_p(hxp.data_ptr()), n, F["dim"], R, L, FL, C, S,
+                                                     alpha, P(offs), P(labs), len(labs), P(starts), F["vocab"],
+                                                     0xFFFFFFFF, gstart, None, None, 0, P(hg), P(hd))
+            dance_b200.check(rc, "gpu_vamana_filtered_build_float")
+
+        e2e_call()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e2e_call()
+        dt = time.perf_counter() - t0
+        line["e2e"] = {"value": n * args.steps / dt, "unit": "vectors/s",
+                       "h2d_bytes_per_step": int(hx.nbytes + offs.nbytes + labs.nbytes + starts.nbytes),
+                       "d2h_bytes_per_step": int(hg.nbytes + hd.nbytes),
+                       "api": "gpu_vamana_filtered_build_float (reference C ABI), pinned vectors, wall clock",
+                       "matches_resident_build": bool(np.array_equal(hg, graph.cpu().numpy().view(np.uint32)))}
+    if not args.no_recall:
+        line["recall_at_10"] = {"L_search": 100, "queries": F["queries"], "search": "label-filtered, from the label start",
+                                "ours": filtered_recall(x, store, stride, offs, labs, graph, starts, R, q, qlabels)}
+        deg = degree.cpu().numpy()
+        line["graph"] = {"avg_degree": float(deg.mean()), "max_degree": int(deg.max()), "min_degree": int(deg.min())}
+    if not args.no_cpu_baseline:
+        import oracle
+        m = min(FILTERED_CPU_SAMPLE, n)
+        so, sl = offs[:m + 1].copy(), labs[:int(offs[m])].copy()
+        ss = np.full(F["vocab"], 0xFFFFFFFF, np.uint32)
+        for pnt in range(m - 1, -1, -1):
+            ss[sl[so[pnt]:so[pnt + 1]]] = pnt
+        lab = oracle.FilteredLabels(so, sl, ss, F["vocab"], 0xFFFFFFFF, 0)
+        threads = os.cpu_count() or 1
+        t0 = time.perf_counter()
+        oracle.filtered_build(oracle.float_to_half(hx[:m]), lab, R, L, FL, C, S, alpha)
+        secs = time.perf_counter() - t0
+        line["cpu_baseline"] = {"value": m / secs, "unit": "vectors/s", "cores": threads, "kind": "port",
+                                "sample": f"first {m} points with their labels, 3-round canonical build ({secs:.1f} s)"}
+    if args.ref_gpu:
+        line["reference_gpu"] = reference_gpu_filtered(hx, offs, labs, starts, gstart, x, store, stride, q, qlabels,
+                                                       graph)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def reference_gpu_filtered(hx, offs, labs, starts, gstart, x, store, stride, q, qlabels, our_graph):
+    """The reference's own filtered builder (DANCE src/gpu_vamana_filtered.cu
+    built for sm_100a) through its C ABI on the same inputs."""
+    import numpy as np
+    import torch
+    lib_path = ROOT / "oracle" / "_ref" / "libref_filtered.so"
+    if not lib_path.exists():
+        return {"unavailable": f"{lib_path.name} not built"}
+    F = FILTERED
+    lib = ctypes.CDLL(str(lib_path))
+    fn = lib.gpu_vamana_filtered_build_float
+    fn.restype = ctypes.c_int
+    U, Pv = ctypes.c_uint32, ctypes.c_void_p
+    fn.argtypes = [Pv, U, U, U, U, U, U, U, ctypes.c_float, Pv, Pv, U, Pv, U, U, U, Pv, Pv, U, Pv, Pv]
+    n = hx.shape[0]
+    R = F["R"]
+    g = np.zeros((n, R), np.uint32)
+    d = np.zeros(n, np.uint32)
+    P = lambda a: ctypes.c_void_p(a.ctypes.data)  # noqa: E731
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    rc = fn(P(hx), n, F["dim"], R, F["L"], F["FL"], F["C"], F["STEPS"], F["alpha"], P(offs), P(labs), len(labs),
+            P(starts), F["vocab"], 0xFFFFFFFF, gstart, None, None, 0, P(g), P(d))
+    dt = time.perf_counter() - t0
+    if rc != 0:
+        return {"unavailable": f"reference build returned {rc}"}
+    gd = torch.from_numpy(g.view(np.int32)).cuda()
+    ours = our_graph.cpu().numpy().view(np.uint32)
+    same = float(np.mean([np.array_equal(np.sort(ours[i]), np.sort(g[i])) for i in range(0, n, 97)]))
+    return {"e2e_vectors_per_s": n / dt, "seconds": dt,
+            "recall_at_10": filtered_recall(x, store, stride, offs, labs, gd, starts, R, q, qlabels),
+            "avg_degree": float(d.mean()), "rows_equal_to_ours_sampled": same,
+            "build": "DANCE GPU-FilteredVamana canonical path, nvcc 12.9 sm_100a"}
+
+
+def run_filtered_reference(args):
+    """--impl reference for the filtered workload: the oracle port of the
+    canonical filtered build on the host cores, a bounded sample per step."""
+    import numpy as np
+    import oracle
+    from dance_b200 import workloads
+    F = FILTERED
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    m = FILTERED_CPU_SAMPLE
+    x = workloads.gaussian_mixture_f32(m, F["dim"], F["centroids"], F["sigma"], seed=F["seed"], device="cpu").numpy()
+    offs, labs = workloads.zipf_multilabels(m, F["vocab"], F["min_labels"], F["max_labels"], seed=F["seed"])
+    ss = np.full(F["vocab"], 0xFFFFFFFF, np.uint32)
+    for pnt in range(m - 1, -1, -1):
+        ss[labs[offs[pnt]:offs[pnt + 1]]] = pnt
+    lab = oracle.FilteredLabels(offs, labs, ss, F["vocab"], 0xFFFFFFFF, 0)
+    xs = oracle.float_to_half(x)
+    args_b = (F["R"], F["L"], F["FL"], F["C"], F["STEPS"], F["alpha"])
+    for _ in range(args.warmup):
+        oracle.filtered_build(xs[:500], oracle.FilteredLabels(offs[:501], labs[:int(offs[500])], ss, F["vocab"]),
+                              *args_b)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.filtered_build(xs, lab, *args_b)
+    dt = time.perf_counter() - t0
+    v = m * args.steps / dt
+    threads = os.cpu_count() or 1
+    print(json.dumps({
+        "impl": "reference", "metric": "filtered_build_vectors_per_s", "value": v, "unit": "vectors/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (BASELINE.json configs[2] recipe)",
+        "config": {"workload": F["name"], "N": m, "labels": F["vocab"]},
+        "cpu_baseline": {"value": v, "unit": "vectors/s", "cores": threads, "kind": "port",
+                         "sample": f"{m} points with their labels per step, 3-round canonical build"},
+        "e2e": {"value": v, "unit": "vectors/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}), flush=True)
+    return 0
+
+
 def main():
     args = parse()
+    if args.workload == "cfg2_filtered":
+        if args.impl == "reference":
+            return run_filtered_reference(args)
+        return run_filtered(args)
     if args.workload == "cfg3_stitched":
         if args.impl == "reference":
             return run_stitched_reference(args, args.n if args.n != WORKLOAD["N"] else STITCHED["N"])

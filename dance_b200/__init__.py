@@ -175,6 +175,8 @@ SIGNATURES = {
     "dance_stage_prune": (_I, [_I, _P, _U64, _U32, _U32, _U32, _U32, _F, _U32, _P, _P, _P, _P, _P, _P, _P]),
     "dance_search_queries": (_I, [_I, _P, _U64, _U32, _U32, _P, _U32, _U32, _P, _U64, _U32, _U32, _U32, _U32, _P,
                                   _P, _P]),
+    "dance_search_queries_filtered": (_I, [_I, _P, _U64, _U32, _U32, _P, _U32, _P, _P, _P, _P, _P, _U64, _U32, _U32,
+                                           _U32, _U32, _P, _P, _P]),
     "dance_merge_shards_gpu": (_I, [ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, ctypes.c_char_p, _U64, _U32,
                                     ctypes.c_char_p, ctypes.c_char_p]),
     "dance_merge_edges_device": (_I, [_P, _P, _U64, _U32, _U32, _U32, _U64, _P, _P, _P]),

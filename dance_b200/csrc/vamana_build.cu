@@ -516,6 +516,43 @@ int dance_search_queries(int dtype, const void *d_data, uint64_t stride, uint32_
     return dispatch<LaunchQuery>(dtype, qp.st.nchunks, qp, as_stream(stream));
 }
 
+int dance_search_queries_filtered(int dtype, const void *d_data, uint64_t stride, uint32_t N, uint32_t dim,
+                                  const uint32_t *d_graph, uint32_t R, const uint32_t *d_label_offsets,
+                                  const uint32_t *d_labels, const uint32_t *d_query_labels,
+                                  const uint32_t *d_query_starts, const void *d_queries, uint64_t query_stride,
+                                  uint32_t nq, uint32_t L_search, uint32_t K, uint32_t visited_log2,
+                                  uint32_t *d_out_ids, float *d_out_dists, void *stream)
+{
+    int rc = check_store(dtype, d_data, stride, N, dim);
+    if (rc)
+        return rc;
+    if (!d_graph || !d_queries || !d_out_ids || !d_out_dists || !d_label_offsets || !d_labels || !d_query_labels ||
+        !d_query_starts || K == 0 || K > L_search || L_search > (uint32_t)kMaxL || query_stride % 16 != 0 ||
+        visited_log2 < 8 || visited_log2 > 16)
+        return fail(-1, "invalid filtered query search arguments");
+    QueryParams qp{};
+    qp.st = make_view(d_data, stride, N, dim, dtype);
+    qp.queries = reinterpret_cast<const uint8_t *>(d_queries);
+    qp.qstride = query_stride;
+    qp.nq = nq;
+    qp.graph = d_graph;
+    qp.R = R;
+    qp.L = L_search;
+    qp.Lcap = lcap_of(L_search);
+    qp.K = K;
+    qp.log2h = visited_log2;
+    qp.start = kInvalid;
+    qp.out_ids = d_out_ids;
+    qp.out_dists = d_out_dists;
+    qp.label_off = d_label_offsets;
+    qp.labels = d_labels;
+    qp.query_label = d_query_labels;
+    qp.query_start = d_query_starts;
+    if (nq == 0)
+        return 0;
+    return dispatch<LaunchQuery>(dtype, qp.st.nchunks, qp, as_stream(stream));
+}
+
 } // extern "C"
 
 // ====================================================================== reference C ABI

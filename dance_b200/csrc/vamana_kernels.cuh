@@ -641,7 +641,22 @@ struct QueryParams
     uint32_t R, L, Lcap, K, log2h, start;
     uint32_t *out_ids;
     float *out_dists;
+    // label-filtered search (all optional): only points carrying the
+    // query's label are visited, from the query's own start point
+    const uint32_t *label_off, *labels; // point label CSR, labels ascending per point
+    const uint32_t *query_label;       // nq
+    const uint32_t *query_start;       // nq
 };
+
+// Point p carries label l (labels of a point ascend).
+__device__ __forceinline__ bool point_has_label(const uint32_t *off, const uint32_t *lab, uint32_t p, uint32_t l)
+{
+    const uint32_t e = off[p + 1];
+    for (uint32_t i = off[p]; i < e; ++i)
+        if (lab[i] >= l)
+            return lab[i] == l;
+    return false;
+}
 
 template <int DT, int CPL>
 __global__ void __launch_bounds__(kBlockThreads, DANCE_SEARCH_MIN_BLOCKS) query_search_kernel(QueryParams p)
@@ -658,7 +673,9 @@ __global__ void __launch_bounds__(kBlockThreads, DANCE_SEARCH_MIN_BLOCKS) query_
         load_frag<CPL>(q, p.queries + (uint64_t)qi * p.qstride, p.st.nchunks, gl);
         clear_visited(sm.vis, p.log2h, lane);
         PoolState ps{0, (int)p.L, 0, 0};
-        const uint32_t s0 = (lane == 0 && p.start < N) ? p.start : kInvalid;
+        const uint32_t start = p.query_start ? p.query_start[qi] : p.start;
+        const uint32_t qlabel = p.query_label ? p.query_label[qi] : kInvalid;
+        const uint32_t s0 = (lane == 0 && start < N) ? start : kInvalid;
         pool_insert_batch<DT, CPL>(sm, ps, p.log2h, p.st, q, s0, kInvalid, 0.0f, 0.0f, false, lane);
         while (true)
         {
@@ -675,9 +692,9 @@ __global__ void __launch_bounds__(kBlockThreads, DANCE_SEARCH_MIN_BLOCKS) query_
                 const uint32_t i0 = b + lane, i1 = b + 32 + lane;
                 uint32_t a0 = i0 < p.R ? row[i0] : kInvalid;
                 uint32_t a1 = i1 < p.R ? row[i1] : kInvalid;
-                if (a0 >= N)
+                if (a0 >= N || (p.query_label && !point_has_label(p.label_off, p.labels, a0, qlabel)))
                     a0 = kInvalid;
-                if (a1 >= N)
+                if (a1 >= N || (p.query_label && !point_has_label(p.label_off, p.labels, a1, qlabel)))
                     a1 = kInvalid;
                 pool_insert_batch<DT, CPL>(sm, ps, p.log2h, p.st, q, a0, a1, 0.0f, 0.0f, false, lane);
             }

@@ -160,6 +160,8 @@ def search_queries(store, dim: int, stride: int, graph, R: int, start: int, quer
                    visited_log2: int = 12, stream=None):
     """Best-first query search over a built graph; returns (ids, dists) CUDA tensors (nq x K)."""
     import torch
+    if queries.dtype != store.dtype:
+        raise ValueError(f"queries are {queries.dtype} but the store is {store.dtype}")
     q, qstride = padded_store(queries)
     nq = q.shape[0]
     ids = torch.empty((nq, K), dtype=torch.int32, device=store.device)
@@ -168,6 +170,25 @@ def search_queries(store, dim: int, stride: int, graph, R: int, start: int, quer
                                      start, _ptr(q), qstride, nq, L_search, K, visited_log2, _ptr(ids), _ptr(dd),
                                      _stream(stream))
     check(rc, "dance_search_queries")
+    return ids, dd
+
+
+def search_queries_filtered(store, dim: int, stride: int, graph, R: int, label_offsets, labels, query_labels,
+                            query_starts, queries, L_search: int, K: int, visited_log2: int = 12, stream=None):
+    """Label-filtered query search: query i visits only points carrying
+    query_labels[i], from query_starts[i].  Label arrays are CUDA tensors."""
+    import torch
+    if queries.dtype != store.dtype:
+        raise ValueError(f"queries are {queries.dtype} but the store is {store.dtype}")
+    q, qstride = padded_store(queries)
+    nq = q.shape[0]
+    ids = torch.empty((nq, K), dtype=torch.int32, device=store.device)
+    dd = torch.empty((nq, K), dtype=torch.float32, device=store.device)
+    rc = load().dance_search_queries_filtered(dtype_code(store), _ptr(store), stride, store.shape[0], dim,
+                                              _ptr(graph), R, _ptr(label_offsets), _ptr(labels), _ptr(query_labels),
+                                              _ptr(query_starts), _ptr(q), qstride, nq, L_search, K, visited_log2,
+                                              _ptr(ids), _ptr(dd), _stream(stream))
+    check(rc, "dance_search_queries_filtered")
     return ids, dd
 
 

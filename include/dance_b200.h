@@ -308,6 +308,16 @@ DANCE_API int dance_search_queries(int dtype, const void *d_data, uint64_t row_s
                          uint32_t dim, const uint32_t *d_graph, uint32_t R, uint32_t start, const void *d_queries,
                          uint64_t query_stride_bytes, uint32_t num_queries, uint32_t L_search, uint32_t K,
                          uint32_t visited_log2, uint32_t *d_out_ids, float *d_out_dists, void *stream);
+/* Label-filtered form (DiskANN filtered search): query i visits only points
+ * carrying d_query_labels[i] (d_label_offsets/d_labels: the points' label
+ * CSR on the device, ascending per point) and starts from d_query_starts[i]. */
+DANCE_API int dance_search_queries_filtered(int dtype, const void *d_data, uint64_t row_stride_bytes,
+                                            uint32_t num_points, uint32_t dim, const uint32_t *d_graph, uint32_t R,
+                                            const uint32_t *d_label_offsets, const uint32_t *d_labels,
+                                            const uint32_t *d_query_labels, const uint32_t *d_query_starts,
+                                            const void *d_queries, uint64_t query_stride_bytes, uint32_t num_queries,
+                                            uint32_t L_search, uint32_t K, uint32_t visited_log2,
+                                            uint32_t *d_out_ids, float *d_out_dists, void *stream);
 
 #ifdef __cplusplus
 }
