@@ -21,7 +21,8 @@ CSRC = PKG / "csrc"
 LIB = PKG / "libdance_b200.so"
 
 SOURCES = ["vamana_build.cu", "vamana_sharded.cu", "gpu_merge.cu", "stitched.cu", "filtered.cu"]
-HEADERS = ["dance_common.cuh", "vamana_kernels.cuh", "host_common.cuh", "filtered_kernels.cuh"]
+HEADERS = ["dance_common.cuh", "vamana_kernels.cuh", "host_common.cuh", "filtered_kernels.cuh",
+           "gram_u8.cuh"]
 PUBLIC_HEADERS = ["dance_b200.h", "gpu_vamana_builder.h", "gpu_vamana_config.h", "gpu_merge.h",
                   "gpu_vamana_filtered.h"]
 

@@ -19,6 +19,7 @@
 #include "../../include/gpu_vamana_builder.h"
 #include "../../include/gpu_vamana_config.h"
 #include "vamana_kernels.cuh"
+#include "gram_u8.cuh"
 
 namespace dance
 {
@@ -297,11 +298,31 @@ struct LaunchPrune
 {
     static int run(PruneParams p, cudaStream_t s)
     {
+        if (DT == kU8)
+            return run_gram(p, s);
         auto k = prune_kernel<DT, CPL>;
         p.Cp = (uint32_t)next_pow2((int)p.C);
         if (p.Cp < 32)
             p.Cp = 32;
         p.per_warp = align16(prune_smem_per_warp(p.C, p.Cp, p.R, p.row_bytes));
+        const size_t smem = (size_t)p.per_warp * kWarpsPerBlock;
+        if ((int)smem > max_optin_smem())
+            return fail(-1, "prune vector cache %zu B exceeds shared memory", smem);
+        DANCE_CUDA(allow_smem(k, smem));
+        const int grid = wave_grid(k, kBlockThreads, smem, p.v1 - p.v0);
+        k<<<grid, kBlockThreads, smem, s>>>(p);
+        DANCE_LAUNCHED();
+        return 0;
+    }
+
+    // uint8: occlusion predicates from the tensor-core Gram matrix
+    static int run_gram(PruneParams p, cudaStream_t s)
+    {
+        auto k = prune_gram_kernel<CPL>;
+        p.Cp = (uint32_t)next_pow2((int)p.C);
+        if (p.Cp < 32)
+            p.Cp = 32;
+        p.per_warp = align16(gram_prune_smem_per_warp(p.C, p.Cp, p.R, p.row_bytes));
         const size_t smem = (size_t)p.per_warp * kWarpsPerBlock;
         if ((int)smem > max_optin_smem())
             return fail(-1, "prune vector cache %zu B exceeds shared memory", smem);
