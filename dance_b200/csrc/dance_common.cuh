@@ -214,29 +214,106 @@ __device__ __forceinline__ void eval_candidates(const uint8_t *__restrict__ data
     constexpr int U = Unroll<CPL>::value;
     const int g = lane >> 3;
     const int gl = lane & 7;
-    for (int base = 0; base < m; base += 4 * U)
+    if constexpr (DT == kU8 && U == 8)
     {
-        uint4 buf[U][CPL];
+        // uint8, 8 candidates per group and pass: each lane accumulates
+        // |q|^2 + |c|^2 - 2<q,c> over its part of every candidate (exact
+        // integers, so equal to the sum of squared differences), and one
+        // transposing butterfly leaves candidate gl's total in lane gl.
+        uint32_t qq = 0;
 #pragma unroll
-        for (int u = 0; u < U; ++u)
+        for (int t = 0; t < CPL; ++t)
         {
-            const int idx = base + 4 * u + g;
-            if (idx < m)
-                load_frag<CPL>(buf[u], data + (uint64_t)bid[idx] * stride, nchunks, gl);
-            else
+            qq = __dp4a(q[t].x, q[t].x, qq);
+            qq = __dp4a(q[t].y, q[t].y, qq);
+            qq = __dp4a(q[t].z, q[t].z, qq);
+            qq = __dp4a(q[t].w, q[t].w, qq);
+        }
+        const bool h4 = gl & 4, h2 = gl & 2, h1 = gl & 1;
+        for (int base = 0; base < m; base += 32)
+        {
+            uint4 buf[8][CPL];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
             {
+                const int idx = base + 4 * u + g;
+                if (idx < m)
+                    load_frag<CPL>(buf[u], data + (uint64_t)bid[idx] * stride, nchunks, gl);
+                else
+                {
+#pragma unroll
+                    for (int t = 0; t < CPL; ++t)
+                        buf[u][t] = make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
+            uint32_t part[8];
+#pragma unroll
+            for (int u = 0; u < 8; ++u)
+            {
+                uint32_t cc = qq, qc = 0;
 #pragma unroll
                 for (int t = 0; t < CPL; ++t)
-                    buf[u][t] = make_uint4(0u, 0u, 0u, 0u);
+                {
+                    cc = __dp4a(buf[u][t].x, buf[u][t].x, cc);
+                    cc = __dp4a(buf[u][t].y, buf[u][t].y, cc);
+                    cc = __dp4a(buf[u][t].z, buf[u][t].z, cc);
+                    cc = __dp4a(buf[u][t].w, buf[u][t].w, cc);
+                    qc = __dp4a(q[t].x, buf[u][t].x, qc);
+                    qc = __dp4a(q[t].y, buf[u][t].y, qc);
+                    qc = __dp4a(q[t].z, buf[u][t].z, qc);
+                    qc = __dp4a(q[t].w, buf[u][t].w, qc);
+                }
+                part[u] = cc - 2u * qc;
             }
-        }
+            uint32_t w4[4], w2[2];
 #pragma unroll
-        for (int u = 0; u < U; ++u)
+            for (int k = 0; k < 4; ++k)
+            {
+                const uint32_t send = h4 ? part[k] : part[k + 4];
+                const uint32_t keep = h4 ? part[k + 4] : part[k];
+                w4[k] = keep + __shfl_xor_sync(kFull, send, 4);
+            }
+#pragma unroll
+            for (int k = 0; k < 2; ++k)
+            {
+                const uint32_t send = h2 ? w4[k] : w4[k + 2];
+                const uint32_t keep = h2 ? w4[k + 2] : w4[k];
+                w2[k] = keep + __shfl_xor_sync(kFull, send, 2);
+            }
+            const uint32_t send = h1 ? w2[0] : w2[1];
+            const uint32_t keep = h1 ? w2[1] : w2[0];
+            const uint32_t tot = keep + __shfl_xor_sync(kFull, send, 1);
+            const int idx = base + 4 * gl + g; // this lane's total is candidate u = gl
+            if (idx < m)
+                bd[idx] = (float)(int32_t)tot;
+        }
+    }
+    else
+    {
+        for (int base = 0; base < m; base += 4 * U)
         {
-            const int idx = base + 4 * u + g;
-            const float d = GroupDist<DT, CPL>::eval(q, buf[u], nchunks, gl);
-            if (idx < m && gl == 0)
-                bd[idx] = d;
+            uint4 buf[U][CPL];
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+            {
+                const int idx = base + 4 * u + g;
+                if (idx < m)
+                    load_frag<CPL>(buf[u], data + (uint64_t)bid[idx] * stride, nchunks, gl);
+                else
+                {
+#pragma unroll
+                    for (int t = 0; t < CPL; ++t)
+                        buf[u][t] = make_uint4(0u, 0u, 0u, 0u);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+            {
+                const int idx = base + 4 * u + g;
+                const float d = GroupDist<DT, CPL>::eval(q, buf[u], nchunks, gl);
+                if (idx < m && gl == 0)
+                    bd[idx] = d;
+            }
         }
     }
 }

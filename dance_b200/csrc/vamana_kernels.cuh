@@ -51,23 +51,21 @@ __device__ __forceinline__ uint32_t visited_slot(uint32_t id, uint32_t log2h)
 // Per-warp scratch of the search kernels.
 struct SearchSmem
 {
-    uint64_t *pk0;  // two pool key buffers of Lcap keys, sorted ascending
-    uint8_t *pf0;   // two expanded-flag buffers aligned with the keys
+    uint64_t *pk;   // pool keys (Lcap), sorted ascending
+    uint8_t *pf;    // expanded flags aligned with the keys
     uint32_t Lcap;
     uint32_t *bid;  // batch ids (64)
     float *bd;      // batch distances (64)
     uint64_t *bkey; // survivor keys (64), sorted before the merge
     uint32_t *bins; // survivors' insertion points in the pool (64)
     uint32_t *vis;  // visited table (1 << log2h ids)
-    __device__ __forceinline__ uint64_t *pk(int b) const { return pk0 + (uint32_t)b * Lcap; }
-    __device__ __forceinline__ uint8_t *pf(int b) const { return pf0 + (uint32_t)b * Lcap; }
 };
 
 __host__ __device__ __forceinline__ uint32_t align16(uint32_t x) { return (x + 15u) & ~15u; }
 
 __host__ __device__ __forceinline__ uint32_t search_smem_per_warp(uint32_t Lcap, uint32_t log2h)
 {
-    return align16(16u * Lcap) + align16(2u * Lcap) + 256u + 256u + 512u + 256u + align16(4u << log2h);
+    return align16(8u * Lcap) + align16(Lcap) + 256u + 256u + 512u + 256u + align16(4u << log2h);
 }
 
 __device__ __forceinline__ SearchSmem carve_search_smem(uint8_t *base, uint32_t Lcap, uint32_t log2h)
@@ -75,10 +73,10 @@ __device__ __forceinline__ SearchSmem carve_search_smem(uint8_t *base, uint32_t 
     SearchSmem s;
     uint8_t *p = base;
     s.Lcap = Lcap;
-    s.pk0 = reinterpret_cast<uint64_t *>(p);
-    p += align16(16u * Lcap);
-    s.pf0 = p;
-    p += align16(2u * Lcap);
+    s.pk = reinterpret_cast<uint64_t *>(p);
+    p += align16(8u * Lcap);
+    s.pf = p;
+    p += align16(Lcap);
     s.bid = reinterpret_cast<uint32_t *>(p);
     p += 256;
     s.bd = reinterpret_cast<float *>(p);
@@ -97,7 +95,6 @@ struct PoolState
     int P;   // entries in the pool
     int L;   // capacity
     int lb;  // every entry below lb is expanded
-    int cur; // which key/flag buffer holds the pool
 };
 
 // Number of elements of sorted a[0..n) that are <= x.
@@ -116,31 +113,50 @@ __device__ __forceinline__ int upper_bound_u32(const uint32_t *a, int n, uint32_
 }
 
 // Merges m2 sorted, distinct survivor keys sm.bkey[0..m2) (whose pool
-// insertion points are sm.bins[0..m2)) with the pool into the other buffer.
+// insertion points are sm.bins[0..m2), ascending) into the pool in place.
+// Entries below the first insertion point stay; the rest move up by the
+// number of survivors inserted at or below them, 32 at a time from the top
+// (a chunk is read whole before it is written, and nothing lands below it).
 __device__ __forceinline__ void pool_merge(const SearchSmem &sm, PoolState &ps, int m2, int lane)
 {
-    const uint64_t *pk = sm.pk(ps.cur);
-    const uint8_t *pf = sm.pf(ps.cur);
-    const int nxt = ps.cur ^ 1;
-    uint64_t *ok = sm.pk(nxt);
-    uint8_t *of = sm.pf(nxt);
-    for (int i = lane; i < ps.P; i += 32)
+    uint64_t *pk = sm.pk;
+    uint8_t *pf = sm.pf;
+    const int lo = (int)sm.bins[0];
+    uint32_t b[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+        b[j] = (m2 <= 8 && j < m2) ? sm.bins[j] : 0xFFFFFFFFu;
+    if (ps.P > lo)
     {
-        int shift;
-        if (m2 <= 8)
+        for (int c0 = lo + ((ps.P - 1 - lo) & ~31); c0 >= lo; c0 -= 32)
         {
-            shift = 0;
-#pragma unroll 8
-            for (int j = 0; j < 8; ++j)
-                shift += (j < m2) && (sm.bins[j] <= (uint32_t)i);
-        }
-        else
-            shift = upper_bound_u32(sm.bins, m2, (uint32_t)i);
-        const int np = i + shift;
-        if (np < ps.L)
-        {
-            ok[np] = pk[i];
-            of[np] = pf[i];
+            const int i = c0 + lane;
+            int np = ps.L;
+            uint64_t key = 0;
+            uint8_t flag = 0;
+            if (i < ps.P)
+            {
+                int shift;
+                if (m2 <= 8)
+                {
+                    shift = 0;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        shift += b[j] <= (uint32_t)i;
+                }
+                else
+                    shift = upper_bound_u32(sm.bins, m2, (uint32_t)i);
+                np = i + shift;
+                key = pk[i];
+                flag = pf[i];
+            }
+            __syncwarp();
+            if (np < ps.L)
+            {
+                pk[np] = key;
+                pf[np] = flag;
+            }
+            __syncwarp();
         }
     }
     for (int j = lane; j < m2; j += 32)
@@ -148,14 +164,13 @@ __device__ __forceinline__ void pool_merge(const SearchSmem &sm, PoolState &ps, 
         const int np = j + (int)sm.bins[j];
         if (np < ps.L)
         {
-            ok[np] = sm.bkey[j];
-            of[np] = 0;
+            pk[np] = sm.bkey[j];
+            pf[np] = 0;
         }
     }
     __syncwarp();
-    ps.lb = min(ps.lb, (int)sm.bins[0]);
+    ps.lb = min(ps.lb, lo);
     ps.P = min(ps.P + m2, ps.L);
-    ps.cur = nxt;
 }
 
 // Inserts up to 64 candidates (two per lane; kInvalid = none) into the pool.
@@ -213,7 +228,7 @@ __device__ __forceinline__ int pool_insert_batch(const SearchSmem &sm, PoolState
         eval_candidates<DT, CPL>(st.data, st.stride, st.nchunks, q, sm.bid, sm.bd, m, lane);
         __syncwarp();
     }
-    const uint64_t *pool = sm.pk(ps.cur);
+    const uint64_t *pool = sm.pk;
     const uint64_t maxk = (ps.P >= ps.L) ? pool[ps.L - 1] : kKeyMax;
     const int e0 = lane, e1 = lane + 32;
     uint64_t k0 = e0 < m ? make_key(sm.bd[e0], sm.bid[e0]) : kKeyMax;
@@ -322,7 +337,7 @@ __device__ __forceinline__ int pool_select(const SearchSmem &sm, PoolState &ps, 
     for (int base = ps.lb; base < ps.P; base += 32)
     {
         const int i = base + lane;
-        const bool u = i < ps.P && sm.pf(ps.cur)[i] == 0;
+        const bool u = i < ps.P && sm.pf[i] == 0;
         const unsigned m = __ballot_sync(kFull, u);
         if (m)
         {
@@ -546,7 +561,7 @@ __global__ void __launch_bounds__(kBlockThreads, DANCE_SEARCH_MIN_BLOCKS) search
         uint4 q[CPL];
         load_frag<CPL>(q, st.data + (uint64_t)v * st.stride, st.nchunks, gl);
         clear_visited(sm.vis, p.log2h, lane);
-        PoolState ps{0, (int)p.L, 0, 0};
+        PoolState ps{0, (int)p.L, 0};
 
         // Seeds: entry point and hash seeds (distances computed) ...
         uint32_t sid = kInvalid;
@@ -594,11 +609,11 @@ __global__ void __launch_bounds__(kBlockThreads, DANCE_SEARCH_MIN_BLOCKS) search
             const int sel = pool_select(sm, ps, lane);
             if (sel < 0)
                 break;
-            const uint64_t key = sm.pk(ps.cur)[sel];
+            const uint64_t key = sm.pk[sel];
             const uint32_t x = key_id(key);
             if (lane == 0)
             {
-                sm.pf(ps.cur)[sel] = 1;
+                sm.pf[sel] = 1;
                 p.exp_ids[(uint64_t)(v - p.lrow0) * p.exp_stride + step] = x;
                 p.exp_dists[(uint64_t)(v - p.lrow0) * p.exp_stride + step] = key_dist(key);
             }
@@ -672,7 +687,7 @@ __global__ void __launch_bounds__(kBlockThreads, DANCE_SEARCH_MIN_BLOCKS) query_
         uint4 q[CPL];
         load_frag<CPL>(q, p.queries + (uint64_t)qi * p.qstride, p.st.nchunks, gl);
         clear_visited(sm.vis, p.log2h, lane);
-        PoolState ps{0, (int)p.L, 0, 0};
+        PoolState ps{0, (int)p.L, 0};
         const uint32_t start = p.query_start ? p.query_start[qi] : p.start;
         const uint32_t qlabel = p.query_label ? p.query_label[qi] : kInvalid;
         const uint32_t s0 = (lane == 0 && start < N) ? start : kInvalid;
@@ -682,9 +697,9 @@ __global__ void __launch_bounds__(kBlockThreads, DANCE_SEARCH_MIN_BLOCKS) query_
             const int sel = pool_select(sm, ps, lane);
             if (sel < 0)
                 break;
-            const uint32_t x = key_id(sm.pk(ps.cur)[sel]);
+            const uint32_t x = key_id(sm.pk[sel]);
             if (lane == 0)
-                sm.pf(ps.cur)[sel] = 1;
+                sm.pf[sel] = 1;
             __syncwarp();
             const uint32_t *row = p.graph + (uint64_t)x * p.R;
             for (uint32_t b = 0; b < p.R; b += 64)
@@ -702,7 +717,7 @@ __global__ void __launch_bounds__(kBlockThreads, DANCE_SEARCH_MIN_BLOCKS) query_
         for (uint32_t k = lane; k < p.K; k += 32)
         {
             const bool have = (int)k < ps.P;
-            const uint64_t key = have ? sm.pk(ps.cur)[k] : kKeyMax;
+            const uint64_t key = have ? sm.pk[k] : kKeyMax;
             p.out_ids[(uint64_t)qi * p.K + k] = have ? key_id(key) : kInvalid;
             p.out_dists[(uint64_t)qi * p.K + k] = have ? key_dist(key) : FLT_MAX;
         }
