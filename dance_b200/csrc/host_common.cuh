@@ -251,7 +251,7 @@ struct LaunchReplay
     static int run(ReplayParams p, cudaStream_t s)
     {
         auto k = replay_kernel<DT, CPL>;
-        p.per_warp = align16(replay_smem_per_warp(p.C, p.cache_rows, p.row_bytes));
+        p.per_warp = align16(replay_smem_per_warp(p.C, p.cache_rows, p.row_bytes, p.exp_stride));
         const size_t smem = (size_t)p.per_warp * kWarpsPerBlock;
         if ((int)smem > max_optin_smem())
             return fail(-1, "replay vector cache %zu B exceeds shared memory (R+steps=%u rows of %u B)", smem,

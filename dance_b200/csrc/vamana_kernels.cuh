@@ -749,11 +749,42 @@ struct ReplayParams
     unsigned long long *counters; // [2] pair evaluations
 };
 
-__host__ __device__ __forceinline__ uint32_t replay_smem_per_warp(uint32_t C, uint32_t cache_rows, uint32_t row_bytes)
+// Per-warp scratch of replay_kernel: the vector cache (initial neighbours,
+// then the expanded nodes in order; before the gather it holds the initial
+// sort keys), the gather ids, the work row by slot (ids, distances), the
+// kept slots in order (distance, cache row, slot) and the expansion list.
+struct ReplayLayout
 {
-    const uint32_t Cp = C <= 32 ? 32u : (uint32_t)next_pow2((int)C);
-    return cache_rows * row_bytes + align16(4u * cache_rows) + align16(4u * C) + align16(4u * C) + align16(2u * C) +
-           2u * align16(2u * C) + align16(8u * Cp);
+    uint32_t gid, wid, wd, od, ou, os, xid, xdd, bytes;
+    __host__ __device__ ReplayLayout(uint32_t C, uint32_t cache_rows, uint32_t row_bytes, uint32_t exp_stride)
+    {
+        const uint32_t Cp = C <= 32 ? 32u : (uint32_t)next_pow2((int)C);
+        const uint32_t cache_bytes = cache_rows * row_bytes;
+        uint32_t o = align16(cache_bytes > 8u * Cp ? cache_bytes : 8u * Cp);
+        gid = o;
+        o += align16(4u * cache_rows);
+        wid = o;
+        o += align16(4u * C);
+        wd = o;
+        o += align16(4u * C);
+        od = o;
+        o += align16(4u * C);
+        ou = o;
+        o += align16(2u * C);
+        os = o;
+        o += align16(2u * C);
+        xid = o;
+        o += align16(4u * exp_stride);
+        xdd = o;
+        o += align16(4u * exp_stride);
+        bytes = o;
+    }
+};
+
+__host__ __device__ __forceinline__ uint32_t replay_smem_per_warp(uint32_t C, uint32_t cache_rows, uint32_t row_bytes,
+                                                                  uint32_t exp_stride)
+{
+    return ReplayLayout(C, cache_rows, row_bytes, exp_stride).bytes;
 }
 
 // Warp argmax over (value, slot) pairs: larger value wins, lower slot on ties.
@@ -802,39 +833,112 @@ __device__ __forceinline__ uint64_t order_key(float d, uint32_t slot)
     return ((uint64_t)(~__float_as_uint(d)) << 32) | slot;
 }
 
+// Pair distances of the replay: x (one cached row) against up to kPairs
+// cached rows per warp pass.  uint8 rows of at most 128 bytes use four lanes
+// per pair (eight pairs a pass; the two 16-byte chunks of a lane are read in
+// an order that keeps each 8-lane phase on distinct banks); the other types
+// use the 8-lane groups of GroupDist, whose summation order is the
+// reference's.
+template <int DT, int CPL>
+struct ReplayPairs
+{
+    static constexpr bool kQuad = (DT == kU8 && CPL == 1);
+    static constexpr int kPairs = kQuad ? 8 : 4;
+    static constexpr int kLanes = 32 / kPairs;
+    uint4 xf[kQuad ? 2 : CPL];
+    int pidx, sl;
+    uint32_t c0, c1;
+
+    __device__ __forceinline__ ReplayPairs(int lane)
+    {
+        pidx = lane / kLanes;
+        sl = lane % kLanes;
+        c0 = (uint32_t)sl + 4u * (uint32_t)(pidx & 1);
+        c1 = c0 ^ 4u;
+    }
+    __device__ __forceinline__ void load_x(const uint8_t *row, uint32_t nchunks)
+    {
+        if constexpr (kQuad)
+        {
+            const uint4 *r = reinterpret_cast<const uint4 *>(row);
+            xf[0] = c0 < nchunks ? r[c0] : make_uint4(0u, 0u, 0u, 0u);
+            xf[1] = c1 < nchunks ? r[c1] : make_uint4(0u, 0u, 0u, 0u);
+        }
+        else
+            load_frag_smem<CPL>(xf, row, nchunks, sl);
+    }
+    __device__ __forceinline__ static uint32_t sqdiff16(const uint4 &a, const uint4 &b, uint32_t acc)
+    {
+        uint32_t t = __vabsdiffu4(a.x, b.x);
+        acc = __dp4a(t, t, acc);
+        t = __vabsdiffu4(a.y, b.y);
+        acc = __dp4a(t, t, acc);
+        t = __vabsdiffu4(a.z, b.z);
+        acc = __dp4a(t, t, acc);
+        t = __vabsdiffu4(a.w, b.w);
+        acc = __dp4a(t, t, acc);
+        return acc;
+    }
+    // d(x, row); every lane of the pair ends with the value.
+    __device__ __forceinline__ float dist(const uint8_t *row, uint32_t nchunks) const
+    {
+        if constexpr (kQuad)
+        {
+            const uint4 *r = reinterpret_cast<const uint4 *>(row);
+            uint32_t acc = 0;
+            if (c0 < nchunks)
+                acc = sqdiff16(xf[0], r[c0], acc);
+            if (c1 < nchunks)
+                acc = sqdiff16(xf[1], r[c1], acc);
+            acc += __shfl_xor_sync(kFull, acc, 1);
+            acc += __shfl_xor_sync(kFull, acc, 2);
+            return (float)(int32_t)acc;
+        }
+        else
+        {
+            uint4 c[CPL];
+            load_frag_smem<CPL>(c, row, nchunks, sl);
+            return GroupDist<DT, CPL>::eval(xf, c, nchunks, sl);
+        }
+    }
+};
+
 // Online RobustInsert replay (reference dynamic_robust_insert_C_warp,
 // src/gpu_vamana_vnew2.cu:759-877) of each vertex's recorded expansion
 // sequence into its C-wide work row.  One warp per vertex; the row's
 // vectors (initial neighbours and expanded nodes) are cached in shared
-// memory, and the valid slots are kept in ord[] sorted by order_key, so
+// memory, and the kept slots are held in order of order_key (distance
+// descending, slot ascending) as parallel arrays (distance, cache row,
+// slot), so
 //  - occlusion is tested from the nearest kept neighbour outwards and stops
 //    at the first occluder,
 //  - the victim is the first qualifying slot from the far end,
-//  - the worst slot is ord[0].
+//  - the worst slot is position 0,
+// and an insertion moves only the positions between its old and new place.
 template <int DT, int CPL>
 __global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
 {
+    using Pairs = ReplayPairs<DT, CPL>;
     extern __shared__ __align__(16) uint8_t smem_raw[];
     const int lane = lane_id();
-    const int g = lane >> 3, gl = lane & 7;
     const uint32_t C = p.C;
     const uint32_t Cp = C <= 32 ? 32u : (uint32_t)next_pow2((int)C);
+    const ReplayLayout lay(C, p.cache_rows, p.row_bytes, p.exp_stride);
     uint8_t *base = smem_raw + warp_id_in_block() * p.per_warp;
     uint8_t *cache = base;
-    uint8_t *q = cache + p.cache_rows * p.row_bytes;
-    uint32_t *gid = reinterpret_cast<uint32_t *>(q);
-    q += align16(4u * p.cache_rows);
-    uint32_t *wid = reinterpret_cast<uint32_t *>(q);
-    q += align16(4u * C);
-    float *wd = reinterpret_cast<float *>(q);
-    q += align16(4u * C);
-    uint16_t *wu = reinterpret_cast<uint16_t *>(q);
-    q += align16(2u * C);
-    uint16_t *ordb = reinterpret_cast<uint16_t *>(q); // two buffers of C slots
-    const uint32_t ordstride = align16(2u * C) / 2u;
-    q += 2u * align16(2u * C);
-    uint64_t *okeys = reinterpret_cast<uint64_t *>(q); // Cp, initial sort
+    uint32_t *gid = reinterpret_cast<uint32_t *>(base + lay.gid);
+    uint32_t *wid = reinterpret_cast<uint32_t *>(base + lay.wid);
+    float *wd = reinterpret_cast<float *>(base + lay.wd);
+    float *od = reinterpret_cast<float *>(base + lay.od);
+    uint16_t *ou = reinterpret_cast<uint16_t *>(base + lay.ou);
+    uint16_t *os = reinterpret_cast<uint16_t *>(base + lay.os);
+    uint32_t *xid = reinterpret_cast<uint32_t *>(base + lay.xid);
+    float *xdd = reinterpret_cast<float *>(base + lay.xdd);
+    uint64_t *okeys = reinterpret_cast<uint64_t *>(base); // initial sort, before the gather
     const uint32_t N = p.st.N;
+    const uint32_t nch = p.st.nchunks;
+    const float alpha = p.alpha;
+    Pairs pe(lane);
     unsigned long long pairs = 0;
 
     for (uint32_t v = p.v0 + blockIdx.x * kWarpsPerBlock + warp_id_in_block(); v < p.v1;
@@ -846,7 +950,6 @@ __global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
         {
             uint32_t nb = kInvalid;
             float d = FLT_MAX;
-            uint16_t u = 0xFFFFu;
             uint64_t ok = kKeyMax;
             if (i < deg_self)
             {
@@ -854,7 +957,6 @@ __global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
                 if (nb < N && nb != v)
                 {
                     d = p.cur_dists[lv * p.R + i];
-                    u = (uint16_t)i;
                     ok = order_key(d, i);
                 }
                 else
@@ -864,7 +966,6 @@ __global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
             {
                 wid[i] = nb;
                 wd[i] = d;
-                wu[i] = u;
             }
             okeys[i] = ok;
         }
@@ -880,66 +981,63 @@ __global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
         }
         __syncwarp();
         warp_sort_smem_u64(okeys, (int)Cp, lane);
+        // kept slots in order; their initial cache row is the slot itself
         int nv = 0;
         for (uint32_t b = 0; b < Cp; b += 32)
-            nv += __popc(__ballot_sync(kFull, okeys[b + lane] != kKeyMax));
-        int ob = 0;
-        for (int j = lane; j < nv; j += 32)
-            ordb[j] = (uint16_t)(okeys[j] & 0xFFFFu);
-        gather_rows_grouped<CPL>(p.st.data, p.st.stride, p.st.nchunks, gid, (int)deg_self, cache, p.row_bytes, lane);
-        gather_rows_grouped<CPL>(p.st.data, p.st.stride, p.st.nchunks, gid + p.R, (int)cnt,
-                                 cache + p.R * p.row_bytes, p.row_bytes, lane);
+        {
+            const uint64_t k = okeys[b + lane];
+            const bool valid = k != kKeyMax;
+            nv += __popc(__ballot_sync(kFull, valid));
+            if (valid)
+            {
+                const uint32_t slot = (uint32_t)(k & 0xFFFFu);
+                od[b + lane] = wd[slot];
+                ou[b + lane] = (uint16_t)slot;
+                os[b + lane] = (uint16_t)slot;
+            }
+        }
+        for (uint32_t k = lane; k < cnt; k += 32)
+        {
+            xid[k] = p.exp_ids[lv * p.exp_stride + k];
+            xdd[k] = p.exp_dists[lv * p.exp_stride + k];
+        }
+        __syncwarp(); // the sort keys are read: the cache may be filled
+        gather_rows_grouped<CPL>(p.st.data, p.st.stride, nch, gid, (int)deg_self, cache, p.row_bytes, lane);
+        gather_rows_grouped<CPL>(p.st.data, p.st.stride, nch, gid + p.R, (int)cnt, cache + p.R * p.row_bytes,
+                                 p.row_bytes, lane);
         __syncwarp();
         uint32_t wdeg = deg_self;
 
         for (uint32_t k = 0; k < cnt; ++k)
         {
-            const uint32_t x = p.exp_ids[lv * p.exp_stride + k];
-            const float dx = p.exp_dists[lv * p.exp_stride + k];
+            const uint32_t x = xid[k];
+            const float dx = xdd[k];
             if (x >= N || x == v)
                 continue;
             const uint32_t deg = min(wdeg, C);
+            // already in the row?  and ngt: positions [0, ngt) have d(v,y) > d(v,x)
             bool present = false;
+            int ngt = 0;
             for (uint32_t b = 0; b < deg; b += 32)
             {
                 const uint32_t i = b + lane;
-                if (__any_sync(kFull, i < deg && wid[i] == x))
-                {
-                    present = true;
-                    break;
-                }
+                present |= i < deg && wid[i] == x;
+                ngt += __popc(__ballot_sync(kFull, (int)i < nv && od[i] > dx));
             }
-            if (present)
+            if (__any_sync(kFull, present))
                 continue;
-            const uint16_t *ord = ordb + ob * ordstride;
-            // ord[0, ngt) have d(v,y) > d(v,x); ord[ngt, nv) have d(v,y) <= d(v,x)
-            int ngt = 0;
-            for (int b = 0; b < nv; b += 32)
-            {
-                const int j = b + lane;
-                ngt += __popc(__ballot_sync(kFull, j < nv && wd[ord[j]] > dx));
-            }
-            uint4 xf[CPL];
-            load_frag_smem<CPL>(xf, cache + (p.R + k) * p.row_bytes, p.st.nchunks, gl);
+            pe.load_x(cache + (p.R + k) * p.row_bytes, nch);
             // occlusion: nearest kept neighbours first
             bool occluded = false;
-            for (int b = nv - 1; b >= ngt; b -= 4)
+            for (int b = nv - 1; b >= ngt; b -= Pairs::kPairs)
             {
-                const int j = b - g;
-                uint4 c[CPL];
+                const int j = b - pe.pidx;
                 const bool act = j >= ngt;
-                if (act)
-                    load_frag_smem<CPL>(c, cache + (uint32_t)wu[ord[j]] * p.row_bytes, p.st.nchunks, gl);
-                else
-                {
-#pragma unroll
-                    for (int t = 0; t < CPL; ++t)
-                        c[t] = make_uint4(0u, 0u, 0u, 0u);
-                }
-                const float d = GroupDist<DT, CPL>::eval(xf, c, p.st.nchunks, gl);
+                const uint32_t u = act ? ou[j] : 0u;
+                const float d = pe.dist(cache + u * p.row_bytes, nch);
                 if (lane == 0)
-                    pairs += (unsigned long long)min(4, b - ngt + 1);
-                if (__any_sync(kFull, act && gl == 0 && __fmul_rn(p.alpha, d) <= dx))
+                    pairs += (unsigned long long)min(Pairs::kPairs, b - ngt + 1);
+                if (__any_sync(kFull, act && pe.sl == 0 && __fmul_rn(alpha, d) <= dx))
                 {
                     occluded = true;
                     break;
@@ -947,35 +1045,28 @@ __global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
             }
             if (occluded)
                 continue;
-            // victim: the first slot from the far end with alpha*d(x,y) <= d(v,y)
+            // victim: the first position from the far end with alpha*d(x,y) <= d(v,y)
             int vj = -1;
-            for (int b = 0; b < ngt; b += 4)
+            for (int b = 0; b < ngt; b += Pairs::kPairs)
             {
-                const int j = b + g;
-                uint4 c[CPL];
+                const int j = b + pe.pidx;
                 const bool act = j < ngt;
-                if (act)
-                    load_frag_smem<CPL>(c, cache + (uint32_t)wu[ord[j]] * p.row_bytes, p.st.nchunks, gl);
-                else
-                {
-#pragma unroll
-                    for (int t = 0; t < CPL; ++t)
-                        c[t] = make_uint4(0u, 0u, 0u, 0u);
-                }
-                const float d = GroupDist<DT, CPL>::eval(xf, c, p.st.nchunks, gl);
+                const uint32_t u = act ? ou[j] : 0u;
+                const float dy = act ? od[j] : 0.0f;
+                const float d = pe.dist(cache + u * p.row_bytes, nch);
                 if (lane == 0)
-                    pairs += (unsigned long long)min(4, ngt - b);
-                const unsigned hit = __ballot_sync(kFull, act && gl == 0 && __fmul_rn(p.alpha, d) <= wd[ord[j]]);
+                    pairs += (unsigned long long)min(Pairs::kPairs, ngt - b);
+                const unsigned hit = __ballot_sync(kFull, act && pe.sl == 0 && __fmul_rn(alpha, d) <= dy);
                 if (hit)
                 {
-                    vj = b + ((__ffs(hit) - 1) >> 3);
+                    vj = b + (__ffs(hit) - 1) / Pairs::kLanes;
                     break;
                 }
             }
             int slot = -1, pr = -1;
             if (vj >= 0)
             {
-                slot = ord[vj];
+                slot = os[vj];
                 pr = vj;
             }
             else if (deg < C)
@@ -983,38 +1074,81 @@ __global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
                 slot = (int)deg;
                 wdeg = deg + 1;
             }
-            else if (nv > 0 && dx < wd[ord[0]])
+            else if (nv > 0 && dx < od[0])
             {
-                slot = ord[0];
+                slot = os[0];
                 pr = 0;
             }
             if (slot < 0)
                 continue;
-            // new order: drop position pr, insert the slot at its key
+            // new position of the slot among the others
             const uint64_t kn = order_key(dx, (uint32_t)slot);
             int pn = 0;
             for (int b = 0; b < nv; b += 32)
             {
                 const int j = b + lane;
-                pn += __popc(__ballot_sync(kFull, j < nv && j != pr && order_key(wd[ord[j]], ord[j]) < kn));
+                pn += __popc(__ballot_sync(kFull, j < nv && j != pr && order_key(od[j], os[j]) < kn));
             }
-            uint16_t *nord = ordb + (ob ^ 1) * ordstride;
-            for (int j = lane; j < nv; j += 32)
+            if (pr >= 0)
             {
-                if (j == pr)
-                    continue;
-                const int j1 = j - ((pr >= 0 && j > pr) ? 1 : 0);
-                nord[j1 + (j1 >= pn ? 1 : 0)] = ord[j];
+                // replaced entry moves from pr to pn >= pr: positions (pr, pn] move down one
+                for (int c0 = pr; c0 < pn; c0 += 32)
+                {
+                    const int i = c0 + lane;
+                    float dd = 0.0f;
+                    uint16_t uu = 0, ss = 0;
+                    if (i < pn)
+                    {
+                        dd = od[i + 1];
+                        uu = ou[i + 1];
+                        ss = os[i + 1];
+                    }
+                    __syncwarp();
+                    if (i < pn)
+                    {
+                        od[i] = dd;
+                        ou[i] = uu;
+                        os[i] = ss;
+                    }
+                    __syncwarp();
+                }
+            }
+            else
+            {
+                // appended entry: positions [pn, nv) move up one, from the top
+                if (nv > pn)
+                {
+                    for (int c0 = pn + ((nv - 1 - pn) & ~31); c0 >= pn; c0 -= 32)
+                    {
+                        const int i = c0 + lane;
+                        float dd = 0.0f;
+                        uint16_t uu = 0, ss = 0;
+                        if (i < nv)
+                        {
+                            dd = od[i];
+                            uu = ou[i];
+                            ss = os[i];
+                        }
+                        __syncwarp();
+                        if (i < nv)
+                        {
+                            od[i + 1] = dd;
+                            ou[i + 1] = uu;
+                            os[i + 1] = ss;
+                        }
+                        __syncwarp();
+                    }
+                }
+                ++nv;
             }
             if (lane == 0)
             {
-                nord[pn] = (uint16_t)slot;
+                od[pn] = dx;
+                ou[pn] = (uint16_t)(p.R + k);
+                os[pn] = (uint16_t)slot;
                 wid[slot] = x;
                 wd[slot] = dx;
-                wu[slot] = (uint16_t)(p.R + k);
             }
-            nv += (pr >= 0) ? 0 : 1;
-            ob ^= 1;
             __syncwarp();
         }
         for (uint32_t i = lane; i < C; i += 32)
