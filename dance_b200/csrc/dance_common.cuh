@@ -361,6 +361,52 @@ __device__ __forceinline__ void gather_rows_to_smem(const uint8_t *__restrict__ 
 
 // ------------------------------------------------------------------ warp sorts
 // Ascending bitonic sort of 64 keys held two per lane (element 2*lane+s).
+// Ascending bitonic sort of 32*NPL keys held NPL per lane in blocked order
+// (element lane*NPL + s in k[s]): in-lane exchanges for distances below NPL,
+// xor shuffles above.
+template <int NPL>
+__device__ __forceinline__ void warp_sort_blocked(uint64_t (&k)[NPL], int lane)
+{
+    constexpr int n = 32 * NPL;
+#pragma unroll
+    for (int size = 2; size <= n; size <<= 1)
+    {
+#pragma unroll
+        for (int j = size >> 1; j > 0; j >>= 1)
+        {
+            if (j < NPL)
+            {
+#pragma unroll
+                for (int s = 0; s < NPL; ++s)
+                {
+                    const int t = s ^ j;
+                    if (t > s)
+                    {
+                        const bool asc = ((lane * NPL + s) & size) == 0;
+                        const uint64_t a = k[s], b = k[t];
+                        const bool sw = asc ? (a > b) : (a < b);
+                        k[s] = sw ? b : a;
+                        k[t] = sw ? a : b;
+                    }
+                }
+            }
+            else
+            {
+                const int lm = j / NPL;
+                const bool lower = (lane & lm) == 0;
+#pragma unroll
+                for (int s = 0; s < NPL; ++s)
+                {
+                    const bool asc = ((lane * NPL + s) & size) == 0;
+                    const uint64_t o = __shfl_xor_sync(kFull, k[s], lm);
+                    const bool take_min = lower == asc;
+                    k[s] = take_min ? (k[s] < o ? k[s] : o) : (k[s] > o ? k[s] : o);
+                }
+            }
+        }
+    }
+}
+
 __device__ __forceinline__ void warp_sort64(uint64_t &k0, uint64_t &k1, int lane)
 {
 #pragma unroll

@@ -322,7 +322,10 @@ struct LaunchPrune
         p.Cp = (uint32_t)next_pow2((int)p.C);
         if (p.Cp < 32)
             p.Cp = 32;
-        p.per_warp = align16(gram_prune_smem_per_warp(p.C, p.Cp, p.R, p.row_bytes));
+        const GramPruneLayout lay(p.C, p.row_bytes);
+        if (lay.staging > lay.rows * gram_stride(p.row_bytes))
+            return fail(-1, "prune staging %u B exceeds the vector cache", lay.staging);
+        p.per_warp = align16(lay.bytes);
         const size_t smem = (size_t)p.per_warp * kWarpsPerBlock;
         if ((int)smem > max_optin_smem())
             return fail(-1, "prune vector cache %zu B exceeds shared memory", smem);
