@@ -1783,9 +1783,13 @@ __global__ void __launch_bounds__(kMergeBlock) heavy_merge_kernel(MergeParams p)
 
 // Huge targets (more than kHeavySortCap sources, e.g. the medoid in the
 // first round, which enters almost every row): the segment is put in
-// ascending order in place by a counting sort over source ids, with 16-bit
-// counters in this block's slice of huge_scratch (kept all-zero between
-// uses), then merged by the block.
+// ascending order in place and merged by the block.  Unless the heavy cap
+// samples the segment, repeated sources are no-ops of the merge, so the
+// segment is reduced to its distinct sources through a bitmap over source
+// ids (N/32 words, a tenth of a pass over the counters below); a sampled
+// segment keeps its repeats through a counting sort with 16-bit counters.
+// Both live in this block's slice of huge_scratch, kept all-zero between
+// uses.
 template <int DT, int CPL>
 __global__ void __launch_bounds__(kMergeBlock) huge_merge_kernel(MergeParams p)
 {
@@ -1794,36 +1798,67 @@ __global__ void __launch_bounds__(kMergeBlock) huge_merge_kernel(MergeParams p)
     BlockMergeSmem sm = carve_block_merge(smem_raw, p.C, p.Cp);
     const uint32_t nhuge = *p.huge_count;
     const uint32_t words = (p.st.N + 1u) / 2u;
+    const uint32_t bwords = (p.st.N + 31u) / 32u;
     uint32_t *cnt = p.huge_scratch + (uint64_t)blockIdx.x * words;
     unsigned long long evals = 0;
     for (uint32_t h = blockIdx.x; h < nhuge; h += gridDim.x)
     {
         const uint32_t t = p.huge_list[h];
         const uint32_t beg = p.offsets[t - p.t0], end = p.offsets[t - p.t0 + 1];
-        const uint32_t n = end - beg;
+        uint32_t n = end - beg;
         uint32_t *seg = p.rev + beg;
-        for (uint32_t i = threadIdx.x; i < n; i += blockDim.x)
+        uint32_t count;
+        bool sampled;
+        merge_list_size(p, n, count, sampled);
+        if (!sampled)
         {
-            const uint32_t s = seg[i];
-            atomicAdd(&cnt[s >> 1], 1u << ((s & 1u) * 16u));
-        }
-        __syncthreads();
-        uint32_t base = 0;
-        for (uint32_t w0 = 0; w0 < words; w0 += blockDim.x)
-        {
-            const uint32_t wi = w0 + threadIdx.x;
-            const uint32_t v = wi < words ? cnt[wi] : 0u;
-            const uint32_t c0 = v & 0xFFFFu, c1 = v >> 16;
-            uint32_t total;
-            const uint32_t ex = block_exclusive_scan(c0 + c1, s_warp, total) + base;
-            for (uint32_t r = 0; r < c0; ++r)
-                seg[ex + r] = 2u * wi;
-            for (uint32_t r = 0; r < c1; ++r)
-                seg[ex + c0 + r] = 2u * wi + 1u;
-            if (v)
-                cnt[wi] = 0u;
-            base += total;
+            for (uint32_t i = threadIdx.x; i < n; i += blockDim.x)
+            {
+                const uint32_t s = seg[i];
+                atomicOr(&cnt[s >> 5], 1u << (s & 31u));
+            }
             __syncthreads();
+            uint32_t base = 0;
+            for (uint32_t w0 = 0; w0 < bwords; w0 += blockDim.x)
+            {
+                const uint32_t wi = w0 + threadIdx.x;
+                const uint32_t v = wi < bwords ? cnt[wi] : 0u;
+                uint32_t total;
+                uint32_t o = block_exclusive_scan(__popc(v), s_warp, total) + base;
+                for (uint32_t r = v; r; r &= r - 1u)
+                    seg[o++] = 32u * wi + (uint32_t)(__ffs(r) - 1);
+                if (v)
+                    cnt[wi] = 0u;
+                base += total;
+                __syncthreads();
+            }
+            n = base;
+        }
+        else
+        {
+            for (uint32_t i = threadIdx.x; i < n; i += blockDim.x)
+            {
+                const uint32_t s = seg[i];
+                atomicAdd(&cnt[s >> 1], 1u << ((s & 1u) * 16u));
+            }
+            __syncthreads();
+            uint32_t base = 0;
+            for (uint32_t w0 = 0; w0 < words; w0 += blockDim.x)
+            {
+                const uint32_t wi = w0 + threadIdx.x;
+                const uint32_t v = wi < words ? cnt[wi] : 0u;
+                const uint32_t c0 = v & 0xFFFFu, c1 = v >> 16;
+                uint32_t total;
+                const uint32_t ex = block_exclusive_scan(c0 + c1, s_warp, total) + base;
+                for (uint32_t r = 0; r < c0; ++r)
+                    seg[ex + r] = 2u * wi;
+                for (uint32_t r = 0; r < c1; ++r)
+                    seg[ex + c0 + r] = 2u * wi + 1u;
+                if (v)
+                    cnt[wi] = 0u;
+                base += total;
+                __syncthreads();
+            }
         }
         __syncthreads();
         merge_target_block<DT, CPL>(p, t, seg, n, sm.wid, sm.wd, sm.rsorted, sm.nl, sm.nd, sm.wcount, *sm.ms, evals);
