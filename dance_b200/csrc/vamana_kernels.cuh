@@ -751,17 +751,19 @@ struct ReplayParams
 
 // Per-warp scratch of replay_kernel: the vector cache (initial neighbours,
 // then the expanded nodes in order; before the gather it holds the initial
-// sort keys), the gather ids, the work row by slot (ids, distances), the
-// kept slots in order (distance, cache row, slot) and the expansion list.
+// sort keys when they are sorted in shared memory), the squared norms of the
+// cached rows (uint8 rows of at most 128 bytes), the work row by slot (ids,
+// distances), the kept slots in order (distance, cache row, slot) and the
+// expansion list.
 struct ReplayLayout
 {
-    uint32_t gid, wid, wd, od, ou, os, xid, xdd, bytes;
+    uint32_t norms, wid, wd, od, ou, os, xid, xdd, bytes;
     __host__ __device__ ReplayLayout(uint32_t C, uint32_t cache_rows, uint32_t row_bytes, uint32_t exp_stride)
     {
         const uint32_t Cp = C <= 32 ? 32u : (uint32_t)next_pow2((int)C);
         const uint32_t cache_bytes = cache_rows * row_bytes;
         uint32_t o = align16(cache_bytes > 8u * Cp ? cache_bytes : 8u * Cp);
-        gid = o;
+        norms = o;
         o += align16(4u * cache_rows);
         wid = o;
         o += align16(4u * C);
@@ -825,6 +827,54 @@ __device__ __forceinline__ void gather_rows_grouped(const uint8_t *__restrict__ 
     }
 }
 
+// Copies `count` rows (row k from vector id idf(k)) into the cache (row k,
+// row_bytes apart) with 8-lane groups, loading Unroll<CPL> rows per group
+// before storing any, so that the loads overlap.
+template <int CPL, class IdFn>
+__device__ __forceinline__ void gather_rows_batched(const uint8_t *__restrict__ data, uint64_t stride,
+                                                    uint32_t nchunks, int count, uint8_t *cache, uint32_t row_bytes,
+                                                    int lane, IdFn idf)
+{
+    constexpr int U = Unroll<CPL>::value;
+    const int g = lane >> 3, gl = lane & 7;
+    for (int r0 = 0; r0 < count; r0 += 4 * U)
+    {
+        uint4 buf[U][CPL];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+        {
+            const int r = r0 + 4 * u + g;
+            if (r < count)
+            {
+                const uint4 *src = reinterpret_cast<const uint4 *>(data + (uint64_t)idf(r) * stride);
+#pragma unroll
+                for (int t = 0; t < CPL; ++t)
+                {
+                    const uint32_t c = (uint32_t)(gl + 8 * t);
+                    if (c < nchunks)
+                        buf[u][t] = ldg_chunk(src + c);
+                }
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+        {
+            const int r = r0 + 4 * u + g;
+            if (r < count)
+            {
+                uint4 *dst = reinterpret_cast<uint4 *>(cache + (uint32_t)r * row_bytes);
+#pragma unroll
+                for (int t = 0; t < CPL; ++t)
+                {
+                    const uint32_t c = (uint32_t)(gl + 8 * t);
+                    if (c < nchunks)
+                        dst[c] = buf[u][t];
+                }
+            }
+        }
+    }
+}
+
 // Order key of a work-row slot: descending distance, then ascending slot --
 // the reference's preference for the victim and the worst entry
 // (src/gpu_vamana_vnew2.cu:816-846, strict '>' scans in slot order).
@@ -836,8 +886,9 @@ __device__ __forceinline__ uint64_t order_key(float d, uint32_t slot)
 // Pair distances of the replay: x (one cached row) against up to kPairs
 // cached rows per warp pass.  uint8 rows of at most 128 bytes use four lanes
 // per pair (eight pairs a pass; the two 16-byte chunks of a lane are read in
-// an order that keeps each 8-lane phase on distinct banks); the other types
-// use the 8-lane groups of GroupDist, whose summation order is the
+// an order that keeps each 8-lane phase on distinct banks) and the cached
+// squared norms: d = |x|^2 + |y|^2 - 2<x,y>, exact in integers.  The other
+// types use the 8-lane groups of GroupDist, whose summation order is the
 // reference's.
 template <int DT, int CPL>
 struct ReplayPairs
@@ -846,6 +897,7 @@ struct ReplayPairs
     static constexpr int kPairs = kQuad ? 8 : 4;
     static constexpr int kLanes = 32 / kPairs;
     uint4 xf[kQuad ? 2 : CPL];
+    uint32_t nx;
     int pidx, sl;
     uint32_t c0, c1;
 
@@ -855,44 +907,49 @@ struct ReplayPairs
         sl = lane % kLanes;
         c0 = (uint32_t)sl + 4u * (uint32_t)(pidx & 1);
         c1 = c0 ^ 4u;
+        nx = 0;
     }
-    __device__ __forceinline__ void load_x(const uint8_t *row, uint32_t nchunks)
+    __device__ __forceinline__ void load_x(const uint8_t *row, uint32_t nchunks, uint32_t norm)
     {
         if constexpr (kQuad)
         {
             const uint4 *r = reinterpret_cast<const uint4 *>(row);
             xf[0] = c0 < nchunks ? r[c0] : make_uint4(0u, 0u, 0u, 0u);
             xf[1] = c1 < nchunks ? r[c1] : make_uint4(0u, 0u, 0u, 0u);
+            nx = norm;
         }
         else
             load_frag_smem<CPL>(xf, row, nchunks, sl);
     }
-    __device__ __forceinline__ static uint32_t sqdiff16(const uint4 &a, const uint4 &b, uint32_t acc)
-    {
-        uint32_t t = __vabsdiffu4(a.x, b.x);
-        acc = __dp4a(t, t, acc);
-        t = __vabsdiffu4(a.y, b.y);
-        acc = __dp4a(t, t, acc);
-        t = __vabsdiffu4(a.z, b.z);
-        acc = __dp4a(t, t, acc);
-        t = __vabsdiffu4(a.w, b.w);
-        acc = __dp4a(t, t, acc);
-        return acc;
-    }
-    // d(x, row); every lane of the pair ends with the value.
-    __device__ __forceinline__ float dist(const uint8_t *row, uint32_t nchunks) const
+    // d(x, row) for the row in cache slot u; every lane of the pair ends with
+    // the value.
+    __device__ __forceinline__ float dist(const uint8_t *row, uint32_t nchunks, const uint32_t *norms,
+                                          uint32_t u) const
     {
         if constexpr (kQuad)
         {
             const uint4 *r = reinterpret_cast<const uint4 *>(row);
-            uint32_t acc = 0;
+            uint32_t a0 = 0, a1 = 0;
             if (c0 < nchunks)
-                acc = sqdiff16(xf[0], r[c0], acc);
+            {
+                const uint4 y = r[c0];
+                a0 = __dp4a(xf[0].x, y.x, a0);
+                a0 = __dp4a(xf[0].y, y.y, a0);
+                a0 = __dp4a(xf[0].z, y.z, a0);
+                a0 = __dp4a(xf[0].w, y.w, a0);
+            }
             if (c1 < nchunks)
-                acc = sqdiff16(xf[1], r[c1], acc);
-            acc += __shfl_xor_sync(kFull, acc, 1);
-            acc += __shfl_xor_sync(kFull, acc, 2);
-            return (float)(int32_t)acc;
+            {
+                const uint4 y = r[c1];
+                a1 = __dp4a(xf[1].x, y.x, a1);
+                a1 = __dp4a(xf[1].y, y.y, a1);
+                a1 = __dp4a(xf[1].z, y.z, a1);
+                a1 = __dp4a(xf[1].w, y.w, a1);
+            }
+            uint32_t dot = a0 + a1;
+            dot += __shfl_xor_sync(kFull, dot, 1);
+            dot += __shfl_xor_sync(kFull, dot, 2);
+            return (float)(int32_t)(nx + norms[u] - 2u * dot);
         }
         else
         {
@@ -902,6 +959,33 @@ struct ReplayPairs
         }
     }
 };
+
+// Squared norms of cache rows [0, n) of at most 128 bytes (8 chunks), one
+// row per lane, chunk order rotated by lane so a warp load touches every
+// bank group.
+__device__ __forceinline__ void cache_row_norms(const uint8_t *cache, uint32_t row_bytes, uint32_t nchunks,
+                                                uint32_t n, uint32_t *norms, int lane)
+{
+    for (uint32_t r = lane; r < n; r += 32)
+    {
+        const uint4 *row = reinterpret_cast<const uint4 *>(cache + r * row_bytes);
+        uint32_t a0 = 0, a1 = 0;
+#pragma unroll
+        for (uint32_t c8 = 0; c8 < 8; ++c8)
+        {
+            const uint32_t c = (c8 + (uint32_t)lane) & 7u;
+            if (c < nchunks)
+            {
+                const uint4 y = row[c];
+                a0 = __dp4a(y.x, y.x, a0);
+                a1 = __dp4a(y.y, y.y, a1);
+                a0 = __dp4a(y.z, y.z, a0);
+                a1 = __dp4a(y.w, y.w, a1);
+            }
+        }
+        norms[r] = a0 + a1;
+    }
+}
 
 // Online RobustInsert replay (reference dynamic_robust_insert_C_warp,
 // src/gpu_vamana_vnew2.cu:759-877) of each vertex's recorded expansion
@@ -915,37 +999,64 @@ struct ReplayPairs
 //  - the victim is the first qualifying slot from the far end,
 //  - the worst slot is position 0,
 // and an insertion moves only the positions between its old and new place.
-template <int DT, int CPL>
-__global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
+// Initial order of a replay row: keys of the valid slots sorted, written as
+// the ordered arrays (distance, cache row = slot, slot); returns their
+// number.  NPL = Cp / 32 keys per lane sorted in registers, or NPL = 0: Cp
+// keys sorted in shared memory (okeys).
+template <int NPL>
+__device__ __forceinline__ int replay_initial_order(const ReplayParams &p, uint32_t v, uint64_t lv, uint32_t Cp,
+                                                    uint32_t deg_self, uint32_t *wid, float *wd, float *od,
+                                                    uint16_t *ou, uint16_t *os, uint64_t *okeys, int lane)
 {
-    using Pairs = ReplayPairs<DT, CPL>;
-    extern __shared__ __align__(16) uint8_t smem_raw[];
-    const int lane = lane_id();
-    const uint32_t C = p.C;
-    const uint32_t Cp = C <= 32 ? 32u : (uint32_t)next_pow2((int)C);
-    const ReplayLayout lay(C, p.cache_rows, p.row_bytes, p.exp_stride);
-    uint8_t *base = smem_raw + warp_id_in_block() * p.per_warp;
-    uint8_t *cache = base;
-    uint32_t *gid = reinterpret_cast<uint32_t *>(base + lay.gid);
-    uint32_t *wid = reinterpret_cast<uint32_t *>(base + lay.wid);
-    float *wd = reinterpret_cast<float *>(base + lay.wd);
-    float *od = reinterpret_cast<float *>(base + lay.od);
-    uint16_t *ou = reinterpret_cast<uint16_t *>(base + lay.ou);
-    uint16_t *os = reinterpret_cast<uint16_t *>(base + lay.os);
-    uint32_t *xid = reinterpret_cast<uint32_t *>(base + lay.xid);
-    float *xdd = reinterpret_cast<float *>(base + lay.xdd);
-    uint64_t *okeys = reinterpret_cast<uint64_t *>(base); // initial sort, before the gather
-    const uint32_t N = p.st.N;
-    const uint32_t nch = p.st.nchunks;
-    const float alpha = p.alpha;
-    Pairs pe(lane);
-    unsigned long long pairs = 0;
-
-    for (uint32_t v = p.v0 + blockIdx.x * kWarpsPerBlock + warp_id_in_block(); v < p.v1;
-         v += gridDim.x * kWarpsPerBlock)
+    const uint32_t C = p.C, N = p.st.N;
+    int nv = 0;
+    if constexpr (NPL > 0)
     {
-        const uint64_t lv = v - p.lrow0;
-        const uint32_t deg_self = min(p.degree[v], p.R);
+        uint64_t k[NPL];
+#pragma unroll
+        for (int t = 0; t < NPL; ++t)
+        {
+            const uint32_t i = (uint32_t)(lane * NPL + t);
+            uint32_t nb = kInvalid;
+            float d = FLT_MAX;
+            uint64_t ok = kKeyMax;
+            if (i < deg_self)
+            {
+                nb = p.cur_ids[(uint64_t)v * p.R + i];
+                if (nb < N && nb != v)
+                {
+                    d = p.cur_dists[lv * p.R + i];
+                    ok = order_key(d, i);
+                }
+                else
+                    nb = kInvalid;
+            }
+            if (i < C)
+            {
+                wid[i] = nb;
+                wd[i] = d;
+            }
+            k[t] = ok;
+        }
+        __syncwarp();
+        warp_sort_blocked<NPL>(k, lane);
+#pragma unroll
+        for (int t = 0; t < NPL; ++t)
+        {
+            const uint32_t e = (uint32_t)(lane * NPL + t);
+            const bool valid = k[t] != kKeyMax;
+            if (valid)
+            {
+                const uint32_t slot = (uint32_t)(k[t] & 0xFFFFu);
+                od[e] = wd[slot];
+                ou[e] = (uint16_t)slot;
+                os[e] = (uint16_t)slot;
+            }
+            nv += __popc(__ballot_sync(kFull, valid));
+        }
+    }
+    else
+    {
         for (uint32_t i = lane; i < Cp; i += 32)
         {
             uint32_t nb = kInvalid;
@@ -969,20 +1080,8 @@ __global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
             }
             okeys[i] = ok;
         }
-        const uint32_t cnt = min(p.exp_count[lv], p.exp_stride);
-        for (uint32_t i = lane; i < p.R + cnt; i += 32)
-        {
-            uint32_t id;
-            if (i < p.R)
-                id = i < deg_self ? p.cur_ids[(uint64_t)v * p.R + i] : v;
-            else
-                id = p.exp_ids[lv * p.exp_stride + (i - p.R)];
-            gid[i] = id < N ? id : v;
-        }
         __syncwarp();
         warp_sort_smem_u64(okeys, (int)Cp, lane);
-        // kept slots in order; their initial cache row is the slot itself
-        int nv = 0;
         for (uint32_t b = 0; b < Cp; b += 32)
         {
             const uint64_t k = okeys[b + lane];
@@ -996,16 +1095,89 @@ __global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
                 os[b + lane] = (uint16_t)slot;
             }
         }
+    }
+    return nv;
+}
+
+// Online RobustInsert replay (reference dynamic_robust_insert_C_warp,
+// src/gpu_vamana_vnew2.cu:759-877) of each vertex's recorded expansion
+// sequence into its C-wide work row.  One warp per vertex; the row's
+// vectors (initial neighbours and expanded nodes) are cached in shared
+// memory, and the kept slots are held in order of order_key (distance
+// descending, slot ascending) as parallel arrays (distance, cache row,
+// slot), so
+//  - occlusion is tested from the nearest kept neighbour outwards and stops
+//    at the first occluder,
+//  - the victim is the first qualifying slot from the far end,
+//  - the worst slot is position 0,
+// and an insertion moves only the positions between its old and new place.
+template <int DT, int CPL>
+__global__ void __launch_bounds__(kBlockThreads, CPL <= 2 ? 3 : 1) replay_kernel(ReplayParams p)
+{
+    using Pairs = ReplayPairs<DT, CPL>;
+    extern __shared__ __align__(16) uint8_t smem_raw[];
+    const int lane = lane_id();
+    const uint32_t C = p.C;
+    const uint32_t Cp = C <= 32 ? 32u : (uint32_t)next_pow2((int)C);
+    const ReplayLayout lay(C, p.cache_rows, p.row_bytes, p.exp_stride);
+    uint8_t *base = smem_raw + warp_id_in_block() * p.per_warp;
+    uint8_t *cache = base;
+    uint32_t *norms = reinterpret_cast<uint32_t *>(base + lay.norms);
+    uint32_t *wid = reinterpret_cast<uint32_t *>(base + lay.wid);
+    float *wd = reinterpret_cast<float *>(base + lay.wd);
+    float *od = reinterpret_cast<float *>(base + lay.od);
+    uint16_t *ou = reinterpret_cast<uint16_t *>(base + lay.ou);
+    uint16_t *os = reinterpret_cast<uint16_t *>(base + lay.os);
+    uint32_t *xid = reinterpret_cast<uint32_t *>(base + lay.xid);
+    float *xdd = reinterpret_cast<float *>(base + lay.xdd);
+    uint64_t *okeys = reinterpret_cast<uint64_t *>(base); // initial sort (NPL = 0), before the gather
+    const uint32_t N = p.st.N;
+    const uint32_t nch = p.st.nchunks;
+    const float alpha = p.alpha;
+    Pairs pe(lane);
+    unsigned long long pairs = 0;
+
+    for (uint32_t v = p.v0 + blockIdx.x * kWarpsPerBlock + warp_id_in_block(); v < p.v1;
+         v += gridDim.x * kWarpsPerBlock)
+    {
+        const uint64_t lv = v - p.lrow0;
+        const uint32_t deg_self = min(p.degree[v], p.R);
+        const uint32_t cnt = min(p.exp_count[lv], p.exp_stride);
         for (uint32_t k = lane; k < cnt; k += 32)
         {
             xid[k] = p.exp_ids[lv * p.exp_stride + k];
             xdd[k] = p.exp_dists[lv * p.exp_stride + k];
         }
-        __syncwarp(); // the sort keys are read: the cache may be filled
-        gather_rows_grouped<CPL>(p.st.data, p.st.stride, nch, gid, (int)deg_self, cache, p.row_bytes, lane);
-        gather_rows_grouped<CPL>(p.st.data, p.st.stride, nch, gid + p.R, (int)cnt, cache + p.R * p.row_bytes,
-                                 p.row_bytes, lane);
+        int nv;
+        if (Cp == 32)
+            nv = replay_initial_order<1>(p, v, lv, Cp, deg_self, wid, wd, od, ou, os, okeys, lane);
+        else if (Cp == 64)
+            nv = replay_initial_order<2>(p, v, lv, Cp, deg_self, wid, wd, od, ou, os, okeys, lane);
+        else if (Cp == 128)
+            nv = replay_initial_order<4>(p, v, lv, Cp, deg_self, wid, wd, od, ou, os, okeys, lane);
+        else
+            nv = replay_initial_order<0>(p, v, lv, Cp, deg_self, wid, wd, od, ou, os, okeys, lane);
+        __syncwarp(); // the sort keys are read and xid is complete: the cache may be filled
+        // cache rows: slot i < deg_self (the row's id, v for an invalid one),
+        // then expansion k at row R + k
+        const uint32_t *own = p.cur_ids + (uint64_t)v * p.R;
+        gather_rows_batched<CPL>(p.st.data, p.st.stride, nch, (int)deg_self, cache, p.row_bytes, lane,
+                                 [&](int r) -> uint32_t {
+                                     const uint32_t id = own[r];
+                                     return id < N ? id : v;
+                                 });
+        gather_rows_batched<CPL>(p.st.data, p.st.stride, nch, (int)cnt, cache + p.R * p.row_bytes, p.row_bytes,
+                                 lane, [&](int r) -> uint32_t {
+                                     const uint32_t id = xid[r];
+                                     return id < N ? id : v;
+                                 });
         __syncwarp();
+        if constexpr (Pairs::kQuad)
+        {
+            cache_row_norms(cache, p.row_bytes, nch, deg_self, norms, lane);
+            cache_row_norms(cache + p.R * p.row_bytes, p.row_bytes, nch, cnt, norms + p.R, lane);
+            __syncwarp();
+        }
         uint32_t wdeg = deg_self;
 
         for (uint32_t k = 0; k < cnt; ++k)
@@ -1026,7 +1198,7 @@ __global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
             }
             if (__any_sync(kFull, present))
                 continue;
-            pe.load_x(cache + (p.R + k) * p.row_bytes, nch);
+            pe.load_x(cache + (p.R + k) * p.row_bytes, nch, Pairs::kQuad ? norms[p.R + k] : 0u);
             // occlusion: nearest kept neighbours first
             bool occluded = false;
             for (int b = nv - 1; b >= ngt; b -= Pairs::kPairs)
@@ -1034,7 +1206,7 @@ __global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
                 const int j = b - pe.pidx;
                 const bool act = j >= ngt;
                 const uint32_t u = act ? ou[j] : 0u;
-                const float d = pe.dist(cache + u * p.row_bytes, nch);
+                const float d = pe.dist(cache + u * p.row_bytes, nch, norms, u);
                 if (lane == 0)
                     pairs += (unsigned long long)min(Pairs::kPairs, b - ngt + 1);
                 if (__any_sync(kFull, act && pe.sl == 0 && __fmul_rn(alpha, d) <= dx))
@@ -1053,7 +1225,7 @@ __global__ void __launch_bounds__(kBlockThreads) replay_kernel(ReplayParams p)
                 const bool act = j < ngt;
                 const uint32_t u = act ? ou[j] : 0u;
                 const float dy = act ? od[j] : 0.0f;
-                const float d = pe.dist(cache + u * p.row_bytes, nch);
+                const float d = pe.dist(cache + u * p.row_bytes, nch, norms, u);
                 if (lane == 0)
                     pairs += (unsigned long long)min(Pairs::kPairs, ngt - b);
                 const unsigned hit = __ballot_sync(kFull, act && pe.sl == 0 && __fmul_rn(alpha, d) <= dy);
