@@ -344,28 +344,12 @@ __device__ __forceinline__ void eval_cached(const uint8_t *cache, uint32_t row_b
     }
 }
 
-// Cooperative copy of `count` rows (ids[k] -> cache slot k) into shared memory.
-__device__ __forceinline__ void gather_rows_to_smem(const uint8_t *__restrict__ data, uint64_t stride,
-                                                    uint32_t nchunks, const uint32_t *ids, int count, uint8_t *cache,
-                                                    uint32_t row_bytes, int lane)
-{
-    const int total = count * (int)nchunks;
-    for (int i = lane; i < total; i += 32)
-    {
-        const int r = i / (int)nchunks;
-        const int c = i - r * (int)nchunks;
-        const uint4 v = ldg_chunk(reinterpret_cast<const uint4 *>(data + (uint64_t)ids[r] * stride) + c);
-        reinterpret_cast<uint4 *>(cache + (uint32_t)r * row_bytes)[c] = v;
-    }
-}
-
 // ------------------------------------------------------------------ warp sorts
-// Ascending bitonic sort of 64 keys held two per lane (element 2*lane+s).
 // Ascending bitonic sort of 32*NPL keys held NPL per lane in blocked order
 // (element lane*NPL + s in k[s]): in-lane exchanges for distances below NPL,
 // xor shuffles above.
-template <int NPL>
-__device__ __forceinline__ void warp_sort_blocked(uint64_t (&k)[NPL], int lane)
+template <int NPL, class K>
+__device__ __forceinline__ void warp_sort_blocked(K (&k)[NPL], int lane)
 {
     constexpr int n = 32 * NPL;
 #pragma unroll
@@ -383,7 +367,7 @@ __device__ __forceinline__ void warp_sort_blocked(uint64_t (&k)[NPL], int lane)
                     if (t > s)
                     {
                         const bool asc = ((lane * NPL + s) & size) == 0;
-                        const uint64_t a = k[s], b = k[t];
+                        const K a = k[s], b = k[t];
                         const bool sw = asc ? (a > b) : (a < b);
                         k[s] = sw ? b : a;
                         k[t] = sw ? a : b;
@@ -398,7 +382,7 @@ __device__ __forceinline__ void warp_sort_blocked(uint64_t (&k)[NPL], int lane)
                 for (int s = 0; s < NPL; ++s)
                 {
                     const bool asc = ((lane * NPL + s) & size) == 0;
-                    const uint64_t o = __shfl_xor_sync(kFull, k[s], lm);
+                    const K o = __shfl_xor_sync(kFull, k[s], lm);
                     const bool take_min = lower == asc;
                     k[s] = take_min ? (k[s] < o ? k[s] : o) : (k[s] > o ? k[s] : o);
                 }
@@ -407,6 +391,7 @@ __device__ __forceinline__ void warp_sort_blocked(uint64_t (&k)[NPL], int lane)
     }
 }
 
+// Ascending bitonic sort of 64 keys held two per lane (element 2*lane+s).
 __device__ __forceinline__ void warp_sort64(uint64_t &k0, uint64_t &k1, int lane)
 {
 #pragma unroll
@@ -490,6 +475,39 @@ __device__ __forceinline__ void warp_sort_smem_u64(uint64_t *a, int n, int lane)
             __syncwarp();
         }
     }
+}
+
+// Ascending sort of a[0..n) (n a power of two, 32..4096; a 16-byte
+// aligned) by one warp: in registers for n <= 128, else in shared memory.
+__device__ __forceinline__ void warp_sort_u32(uint32_t *a, int n, int lane)
+{
+    if (n > 128)
+    {
+        warp_sort_smem_u32(a, n, lane);
+        return;
+    }
+    __syncwarp();
+    if (n == 32)
+    {
+        uint32_t k[1] = {a[lane]};
+        warp_sort_blocked<1>(k, lane);
+        a[lane] = k[0];
+    }
+    else if (n == 64)
+    {
+        const uint2 x = reinterpret_cast<const uint2 *>(a)[lane];
+        uint32_t k[2] = {x.x, x.y};
+        warp_sort_blocked<2>(k, lane);
+        reinterpret_cast<uint2 *>(a)[lane] = make_uint2(k[0], k[1]);
+    }
+    else
+    {
+        const uint4 x = reinterpret_cast<const uint4 *>(a)[lane];
+        uint32_t k[4] = {x.x, x.y, x.z, x.w};
+        warp_sort_blocked<4>(k, lane);
+        reinterpret_cast<uint4 *>(a)[lane] = make_uint4(k[0], k[1], k[2], k[3]);
+    }
+    __syncwarp();
 }
 
 // Number of elements of sorted a[0..n) strictly less than key.

@@ -354,7 +354,8 @@ __global__ void __launch_bounds__(kBlockThreads, 4) prune_gram_kernel(PruneParam
             m += __popc(bm);
         }
         __syncwarp();
-        gather_rows_grouped<CPL>(p.st.data, p.st.stride, p.st.nchunks, cid, (int)m, cache, Sg, lane);
+        gather_rows_batched<CPL>(p.st.data, p.st.stride, p.st.nchunks, (int)m, cache, Sg, lane,
+                                 [&](int r) -> uint32_t { return cid[r]; });
         gram_zero_pad(cache, Sg, p.row_bytes, m, lane);
         __syncwarp();
         gram_norms(cache, Sg, kbytes, m, norms, lane);

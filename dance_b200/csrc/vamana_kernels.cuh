@@ -806,27 +806,6 @@ __device__ __forceinline__ void warp_argmax_lowslot(float &v, int &s)
     s = __shfl_sync(kFull, s, 0);
 }
 
-// Copies `count` rows (ids[k] -> slot k of cache) with 8-lane groups.
-template <int CPL>
-__device__ __forceinline__ void gather_rows_grouped(const uint8_t *__restrict__ data, uint64_t stride,
-                                                    uint32_t nchunks, const uint32_t *ids, int count, uint8_t *cache,
-                                                    uint32_t row_bytes, int lane)
-{
-    const int g = lane >> 3, gl = lane & 7;
-    for (int r = g; r < count; r += 4)
-    {
-        const uint4 *src = reinterpret_cast<const uint4 *>(data + (uint64_t)ids[r] * stride);
-        uint4 *dst = reinterpret_cast<uint4 *>(cache + (uint32_t)r * row_bytes);
-#pragma unroll
-        for (int t = 0; t < CPL; ++t)
-        {
-            const uint32_t c = (uint32_t)(gl + 8 * t);
-            if (c < nchunks)
-                dst[c] = ldg_chunk(src + c);
-        }
-    }
-}
-
 // Copies `count` rows (row k from vector id idf(k)) into the cache (row k,
 // row_bytes apart) with 8-lane groups, loading Unroll<CPL> rows per group
 // before storing any, so that the loads overlap.
@@ -1675,7 +1654,7 @@ __device__ __forceinline__ uint32_t merge_load_row(const MergeParams &p, uint32_
         rsorted[i] = i < deg0 ? p.work_ids[lt * C + i] : kInvalid;
     }
     __syncwarp();
-    warp_sort_smem_u32(rsorted, (int)Cp, lane);
+    warp_sort_u32(rsorted, (int)Cp, lane);
     return deg0;
 }
 
@@ -1861,7 +1840,7 @@ __global__ void __launch_bounds__(kBlockThreads) merge_kernel(MergeParams p)
         for (int i = lane; i < n2; i += 32)
             buf[i] = (uint32_t)i < n ? p.rev[beg + i] : kInvalid;
         __syncwarp();
-        warp_sort_smem_u32(buf, n2, lane);
+        warp_sort_u32(buf, n2, lane);
         merge_target_warp<DT, CPL>(p, t, buf, n, wid, wd, rsorted, nl, nd, lane, evals);
     }
     if (lane == 0 && p.counters)
@@ -2150,7 +2129,8 @@ __global__ void __launch_bounds__(kBlockThreads) prune_kernel(PruneParams p)
             m += __popc(bm);
         }
         __syncwarp();
-        gather_rows_to_smem(p.st.data, p.st.stride, p.st.nchunks, cid, m, cache, p.row_bytes, lane);
+        gather_rows_batched<CPL>(p.st.data, p.st.stride, p.st.nchunks, m, cache, p.row_bytes, lane,
+                                 [&](int r) -> uint32_t { return cid[r]; });
         __syncwarp();
         uint32_t out = 0;
         for (int j = 0; j < m; ++j)
