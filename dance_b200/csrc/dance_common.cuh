@@ -250,6 +250,9 @@ __device__ __forceinline__ void eval_candidates(const uint8_t *__restrict__ data
 #pragma unroll
             for (int u = 0; u < 8; ++u)
             {
+                part[u] = 0u;
+                if (base + 4 * u >= m) // no candidate of this pass row (warp-uniform)
+                    continue;
                 uint32_t cc = qq, qc = 0;
 #pragma unroll
                 for (int t = 0; t < CPL; ++t)
@@ -510,19 +513,16 @@ __device__ __forceinline__ void warp_sort_u32(uint32_t *a, int n, int lane)
     __syncwarp();
 }
 
-// Number of elements of sorted a[0..n) strictly less than key.
+// Number of elements of sorted a[0..n) strictly less than key (n <= 256).
 __device__ __forceinline__ int lower_bound_u64(const uint64_t *a, int n, uint64_t key)
 {
-    int lo = 0, hi = n;
-    while (lo < hi)
-    {
-        const int mid = (lo + hi) >> 1;
-        if (a[mid] < key)
-            lo = mid + 1;
-        else
-            hi = mid;
-    }
-    return lo;
+    // fixed steps of a power-of-two search (n <= 256): no data-dependent branches
+    int pos = 0;
+#pragma unroll
+    for (int step = 256; step > 0; step >>= 1)
+        if (pos + step <= n && a[pos + step - 1] < key)
+            pos += step;
+    return pos;
 }
 
 __host__ __device__ __forceinline__ int next_pow2(int n)

@@ -253,13 +253,8 @@ __device__ __forceinline__ int pool_insert_batch(const SearchSmem &sm, PoolState
             sm.bkey[__popc(s0) + __popc(s1 & lt)] = k1;
         __syncwarp();
         const uint64_t key = lane < k ? sm.bkey[lane] : kKeyMax;
-        bool dup = false;
-#pragma unroll 4
-        for (int i = 0; i < k; ++i)
-        {
-            const uint64_t o = sm.bkey[i];
-            dup |= (i < lane) && (o == key);
-        }
+        // a copy of the key in an earlier lane (only survivors hold finite keys)
+        const bool dup = (__match_any_sync(kFull, key) & lt) != 0u;
         bool keep = lane < k && !dup;
         uint32_t ins = 0;
         if (keep)
