@@ -1,4 +1,5 @@
-"""Multi-GPU build: one graph sharded over 2 GPUs equals the one-GPU build."""
+"""Multi-GPU builds: one graph sharded over 2 GPUs, and the stitched label
+graphs spread over 2 GPUs, each equal the one-GPU build."""
 import os
 import socket
 import subprocess
@@ -24,6 +25,19 @@ def test_sharded_build_matches_single_gpu(dance_lib):
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
            "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(_port()),
            os.path.join(HERE, "sharded_check.py"), "20000"]
+    res = subprocess.run(cmd, capture_output=True, text=True, env=env)
+    assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
+    assert "identical=True" in res.stdout
+
+
+def test_stitched_sharded_build_matches_single_gpu(dance_lib):
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(_port()),
+           os.path.join(HERE, "stitched_sharded_check.py"), "30000"]
     res = subprocess.run(cmd, capture_output=True, text=True, env=env)
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
     assert "identical=True" in res.stdout
