@@ -1161,18 +1161,34 @@ __global__ void __launch_bounds__(kBlockThreads, CPL <= 2 ? 3 : 1) replay_kernel
             if (x >= N || x == v)
                 continue;
             const uint32_t deg = min(wdeg, C);
+            // x's row is read while the row is scanned (unused if x is present)
+            pe.load_x(cache + (p.R + k) * p.row_bytes, nch, Pairs::kQuad ? norms[p.R + k] : 0u);
             // already in the row?  and ngt: positions [0, ngt) have d(v,y) > d(v,x)
             bool present = false;
             int ngt = 0;
-            for (uint32_t b = 0; b < deg; b += 32)
+            if (C <= 128)
             {
-                const uint32_t i = b + lane;
-                present |= i < deg && wid[i] == x;
-                ngt += __popc(__ballot_sync(kFull, (int)i < nv && od[i] > dx));
+#pragma unroll
+                for (uint32_t r = 0; r < 4; ++r)
+                {
+                    const uint32_t i = 32u * r + lane;
+                    const uint32_t w = i < deg ? wid[i] : kInvalid;
+                    const float o = (int)i < nv ? od[i] : 0.0f;
+                    present |= i < deg && w == x;
+                    ngt += __popc(__ballot_sync(kFull, (int)i < nv && o > dx));
+                }
+            }
+            else
+            {
+                for (uint32_t b = 0; b < deg; b += 32)
+                {
+                    const uint32_t i = b + lane;
+                    present |= i < deg && wid[i] == x;
+                    ngt += __popc(__ballot_sync(kFull, (int)i < nv && od[i] > dx));
+                }
             }
             if (__any_sync(kFull, present))
                 continue;
-            pe.load_x(cache + (p.R + k) * p.row_bytes, nch, Pairs::kQuad ? norms[p.R + k] : 0u);
             // occlusion: nearest kept neighbours first
             bool occluded = false;
             for (int b = nv - 1; b >= ngt; b -= Pairs::kPairs)
@@ -1230,10 +1246,24 @@ __global__ void __launch_bounds__(kBlockThreads, CPL <= 2 ? 3 : 1) replay_kernel
             // new position of the slot among the others
             const uint64_t kn = order_key(dx, (uint32_t)slot);
             int pn = 0;
-            for (int b = 0; b < nv; b += 32)
+            if (C <= 128)
             {
-                const int j = b + lane;
-                pn += __popc(__ballot_sync(kFull, j < nv && j != pr && order_key(od[j], os[j]) < kn));
+#pragma unroll
+                for (int r = 0; r < 4; ++r)
+                {
+                    const int j = 32 * r + lane;
+                    const bool in = j < nv && j != pr;
+                    const uint64_t kj = in ? order_key(od[j], os[j]) : kKeyMax;
+                    pn += __popc(__ballot_sync(kFull, in && kj < kn));
+                }
+            }
+            else
+            {
+                for (int b = 0; b < nv; b += 32)
+                {
+                    const int j = b + lane;
+                    pn += __popc(__ballot_sync(kFull, j < nv && j != pr && order_key(od[j], os[j]) < kn));
+                }
             }
             if (pr >= 0)
             {
