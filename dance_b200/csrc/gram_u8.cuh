@@ -354,10 +354,10 @@ __global__ void __launch_bounds__(kBlockThreads, 4) prune_gram_kernel(PruneParam
             m += __popc(bm);
         }
         __syncwarp();
-        gather_rows_batched<CPL>(p.st.data, p.st.stride, p.st.nchunks, (int)m, cache, Sg, lane,
-                                 [&](int r) -> uint32_t { return cid[r]; });
+        gather_rows_async<CPL>(p.st.data, p.st.stride, p.st.nchunks, (int)m, cache, Sg, lane,
+                               [&](int r) -> uint32_t { return cid[r]; });
         gram_zero_pad(cache, Sg, p.row_bytes, m, lane);
-        __syncwarp();
+        gather_rows_async_wait();
         gram_norms(cache, Sg, kbytes, m, norms, lane);
         __syncwarp();
         gram_prune_masks<CPL == 1>(cache, Sg, kbytes, norms, cd, m, lay.W, occ, alpha, lane);

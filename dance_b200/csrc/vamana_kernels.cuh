@@ -849,6 +849,36 @@ __device__ __forceinline__ void gather_rows_batched(const uint8_t *__restrict__ 
     }
 }
 
+// Same copy through cp.async (global -> shared without registers): every
+// row's chunks are in flight at once.  The caller waits with
+// gather_rows_async_wait() before reading the rows.
+template <int CPL, class IdFn>
+__device__ __forceinline__ void gather_rows_async(const uint8_t *__restrict__ data, uint64_t stride, uint32_t nchunks,
+                                                  int count, uint8_t *cache, uint32_t row_bytes, int lane, IdFn idf)
+{
+    const int g = lane >> 3, gl = lane & 7;
+    for (int r = g; r < count; r += 4)
+    {
+        const uint8_t *src = data + (uint64_t)idf(r) * stride;
+        const uint32_t dst = (uint32_t)__cvta_generic_to_shared(cache + (uint32_t)r * row_bytes);
+#pragma unroll
+        for (int t = 0; t < CPL; ++t)
+        {
+            const uint32_t c = (uint32_t)(gl + 8 * t);
+            if (c < nchunks)
+                asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst + 16u * c), "l"(src + 16u * c)
+                             : "memory");
+        }
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void gather_rows_async_wait()
+{
+    asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    __syncwarp();
+}
+
 // Order key of a work-row slot: descending distance, then ascending slot --
 // the reference's preference for the victim and the worst entry
 // (src/gpu_vamana_vnew2.cu:816-846, strict '>' scans in slot order).
@@ -1135,17 +1165,17 @@ __global__ void __launch_bounds__(kBlockThreads, CPL <= 2 ? 3 : 1) replay_kernel
         // cache rows: slot i < deg_self (the row's id, v for an invalid one),
         // then expansion k at row R + k
         const uint32_t *own = p.cur_ids + (uint64_t)v * p.R;
-        gather_rows_batched<CPL>(p.st.data, p.st.stride, nch, (int)deg_self, cache, p.row_bytes, lane,
-                                 [&](int r) -> uint32_t {
-                                     const uint32_t id = own[r];
-                                     return id < N ? id : v;
-                                 });
-        gather_rows_batched<CPL>(p.st.data, p.st.stride, nch, (int)cnt, cache + p.R * p.row_bytes, p.row_bytes,
-                                 lane, [&](int r) -> uint32_t {
-                                     const uint32_t id = xid[r];
-                                     return id < N ? id : v;
-                                 });
-        __syncwarp();
+        gather_rows_async<CPL>(p.st.data, p.st.stride, nch, (int)deg_self, cache, p.row_bytes, lane,
+                               [&](int r) -> uint32_t {
+                                   const uint32_t id = own[r];
+                                   return id < N ? id : v;
+                               });
+        gather_rows_async<CPL>(p.st.data, p.st.stride, nch, (int)cnt, cache + p.R * p.row_bytes, p.row_bytes, lane,
+                               [&](int r) -> uint32_t {
+                                   const uint32_t id = xid[r];
+                                   return id < N ? id : v;
+                               });
+        gather_rows_async_wait();
         if constexpr (Pairs::kQuad)
         {
             cache_row_norms(cache, p.row_bytes, nch, deg_self, norms, lane);
