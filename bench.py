@@ -129,14 +129,17 @@ def measured_peaks():
     return 6650.0, "fallback"
 
 
-def traffic_per_launch(kernel: str, workload: str):
-    """DRAM bytes (read+write) per launch of `kernel` from the committed ncu summary, or None."""
-    p = ROOT / "profiles" / "traffic.json"
+def traffic_per_launch(kernel: str, workload: str, n: int):
+    """DRAM bytes (read+write) per launch of `kernel` at the full workload, from
+    the committed ncu summary profiles/<kernel>_traffic_<workload>.md, or None."""
+    import re
+    if n != WORKLOAD["N"]:
+        return None
+    p = ROOT / "profiles" / f"{kernel}_traffic_{workload}.md"
     if not p.exists():
         return None
-    d = json.loads(p.read_text())
-    e = d.get(kernel, {}).get(workload)
-    return e.get("bytes_per_launch") if e else None
+    m = re.search(r"traffic_bytes_per_launch:\s*(\d+)", p.read_text())
+    return int(m.group(1)) if m else None
 
 
 def make_workload(device, n, seed=WORKLOAD["seed"]):
@@ -277,7 +280,7 @@ def run_ours(args):
     stage = {k: statistics.mean(r[k] for r in reports) for k in reports[0] if k.endswith("_seconds")}
     counters = {k: reports[-1][k] for k in ("search_evals", "expansions", "replay_pairs", "reverse_evals",
                                             "prune_pairs")}
-    traffic = traffic_per_launch("search_kernel", WORKLOAD["name"])
+    traffic = traffic_per_launch("search_kernel", WORKLOAD["name"], n)
 
     line = {
         "metric": "vamana_build_vectors_per_s", "value": value, "unit": "vectors/s", "n_gpus": 1,
