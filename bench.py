@@ -54,8 +54,10 @@ def parse():
     ap.add_argument("--no-recall", action="store_true")
     ap.add_argument("--ref-gpu", action="store_true",
                     help="also time the reference's own GPU builder (oracle/_ref, sm_100a) once on the workload")
-    ap.add_argument("--workload", choices=["cfg1_u8_10M", "cfg2_filtered", "cfg3_stitched"], default="cfg1_u8_10M",
-                    help="cfg1_u8_10M: the headline standard build; cfg2_filtered: the GPU-FilteredVamana build of "
+    ap.add_argument("--workload", choices=["cfg1_u8_10M", "cfg0_f32", "cfg2_filtered", "cfg3_stitched"],
+                    default="cfg1_u8_10M",
+                    help="cfg1_u8_10M: the headline standard build; cfg0_f32: configs[0], 1M float vectors "
+                         "stored in fp16 (FAST_SMALL); cfg2_filtered: the GPU-FilteredVamana build of "
                          "BASELINE.json configs[2]; cfg3_stitched: the per-label stitched build of configs[3]")
     return ap.parse_args()
 
@@ -513,6 +515,217 @@ def run_sharded(args):
 
 
 # ------------------------------------------------------------------ stitched
+CFG0 = dict(name="cfg0_f32_1M_fp16", N=1_000_000, dim=96, centroids=1000, sigma=0.3, R=64, L=100, C=80, STEPS=64,
+            alpha=1.2, iters=4, seed=42, queries=10_000)
+CFG0_CPU_SAMPLE = 8_000  # vectors built by the oracle (fp16 arithmetic done in software)
+# The reference's only published build number: DEEP1M (1M x 96 f32, FAST_SMALL,
+# fp16 storage, same R/L/C/STEPS) on one RTX 4090 -- another dataset and GPU.
+CFG0_PUBLISHED = {"seconds": 2.768, "vectors_per_s": 1e6 / 2.768,
+                  "source": "DANCE REPRODUCIBILITY.md:21-42, DEEP1M on RTX 4090 (FAST_SMALL)"}
+
+
+def cfg0_inputs(n):
+    from dance_b200 import workloads
+    C0 = CFG0
+    x = workloads.gaussian_mixture_f32(n, C0["dim"], C0["centroids"], C0["sigma"], seed=C0["seed"], device="cuda")
+    q = workloads.gaussian_mixture_f32(C0["queries"], C0["dim"], C0["centroids"], C0["sigma"], seed=C0["seed"],
+                                       device="cuda", stream_offset=1)
+    return x, q
+
+
+def cfg0_config(n):
+    C0 = CFG0
+    return {"workload": C0["name"], "N": n, "dim": C0["dim"], "R": C0["R"], "L": C0["L"], "C": C0["C"],
+            "STEPS": C0["STEPS"], "alpha": C0["alpha"], "iters": C0["iters"], "seed": C0["seed"],
+            "storage": "fp16 (the reference's FAST_SMALL profile: ENABLE_FLOAT16_BUILD=1)",
+            "l2": "inputs larger than L2 (192 MB fp16 vector store + graph rows), no flush"}
+
+
+def run_cfg0(args):
+    """1M x 96 normalised Gaussian mixture, float input
+    stored and searched in fp16 like the reference's FAST_SMALL profile."""
+    import torch
+    import dance_b200
+    from dance_b200 import vamana, workloads
+    rank, world, local = dist_env()
+    if rank != 0:
+        return 0
+    torch.cuda.set_device(local)
+    lib = dance_b200.load()
+    C0 = CFG0
+    n = args.n if args.n != WORKLOAD["N"] else C0["N"]
+    R, L, C, S = C0["R"], C0["L"], C0["C"], C0["STEPS"]
+    x, q = cfg0_inputs(n)
+    store, stride = vamana.padded_store(x.half())
+    ws = vamana.Workspace.create(n, R, L, C, S)
+    prm = dance_b200.default_params()
+    graph = torch.empty((n, R), dtype=torch.int32, device="cuda")
+    degree = torch.empty((n,), dtype=torch.int32, device="cuda")
+    dists = torch.empty((n, R), dtype=torch.float32, device="cuda")
+    stream = torch.cuda.Stream()
+    torch.cuda.synchronize()
+
+    def one_build():
+        with torch.cuda.stream(stream):
+            return vamana.build_resident(store, C0["dim"], stride, R, L, C, S, params=prm, workspace=ws,
+                                         graph=graph, degree=degree, dists=dists, stream=stream)
+
+    for _ in range(args.warmup):
+        one_build()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(torch.cuda.current_device())
+    clocks.start()
+    launches0 = lib.dance_kernel_launch_count()
+    reports = []
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    medoid = 0
+    for _ in range(args.steps):
+        _, _, _, medoid = one_build()
+        reports.append(dance_b200.last_build_report())
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    launches = lib.dance_kernel_launch_count() - launches0
+    clk = clocks.stop()
+    elapsed = ev0.elapsed_time(ev1) * 1e-3
+    peak, peak_kind = measured_peaks()
+    alg = sum(search_algorithmic_bytes(r, n, stride, R, C0["iters"]) for r in reports)
+    ksec = sum(r["search_kernel_seconds"] for r in reports)
+    achieved = alg / ksec / 1e9
+    line = {
+        "metric": "vamana_build_vectors_per_s", "value": n * args.steps / elapsed, "unit": "vectors/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded GPU generator, BASELINE.json configs[0] recipe)",
+        "config": cfg0_config(n),
+        "roofline": {"kernel": "search_kernel", "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_source": peak_kind, "traffic": None,
+                     "algorithmic_bytes_per_launch": alg / (len(reports) * C0["iters"]),
+                     "avg_launch_ms": ksec / (len(reports) * C0["iters"]) * 1e3},
+        "gpu_launches": int(launches),
+        "clocks": clk,
+        "stage_seconds": {k: statistics.mean(r[k] for r in reports) for k in reports[0] if k.endswith("_seconds")},
+        "counters_per_build": {k: reports[-1][k] for k in ("search_evals", "expansions", "replay_pairs",
+                                                           "reverse_evals", "prune_pairs")},
+        "published_reference": CFG0_PUBLISHED,
+    }
+    if not args.no_e2e:
+        # the reference's float entry point; fp16 storage selected at run time
+        os.environ["DANCE_FLOAT16_BUILD"] = "1"
+        hx = x.cpu().pin_memory()
+        hg = torch.empty((n, R), dtype=torch.int32).pin_memory()
+        hd = torch.empty((n,), dtype=torch.int32).pin_memory()
+        fn = lib.gpu_vamana_vnew2_build_float
+
+        def e2e_call():
+            rc = fn(ctypes.c_void_p(hx.data_ptr()), n, C0["dim"], R, L, C, S, ctypes.c_void_p(hg.data_ptr()),
+                    ctypes.c_void_p(hd.data_ptr()))
+            dance_b200.check(rc, "gpu_vamana_vnew2_build_float")
+
+        e2e_call()
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        for _ in range(args.steps):
+            e2e_call()
+        torch.cuda.synchronize()
+        e2e_dt = time.perf_counter() - t0
+        line["e2e"] = {"value": n * args.steps / e2e_dt, "unit": "vectors/s", "h2d_bytes_per_step": int(hx.numel() * 4),
+                       "d2h_bytes_per_step": int(hg.numel() * 4 + hd.numel() * 4),
+                       "api": "gpu_vamana_vnew2_build_float (reference C ABI, DANCE_FLOAT16_BUILD=1), pinned host "
+                              "buffers, wall clock", "warmup": 1,
+                       "matches_resident_build": bool(torch.equal(hg.cuda(), graph))}
+    if not args.no_recall:
+        gt, _ = workloads.brute_force_knn(x, q, 10)
+        ids, _ = vamana.search_queries(store, C0["dim"], stride, graph, R, medoid, q.half(), 100, 10)
+        line["recall_at_10"] = {"L_search": 100, "queries": int(q.shape[0]),
+                                "ours": vamana.recall_at_k(ids.cpu().numpy(), gt.cpu().numpy()),
+                                "ground_truth": "brute force on the float32 vectors"}
+    if not args.no_cpu_baseline:
+        sample = x[:min(CFG0_CPU_SAMPLE, n)].half().cpu().numpy()
+        threads = os.cpu_count() or 1
+        rate, secs = oracle_sample_rate(sample, threads)
+        line["cpu_baseline"] = {"value": rate, "unit": "vectors/s", "cores": threads, "kind": "port",
+                                "sample": f"first {len(sample)} vectors of the workload (fp16), full 4-round "
+                                          f"build ({secs:.1f} s)"}
+    if args.ref_gpu:
+        line["reference_gpu"] = reference_gpu_cfg0(x, q, store, stride)
+    print(json.dumps(line), flush=True)
+    ws.close()
+    return 0
+
+
+def reference_gpu_cfg0(x, q, store, stride):
+    """The reference's vnew2 builder in its FAST_SMALL profile (fp16 storage),
+    compiled for sm_100a, on the same float vectors through its C ABI."""
+    import numpy as np
+    import torch
+    from dance_b200 import vamana, workloads
+    lib_path = ROOT / "oracle" / "_ref" / "libref_vnew2_fast_small.so"
+    if not lib_path.exists():
+        return {"unavailable": f"{lib_path.name} not built"}
+    lib = ctypes.CDLL(str(lib_path))
+    f = lib.gpu_vamana_vnew2_build_float
+    f.restype = ctypes.c_int
+    f.argtypes = [ctypes.c_void_p] + [ctypes.c_uint32] * 6 + [ctypes.c_void_p] * 2
+    lib.gpu_vamana_vnew2_get_last_medoid.restype = ctypes.c_uint32
+    C0 = CFG0
+    n = x.shape[0]
+    R, L, C, S = C0["R"], C0["L"], C0["C"], C0["STEPS"]
+    hx = np.ascontiguousarray(x.cpu().numpy())
+    g = np.zeros((n, R), np.uint32)
+    d = np.zeros(n, np.uint32)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    rc = f(ctypes.c_void_p(hx.ctypes.data), n, C0["dim"], R, L, C, S, ctypes.c_void_p(g.ctypes.data),
+           ctypes.c_void_p(d.ctypes.data))
+    dt = time.perf_counter() - t0
+    if rc != 0:
+        return {"unavailable": f"reference build returned {rc}"}
+    med = int(lib.gpu_vamana_vnew2_get_last_medoid())
+    gt, _ = workloads.brute_force_knn(x, q, 10)
+    gd = torch.from_numpy(g.view(np.int32)).cuda()
+    ids, _ = vamana.search_queries(store, C0["dim"], stride, gd, R, med, q.half(), 100, 10)
+    return {"e2e_vectors_per_s": n / dt, "seconds": dt,
+            "recall_at_10": vamana.recall_at_k(ids.cpu().numpy(), gt.cpu().numpy()), "medoid": med,
+            "avg_degree": float(d.mean()),
+            "build": "DANCE vnew2 FAST_SMALL profile (fp16 storage, VAMANA_ITERS=4), nvcc 12.9 sm_100a"}
+
+
+def run_cfg0_reference(args):
+    rank, world, local = dist_env()
+    if rank != 0:
+        return 0
+    import torch
+    import oracle
+    oracle.build()
+    C0 = CFG0
+    from dance_b200 import workloads
+    dev = "cuda" if torch.cuda.is_available() else "cpu"
+    sample = workloads.gaussian_mixture_f32(CFG0_CPU_SAMPLE, C0["dim"], C0["centroids"], C0["sigma"],
+                                            seed=C0["seed"], device=dev).half().cpu().numpy()
+    threads = os.cpu_count() or 1
+    for _ in range(args.warmup):
+        oracle.build_graph(sample, C0["R"], C0["L"], C0["C"], C0["STEPS"], nthreads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.build_graph(sample, C0["R"], C0["L"], C0["C"], C0["STEPS"], nthreads=threads)
+    dt = time.perf_counter() - t0
+    value = CFG0_CPU_SAMPLE * args.steps / dt
+    desc = (f"first {CFG0_CPU_SAMPLE} vectors of the {C0['name']} workload (fp16), full 4-round build per step, "
+            f"{threads} OpenMP threads")
+    line = {
+        "impl": "reference", "metric": "vamana_build_vectors_per_s", "value": value, "unit": "vectors/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt / args.steps * 1e3,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": cfg0_config(CFG0_CPU_SAMPLE),
+        "cpu_baseline": {"value": value, "unit": "vectors/s", "cores": threads, "kind": "port", "sample": desc},
+        "e2e": {"value": value, "unit": "vectors/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 STITCHED = dict(name="cfg3_stitched_f32_1M", N=1_000_000, dim=96, centroids=1000, sigma=0.3, labels=100,
                 r_small=32, l_small=100, r_stitched=64, C=96, steps=64, alpha=1.2, seed=42, queries=10_000)
 STITCHED_CPU_SAMPLE = 20_000  # label memberships built by the oracle for cpu_baseline
@@ -1092,6 +1305,10 @@ def run_filtered_reference(args):
 
 def main():
     args = parse()
+    if args.workload == "cfg0_f32":
+        if args.impl == "reference":
+            return run_cfg0_reference(args)
+        return run_cfg0(args)
     if args.workload == "cfg2_filtered":
         if args.impl == "reference":
             return run_filtered_reference(args)

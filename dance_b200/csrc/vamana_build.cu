@@ -236,7 +236,7 @@ void dance_vamana_default_params(DanceVamanaParams *p)
     p->reverse_heavy_cap = ENABLE_REVERSE_HEAVY_CAP;
     p->reverse_heavy_threshold = REVERSE_HEAVY_THRESHOLD;
     p->reverse_heavy_sample = REVERSE_HEAVY_SAMPLE;
-    p->visited_log2 = 10;
+    p->visited_log2 = DANCE_VISITED_LOG2;
 }
 
 const char *dance_last_error(void) { return dance::g_err; }

@@ -30,6 +30,11 @@ constexpr int kMaxL = 256; // search pool capacity limit (8 entries per lane)
 #ifndef DANCE_SEARCH_MIN_BLOCKS
 #define DANCE_SEARCH_MIN_BLOCKS 8
 #endif
+// Default log2 size of the build search's per-warp visited table (shared
+// memory; a lost entry only costs a repeated distance evaluation).
+#ifndef DANCE_VISITED_LOG2
+#define DANCE_VISITED_LOG2 10
+#endif
 constexpr int kBlockThreads = kWarpsPerBlock * 32;
 
 struct StoreView

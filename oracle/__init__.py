@@ -27,6 +27,7 @@ _SIGS = {
     "oracle_get_counters": (None, [_P]),
     "oracle_distance": (_F, [_I, _P, _P, _U32]),
     "oracle_float_to_half": (None, [_P, _P, _U64]),
+    "oracle_half_selftest": (_U64, [_U64]),
     "oracle_hash_u32": (_U32, [_U32]),
     "oracle_hash_edge32": (_U32, [_U32, _U32, _U64]),
     "oracle_merge_edges": (_I, [_P, _P, _U64, _U32, _U32, _U64, _P, _P]),

@@ -158,15 +158,84 @@ float dist_f32(const float *x, const float *y, uint32_t dim)
     return tree32(acc);
 }
 
+// The same rounding from the bits of the double (round to nearest even on
+// the 42 or more dropped significand bits); checked against double_to_half
+// by oracle_half_selftest.
+uint16_t double_to_half_bits(double x)
+{
+    uint64_t b;
+    std::memcpy(&b, &x, sizeof(b));
+    const uint16_t sign = (uint16_t)((b >> 48) & 0x8000u);
+    const uint64_t a = b & 0x7FFFFFFFFFFFFFFFull;
+    if (a > 0x7FF0000000000000ull)
+        return 0x7E00u;
+    const int exp = (int)(a >> 52);
+    if (exp == 0)
+        return sign; // zero or a double subnormal: far below half's unit 2^-24
+    const int e = exp - 1023;
+    if (e >= 16)
+        return sign | 0x7C00u;
+    const uint64_t m = (a & 0xFFFFFFFFFFFFFull) | (1ull << 52); // 53-bit significand
+    if (e >= -14)
+    {
+        uint64_t q = m >> 42;
+        const uint64_t rem = m & ((1ull << 42) - 1), halfway = 1ull << 41;
+        if (rem > halfway || (rem == halfway && (q & 1u)))
+            ++q;
+        int eh = e;
+        if (q == (1ull << 11))
+        {
+            q >>= 1;
+            ++eh;
+        }
+        if (eh > 15)
+            return sign | 0x7C00u;
+        return sign | (uint16_t)((eh + 15) << 10) | (uint16_t)(q & 0x3FFu);
+    }
+    const int shift = 28 - e; // value in units of 2^-24 is m >> shift
+    if (shift > 53)
+        return sign; // below half the smallest subnormal
+    uint64_t q = m >> shift;
+    const uint64_t rem = m & ((1ull << shift) - 1), halfway = 1ull << (shift - 1);
+    if (rem > halfway || (rem == halfway && (q & 1u)))
+        ++q;
+    return sign | (uint16_t)q; // q == 1024 is the smallest normal, bit for bit
+}
+
+// Tables over all 65536 halves: value, and the half-rounded square.
+struct HalfTables
+{
+    float h2f[65536];
+    float sq[65536];
+    HalfTables()
+    {
+        for (uint32_t h = 0; h < 65536u; ++h)
+            h2f[h] = half_to_float((uint16_t)h);
+        for (uint32_t h = 0; h < 65536u; ++h)
+        {
+            const double d = (double)h2f[h];
+            sq[h] = half_to_float(double_to_half(d * d));
+        }
+    }
+};
+
+const HalfTables &half_tables()
+{
+    static const HalfTables t;
+    return t;
+}
+
+// (a - b) rounded to half, squared, rounded to half (the reference's
+// __hsub2 / __hmul2 pair), returned as float.
 float half_sq_diff(uint16_t a, uint16_t b)
 {
-    uint16_t diff = double_to_half((double)half_to_float(a) - (double)half_to_float(b));
-    double df = (double)half_to_float(diff);
-    return half_to_float(double_to_half(df * df));
+    const HalfTables &t = half_tables();
+    return t.sq[double_to_half_bits((double)t.h2f[a] - (double)t.h2f[b])];
 }
 
 float dist_f16(const uint16_t *x, const uint16_t *y, uint32_t dim)
 {
+    const HalfTables &t = half_tables();
     float acc[32] = {0};
     const uint32_t pairs = dim / 2;
     for (uint32_t h = 0; h < pairs; ++h)
@@ -177,7 +246,7 @@ float dist_f16(const uint16_t *x, const uint16_t *y, uint32_t dim)
     }
     if (dim & 1u)
     {
-        float d = half_to_float(x[dim - 1]) - half_to_float(y[dim - 1]);
+        float d = t.h2f[x[dim - 1]] - t.h2f[y[dim - 1]];
         acc[0] = std::fma(d, d, acc[0]);
     }
     return tree32(acc);
@@ -965,7 +1034,36 @@ float oracle_distance(int dtype, const void *a, const void *b, uint32_t dim)
 void oracle_float_to_half(const float *src, uint16_t *dst, uint64_t n)
 {
     for (uint64_t i = 0; i < n; ++i)
-        dst[i] = double_to_half((double)src[i]);
+        dst[i] = double_to_half_bits((double)src[i]);
+}
+
+// Mismatches between double_to_half_bits and the frexp definition over
+// every half value, the midpoints and quarter points between neighbouring
+// halves, and n_random differences of random half pairs.
+uint64_t oracle_half_selftest(uint64_t n_random)
+{
+    const HalfTables &t = half_tables();
+    uint64_t bad = 0;
+    for (uint32_t h = 0; h < 0x7C00u; ++h)
+    {
+        const double lo = (double)t.h2f[h], hi = (double)t.h2f[h + 1];
+        const double probes[5] = {lo, 0.5 * (lo + hi), 0.25 * (3 * lo + hi), 0.25 * (lo + 3 * hi), hi};
+        for (double v : probes)
+            for (double sgn : {1.0, -1.0})
+                bad += double_to_half_bits(sgn * v) != double_to_half(sgn * v);
+    }
+    uint64_t st = 0x9E3779B97F4A7C15ull;
+    for (uint64_t i = 0; i < n_random; ++i)
+    {
+        st ^= st << 13;
+        st ^= st >> 7;
+        st ^= st << 17;
+        const uint16_t a = (uint16_t)(st & 0x7BFFu), b = (uint16_t)((st >> 16) & 0xFBFFu);
+        const double d = (double)t.h2f[a] - (double)t.h2f[b];
+        bad += double_to_half_bits(d) != double_to_half(d);
+        bad += double_to_half_bits(d * d) != double_to_half(d * d);
+    }
+    return bad;
 }
 
 uint32_t oracle_hash_u32(uint32_t x) { return hash_u32(x); }
