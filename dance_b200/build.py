@@ -22,7 +22,7 @@ LIB = PKG / "libdance_b200.so"
 
 SOURCES = ["vamana_build.cu", "vamana_sharded.cu", "gpu_merge.cu", "stitched.cu", "filtered.cu"]
 HEADERS = ["dance_common.cuh", "vamana_kernels.cuh", "host_common.cuh", "filtered_kernels.cuh",
-           "gram_u8.cuh"]
+           "gram_u8.cuh", "prune_quad.cuh"]
 PUBLIC_HEADERS = ["dance_b200.h", "gpu_vamana_builder.h", "gpu_vamana_config.h", "gpu_merge.h",
                   "gpu_vamana_filtered.h"]
 

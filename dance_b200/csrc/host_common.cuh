@@ -20,6 +20,7 @@
 #include "../../include/gpu_vamana_config.h"
 #include "vamana_kernels.cuh"
 #include "gram_u8.cuh"
+#include "prune_quad.cuh"
 
 namespace dance
 {
@@ -298,13 +299,36 @@ struct LaunchPrune
 {
     static int run(PruneParams p, cudaStream_t s)
     {
-        if (DT == kU8)
+        if constexpr (DT == kU8)
             return run_gram(p, s);
+        else
+        {
+            if (CPL <= 3 && p.C <= 128)
+                return run_quad(p, s);
+        }
         auto k = prune_kernel<DT, CPL>;
         p.Cp = (uint32_t)next_pow2((int)p.C);
         if (p.Cp < 32)
             p.Cp = 32;
         p.per_warp = align16(prune_smem_per_warp(p.C, p.Cp, p.R, p.row_bytes));
+        const size_t smem = (size_t)p.per_warp * kWarpsPerBlock;
+        if ((int)smem > max_optin_smem())
+            return fail(-1, "prune vector cache %zu B exceeds shared memory", smem);
+        DANCE_CUDA(allow_smem(k, smem));
+        const int grid = wave_grid(k, kBlockThreads, smem, p.v1 - p.v0);
+        k<<<grid, kBlockThreads, smem, s>>>(p);
+        DANCE_LAUNCHED();
+        return 0;
+    }
+
+    // float / half rows of up to 24 chunks: eight pairs per pass
+    static int run_quad(PruneParams p, cudaStream_t s)
+    {
+        auto k = prune_quad_kernel<DT, (CPL <= 3 ? 2 * CPL : 2)>;
+        p.Cp = (uint32_t)next_pow2((int)p.C);
+        if (p.Cp < 32)
+            p.Cp = 32;
+        p.per_warp = align16(QuadPruneLayout(p.C, p.row_bytes).bytes);
         const size_t smem = (size_t)p.per_warp * kWarpsPerBlock;
         if ((int)smem > max_optin_smem())
             return fail(-1, "prune vector cache %zu B exceeds shared memory", smem);
