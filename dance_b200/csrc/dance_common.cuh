@@ -170,6 +170,114 @@ struct GroupDist<kU8, CPL>
     }
 };
 
+// Four-lane pair distance: the reference's warp arithmetic (virtual lanes
+// over 16-byte chunks and the shfl_down tree 16,8,4,2,1) evaluated by four
+// lanes instead of GroupDist's eight, so a warp pass covers eight pairs.
+// Lane sl holds chunks sl, sl+4, sl+8, ... (x[t] is chunk sl + 4t of the
+// first row).  For half, chunk c feeds virtual lanes 4 (c mod 8) + i, so a
+// lane's even chunks feed 4 sl + i and its odd ones 4 sl + 16 + i: tree
+// level 16 is in-lane, 8 and 4 are xor 2 and xor 1, 2 and 1 in-lane again.
+// For float, chunk c feeds virtual lane c mod 32 = sl + 4 (t mod 8): levels
+// 16, 8 and 4 are in-lane, 2 and 1 are xor 2 and xor 1.  Each virtual lane
+// adds its chunks in ascending order, as the reference lane does, so the
+// results are GroupDist's bit for bit.
+template <int DT, int T>
+struct QuadDist;
+
+template <int T>
+struct QuadDist<kF16, T>
+{
+    __device__ __forceinline__ static float eval(const uint4 (&x)[T], const uint8_t *row, uint32_t nchunks, int sl)
+    {
+        const uint4 *r = reinterpret_cast<const uint4 *>(row);
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int t = 0; t < T; ++t)
+        {
+            const uint32_t c = (uint32_t)(sl + 4 * t);
+            if (c < nchunks)
+            {
+                const uint4 y = r[c];
+                const __half2 *a = reinterpret_cast<const __half2 *>(&x[t]);
+                const __half2 *b = reinterpret_cast<const __half2 *>(&y);
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                {
+                    const __half2 df = __hsub2(a[i], b[i]);
+                    const __half2 pr = __hmul2(df, df);
+                    const float2 f = __half22float2(pr);
+                    acc[(t & 1) * 4 + i] = __fadd_rn(acc[(t & 1) * 4 + i], __fadd_rn(f.x, f.y));
+                }
+            }
+        }
+        float s[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            s[i] = __fadd_rn(acc[i], acc[4 + i]); // level 16
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            s[i] = __fadd_rn(s[i], __shfl_xor_sync(kFull, s[i], 2)); // level 8
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+            s[i] = __fadd_rn(s[i], __shfl_xor_sync(kFull, s[i], 1)); // level 4
+        return __fadd_rn(__fadd_rn(s[0], s[2]), __fadd_rn(s[1], s[3])); // levels 2, 1
+    }
+};
+
+template <int T>
+struct QuadDist<kF32, T>
+{
+    __device__ __forceinline__ static float eval(const uint4 (&x)[T], const uint8_t *row, uint32_t nchunks, int sl)
+    {
+        const uint4 *r = reinterpret_cast<const uint4 *>(row);
+        float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int t = 0; t < T; ++t)
+        {
+            const uint32_t c = (uint32_t)(sl + 4 * t);
+            if (c < nchunks)
+            {
+                const uint4 yv = r[c];
+                const float4 a = *reinterpret_cast<const float4 *>(&x[t]);
+                const float4 b = *reinterpret_cast<const float4 *>(&yv);
+                const float d0 = __fsub_rn(a.x, b.x);
+                const float d1 = __fsub_rn(a.y, b.y);
+                const float d2 = __fsub_rn(a.z, b.z);
+                const float d3 = __fsub_rn(a.w, b.w);
+                float p = __fmul_rn(d1, d1);
+                p = __fmaf_rn(d0, d0, p);
+                p = __fmaf_rn(d2, d2, p);
+                p = __fmaf_rn(d3, d3, p);
+                acc[t & 7] = __fadd_rn(acc[t & 7], p);
+            }
+        }
+        // virtual lane sl + 4u is acc[u]
+        const float b0 = __fadd_rn(acc[0], acc[4]), b1 = __fadd_rn(acc[1], acc[5]); // level 16
+        const float b2 = __fadd_rn(acc[2], acc[6]), b3 = __fadd_rn(acc[3], acc[7]);
+        const float c0 = __fadd_rn(b0, b2), c1 = __fadd_rn(b1, b3); // level 8
+        float r1 = __fadd_rn(c0, c1);                               // level 4
+        r1 = __fadd_rn(r1, __shfl_xor_sync(kFull, r1, 2));          // level 2
+        r1 = __fadd_rn(r1, __shfl_xor_sync(kFull, r1, 1));          // level 1
+        return r1;
+    }
+};
+
+// Position of the n-th (0-based) set bit of w; n < popc(w).
+__device__ __forceinline__ int nth_set_bit(uint32_t w, int n)
+{
+    int pos = 0;
+#pragma unroll
+    for (int half = 16; half > 0; half >>= 1)
+    {
+        const int c = __popc(w & ((1u << half) - 1u));
+        const bool up = n >= c;
+        n -= up ? c : 0;
+        w = up ? (w >> half) : w;
+        pos += up ? half : 0;
+    }
+    return pos;
+}
+
 // Load the fragment of `row` owned by group lane gl (zero beyond nchunks).
 template <int CPL>
 __device__ __forceinline__ void load_frag(uint4 (&f)[CPL], const uint8_t *row, uint32_t nchunks, int gl)

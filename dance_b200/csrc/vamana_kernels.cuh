@@ -903,9 +903,11 @@ template <int DT, int CPL>
 struct ReplayPairs
 {
     static constexpr bool kQuad = (DT == kU8 && CPL == 1);
-    static constexpr int kPairs = kQuad ? 8 : 4;
+    static constexpr bool kFQuad = (DT != kU8 && CPL <= 3); // float / half: QuadDist
+    static constexpr int kPairs = (kQuad || kFQuad) ? 8 : 4;
     static constexpr int kLanes = 32 / kPairs;
-    uint4 xf[kQuad ? 2 : CPL];
+    static constexpr int kT = kQuad ? 2 : (kFQuad ? 2 * CPL : CPL);
+    uint4 xf[kT];
     uint32_t nx;
     int pidx, sl;
     uint32_t c0, c1;
@@ -926,6 +928,16 @@ struct ReplayPairs
             xf[0] = c0 < nchunks ? r[c0] : make_uint4(0u, 0u, 0u, 0u);
             xf[1] = c1 < nchunks ? r[c1] : make_uint4(0u, 0u, 0u, 0u);
             nx = norm;
+        }
+        else if constexpr (kFQuad)
+        {
+            const uint4 *r = reinterpret_cast<const uint4 *>(row);
+#pragma unroll
+            for (int t = 0; t < kT; ++t)
+            {
+                const uint32_t c = (uint32_t)sl + 4u * (uint32_t)t;
+                xf[t] = c < nchunks ? r[c] : make_uint4(0u, 0u, 0u, 0u);
+            }
         }
         else
             load_frag_smem<CPL>(xf, row, nchunks, sl);
@@ -960,6 +972,8 @@ struct ReplayPairs
             dot += __shfl_xor_sync(kFull, dot, 2);
             return (float)(int32_t)(nx + norms[u] - 2u * dot);
         }
+        else if constexpr (kFQuad)
+            return QuadDist<DT, kT>::eval(xf, row, nchunks, sl);
         else
         {
             uint4 c[CPL];
