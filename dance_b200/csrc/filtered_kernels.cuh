@@ -828,6 +828,7 @@ struct PruneScratch
     uint32_t cover[kShortList];
     float pd[kShortList];
     uint32_t sel_labels[64];
+    uint32_t killw[kShortList / 32]; // entries a selection occludes, bit lane of word i = entry 32 i + lane
 };
 
 __device__ __forceinline__ void row_list(const PruneParams &p, uint32_t row, uint32_t &begin, uint32_t &n)
@@ -857,6 +858,9 @@ __global__ void __launch_bounds__(kThreads) fl_prune_kernel(PruneParams p)
     const int lane = threadIdx.x & 31, gl = lane & 7;
     unsigned long long evals = 0;
     const uint32_t count = p.rows ? p.nrows : p.st.N;
+    if ((uint32_t)lane < kShortList / 32)
+        w.killw[lane] = 0u;
+    __syncwarp();
     for (uint32_t r = blockIdx.x * kWarps + (threadIdx.x >> 5); r < count; r += gridDim.x * kWarps)
     {
         const uint32_t row = p.rows ? p.rows[r] : r;
@@ -944,13 +948,21 @@ __global__ void __launch_bounds__(kThreads) fl_prune_kernel(PruneParams p)
                                          reinterpret_cast<const uint32_t *>(w.pd), w.pd, (int)m, lane);
                 __syncwarp();
                 evals += m;
-                for (uint32_t i = 0; i < m; ++i)
+                // occluded entries leave the live set (order-free: only removals)
+                for (uint32_t i = lane; i < m; i += 32)
                 {
                     const uint32_t k = w.cover[i];
                     const float pd = w.pd[i];
-                    if ((k & 31u) == (uint32_t)lane && pd > 0.0f && __fmul_rn(p.alpha, pd) <= w.d[k])
-                        live &= ~(1u << (k >> 5));
+                    if (pd > 0.0f && __fmul_rn(p.alpha, pd) <= w.d[k])
+                        atomicOr(&w.killw[k >> 5], 1u << (k & 31u));
                 }
+                __syncwarp();
+                for (uint32_t i = 0; i * 32 < n; ++i)
+                    if ((w.killw[i] >> lane) & 1u)
+                        live &= ~(1u << i);
+                __syncwarp();
+                if ((uint32_t)lane < kShortList / 32)
+                    w.killw[lane] = 0u;
             }
             __syncwarp();
         }
