@@ -829,7 +829,30 @@ struct PruneScratch
     float pd[kShortList];
     uint32_t sel_labels[64];
     uint32_t killw[kShortList / 32]; // entries a selection occludes, bit lane of word i = entry 32 i + lane
+    uint32_t cmask[kShortList];      // per entry: bit t = it carries the row's label t (rows of <= 32 labels)
 };
+
+// Bit t set when the candidate carries the row's label rl[t] (nr <= 32).
+__device__ __forceinline__ uint32_t row_label_mask(const Labels &L, const uint32_t *rl, uint32_t nr, uint32_t cand)
+{
+    uint32_t t = 0, c = L.off[cand], m = 0;
+    const uint32_t ce = L.off[cand + 1];
+    while (t < nr && c < ce)
+    {
+        const uint32_t a = rl[t], b = L.lab[c];
+        if (a < b)
+            ++t;
+        else if (b < a)
+            ++c;
+        else
+        {
+            m |= 1u << t;
+            ++t;
+            ++c;
+        }
+    }
+    return m;
+}
 
 __device__ __forceinline__ void row_list(const PruneParams &p, uint32_t row, uint32_t &begin, uint32_t &n)
 {
@@ -870,10 +893,16 @@ __global__ void __launch_bounds__(kThreads) fl_prune_kernel(PruneParams p)
             continue;
         const uint32_t lb = p.L.off[row], nl = p.L.off[row + 1] - lb;
         const uint32_t *rl = p.L.lab + lb;
+        // rows of up to 32 labels: coverage by a selection becomes a mask test,
+        // (labels shared by row and entry) subset of (row labels the selection carries)
+        const bool masks = nl <= 32;
         for (uint32_t k = lane; k < n; k += 32)
         {
-            w.ids[k] = p.list_ids[begin + k];
+            const uint32_t id = p.list_ids[begin + k];
+            w.ids[k] = id;
             w.d[k] = p.list_d[begin + k];
+            if (masks)
+                w.cmask[k] = id < p.st.N ? row_label_mask(p.L, rl, nl, id) : 0u;
         }
         __syncwarp();
         uint32_t *out = p.graph + (uint64_t)row * p.R;
@@ -925,11 +954,24 @@ __global__ void __launch_bounds__(kThreads) fl_prune_kernel(PruneParams p)
                 sl = w.sel_labels;
             }
             // live entries whose shared labels the selection covers
+            uint32_t smask = 0;
+            if (masks)
+            {
+                bool has = false;
+                if ((uint32_t)lane < nl)
+                {
+                    const uint32_t a = rl[lane];
+                    for (uint32_t s2 = 0; s2 < ns && !has; ++s2)
+                        has = sl[s2] == a;
+                }
+                smask = __ballot_sync(kFull, has);
+            }
             uint32_t m = 0;
             for (uint32_t i = 0; i * 32 < n; ++i)
             {
                 const uint32_t k = i * 32 + lane;
-                const bool cand = k < n && ((live >> i) & 1u) && covers(p.L, rl, nl, sl, ns, w.ids[k]);
+                const bool cand = k < n && ((live >> i) & 1u) &&
+                                  (masks ? (w.cmask[k] & ~smask) == 0u : covers(p.L, rl, nl, sl, ns, w.ids[k]));
                 const unsigned cb = __ballot_sync(kFull, cand);
                 if (cand)
                     w.cover[m + __popc(cb & ((1u << lane) - 1u))] = k;
