@@ -73,7 +73,7 @@ FilteredSetup make_setup(uint32_t N, uint32_t R, uint32_t L, uint32_t FL, uint32
 
 struct FilteredWorkspace
 {
-    DevBuf off, lab, lpo, lp, starts, task_rows;
+    DevBuf off, lab, lpo, lp, starts, task_rows, label_bits;
     DevBuf ga, da, gb, db;
     DevBuf task_ids, task_d, union_ids, union_d;
     DevBuf work_ids, work_d, work_deg;
@@ -115,6 +115,10 @@ struct FilteredWorkspace
     }
 };
 
+// Largest label-membership bitmap (num_labels x N bits) kept on the device;
+// larger vocabularies test membership through the points' label lists.
+constexpr uint64_t kLabelBitsBudget = 1ull << 30;
+
 // Labels on the device; the label -> points postings are built on the host
 // (ascending points, as the reference's h_label_points :5762-5773).
 int upload_labels(FilteredWorkspace &ws, uint32_t N, const uint32_t *h_off, const uint32_t *h_lab,
@@ -149,6 +153,20 @@ int upload_labels(FilteredWorkspace &ws, uint32_t N, const uint32_t *h_off, cons
     L.lp = ws.lp.as<uint32_t>();
     L.starts = ws.starts.as<uint32_t>();
     L.num_labels = num_labels;
+    // membership bitmaps, when they take at most kLabelBitsBudget bytes
+    const uint64_t words = ((uint64_t)N + 31) / 32;
+    const uint64_t bytes = words * 4 * (uint64_t)num_labels;
+    L.bits = nullptr;
+    L.bit_words = words;
+    if (num_labels && bytes <= kLabelBitsBudget)
+    {
+        DANCE_CUDA(ws.label_bits.ensure(bytes));
+        DANCE_CUDA(cudaMemsetAsync(ws.label_bits.p, 0, bytes, s));
+        const int grid = (int)std::min<uint64_t>(((uint64_t)N + 255) / 256, (uint64_t)sm_count() * 8);
+        fl::fl_label_bits_kernel<<<grid, 256, 0, s>>>(N, L.off, L.lab, words, ws.label_bits.as<uint32_t>());
+        DANCE_LAUNCHED();
+        L.bits = ws.label_bits.as<uint32_t>();
+    }
     return 0;
 }
 

@@ -49,11 +49,16 @@ struct Labels
     const uint32_t *starts; // num_labels
     uint32_t num_labels;
     uint32_t universal;
+    const uint32_t *bits; // optional: label l's members as a bitmap of bit_words words, or nullptr
+    uint64_t bit_words;
 };
 
-// point_has_exact_label_device (ref :557-571)
+// point_has_exact_label_device (ref :557-571); with the label bitmaps one
+// load instead of the point's label list.
 __device__ __forceinline__ bool has_label(const Labels &L, uint32_t p, uint32_t l)
 {
+    if (L.bits)
+        return (L.bits[(uint64_t)l * L.bit_words + (p >> 5)] >> (p & 31u)) & 1u;
     const uint32_t e = L.off[p + 1];
     for (uint32_t i = L.off[p]; i < e; ++i)
     {
@@ -1280,6 +1285,15 @@ static __global__ void fl_random_graph_kernel(uint32_t N, uint32_t R, uint32_t i
 }
 
 // task_rows[p] = the point whose label position p is (ref canonical_make_task_rows :4139-4146).
+// Label membership bitmaps: bit p of label l's bitmap for every (p, l) pair.
+static __global__ void fl_label_bits_kernel(uint32_t N, const uint32_t *off, const uint32_t *lab,
+                                            uint64_t bit_words, uint32_t *bits)
+{
+    for (uint32_t p = blockIdx.x * blockDim.x + threadIdx.x; p < N; p += gridDim.x * blockDim.x)
+        for (uint32_t i = off[p]; i < off[p + 1]; ++i)
+            atomicOr(&bits[(uint64_t)lab[i] * bit_words + (p >> 5)], 1u << (p & 31u));
+}
+
 static __global__ void fl_task_rows_kernel(uint32_t N, const uint32_t *off, uint32_t *task_rows)
 {
     for (uint32_t row = blockIdx.x * blockDim.x + threadIdx.x; row < N; row += gridDim.x * blockDim.x)
