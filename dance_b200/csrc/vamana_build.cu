@@ -719,8 +719,9 @@ int gpu_vamana_vnew2_build_device_float(const float *h_data, uint32_t num_points
     return rc ? -1 : 0;
 }
 
-// The legacy v8 entry points build with the same engine (see DESIGN.md for
-// the v8-specific schedule differences that are not reproduced).
+// The legacy v8 entry points (reference src/gpu_vamana_uint8.cu) build with
+// the vnew2 engine above: same rules and outputs format; the v8 file's own
+// schedule (C-wide ping-pong graph buffers between rounds) is not reproduced.
 int gpu_vamana_build(const uint8_t *h_data, uint32_t num_points, uint32_t dim, uint32_t R, uint32_t L, uint32_t C,
                      uint32_t STEPS, uint32_t *h_graph, uint32_t *h_degree)
 {
