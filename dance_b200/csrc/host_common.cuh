@@ -303,7 +303,7 @@ struct LaunchPrune
             return run_gram(p, s);
         else
         {
-            if (CPL <= 3 && p.C <= 128)
+            if (CPL <= 4 && p.C <= 128)
                 return run_quad(p, s);
         }
         auto k = prune_kernel<DT, CPL>;
@@ -321,10 +321,10 @@ struct LaunchPrune
         return 0;
     }
 
-    // float / half rows of up to 24 chunks: eight pairs per pass
+    // float / half rows of up to 32 chunks: eight pairs per pass
     static int run_quad(PruneParams p, cudaStream_t s)
     {
-        auto k = prune_quad_kernel<DT, (CPL <= 3 ? 2 * CPL : 2)>;
+        auto k = prune_quad_kernel<DT, (CPL <= 4 ? 2 * CPL : 2)>;
         p.Cp = (uint32_t)next_pow2((int)p.C);
         if (p.Cp < 32)
             p.Cp = 32;

@@ -903,7 +903,7 @@ template <int DT, int CPL>
 struct ReplayPairs
 {
     static constexpr bool kQuad = (DT == kU8 && CPL == 1);
-    static constexpr bool kFQuad = (DT != kU8 && CPL <= 3); // float / half: QuadDist
+    static constexpr bool kFQuad = (DT != kU8 && CPL <= 4); // float / half: QuadDist
     static constexpr int kPairs = (kQuad || kFQuad) ? 8 : 4;
     static constexpr int kLanes = 32 / kPairs;
     static constexpr int kT = kQuad ? 2 : (kFQuad ? 2 * CPL : CPL);
