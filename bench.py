@@ -52,7 +52,13 @@ def parse():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-recall", action="store_true")
-    ap.add_argument("--ref-gpu", action="store_true",
+    ap.add_argument("--no-ref-gpu", dest="ref_gpu", action="store_false",
+                    help="skip the reference's own GPU build (run by default at N=1)")
+    ap.add_argument("--no-others", action="store_true",
+                    help="skip the other workloads that the default N=1 line carries in other_workloads")
+    ap.add_argument("--cfg0-storage", choices=["f16", "f32"], default="f16",
+                    help="cfg0_f32 vector storage: f16 (the reference's FAST_SMALL) or f32 (QUALITY)")
+    ap.add_argument("--ref-gpu", action="store_true", default=True,
                     help="also time the reference's own GPU builder (oracle/_ref, sm_100a) once on the workload")
     ap.add_argument("--workload", choices=["cfg1_u8_10M", "cfg0_f32", "cfg2_filtered", "cfg3_stitched"],
                     default="cfg1_u8_10M",
@@ -121,6 +127,25 @@ class ClockSampler:
                     reasons.add(n)
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
                 "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def emit(args, line):
+    """Print the JSON line, or hand it to the caller that collects the other
+    workloads into the headline line (args.collect)."""
+    if getattr(args, "collect", None) is not None:
+        args.collect.append(line)
+    else:
+        print(json.dumps(line), flush=True)
+
+
+def graph_digest(graph, degree, n):
+    """sha256 (first 16 hex digits) of the first n graph rows and degrees as
+    int32 bytes: equal digests across N=1/2/4/8 show identical graphs."""
+    import hashlib
+    h = hashlib.sha256()
+    h.update(graph[:n].contiguous().cpu().numpy().tobytes())
+    h.update(degree[:n].contiguous().cpu().numpy().tobytes())
+    return h.hexdigest()[:16]
 
 
 def measured_peaks():
@@ -201,7 +226,7 @@ def run_reference(args):
         "note": ("DANCE has no CPU implementation of this path and DiskANN's CPU Vamana is not vendored; "
                  "this arm runs the C++ restatement of the reference algorithm (oracle/vamana_oracle.cpp)"),
     }
-    print(json.dumps(line), flush=True)
+    emit(args, line)
     return 0
 
 
@@ -325,6 +350,9 @@ def run_ours(args):
         # the C-ABI graph equals the device-resident build's graph
         line["e2e"]["matches_resident_build"] = bool(torch.equal(hg.cuda(), graph))
         del hx
+    deg = degree.cpu().numpy()
+    line["graph"] = {"medoid": int(medoid), "avg_degree": float(deg.mean()), "max_degree": int(deg.max()),
+                     "min_degree": int(deg.min()), "digest": graph_digest(graph, degree, n)}
     # ---- recall@10 at L_search=100 on 10k queries against brute force
     if not args.no_recall:
         q = make_queries("cuda")
@@ -332,9 +360,6 @@ def run_ours(args):
         ids, _ = vamana.search_queries(store, WORKLOAD["dim"], stride, graph, R, medoid, q, 100, 10)
         line["recall_at_10"] = {"L_search": 100, "queries": int(q.shape[0]),
                                 "ours": vamana.recall_at_k(ids.cpu().numpy(), gt.cpu().numpy())}
-        deg = degree.cpu().numpy()
-        line["graph"] = {"medoid": int(medoid), "avg_degree": float(deg.mean()), "max_degree": int(deg.max()),
-                         "min_degree": int(deg.min())}
     # ---- CPU baseline: the oracle restatement on the host cores, bounded sample
     if not args.no_cpu_baseline:
         sample = x[:min(CPU_BASELINE_SAMPLE, n)].cpu().numpy()
@@ -344,10 +369,61 @@ def run_ours(args):
                                 "sample": f"first {len(sample)} vectors of the workload, full 4-round build "
                                           f"({secs:.1f} s)"}
     if args.ref_gpu:
-        line["reference_gpu"] = reference_gpu(x, store, stride, medoid, args)
-    print(json.dumps(line), flush=True)
+        ref = reference_gpu(x, store, stride, medoid, args)
+        line["reference_gpu"] = ref
+        add_recall_delta(line, ref)
     ws.close()
+    if not args.no_others and n == WORKLOAD["N"]:
+        del graph, degree, dists, store, x, ws
+        torch.cuda.empty_cache()
+        line["other_workloads"] = run_other_workloads(args)
+    emit(args, line)
     return 0
+
+
+def add_recall_delta(line, ref):
+    """recall_at_10.reference / .delta from the reference GPU build's recall on
+    the same queries, with the same searcher (north_star: |delta| <= 0.005)."""
+    rec = line.get("recall_at_10")
+    if rec is not None and isinstance(ref, dict) and "recall_at_10" in ref:
+        rec["reference"] = ref["recall_at_10"]
+        rec["delta"] = rec["ours"] - ref["recall_at_10"]
+        rec["within_0.005"] = abs(rec["delta"]) <= 0.005
+
+
+def run_other_workloads(args):
+    """The other BASELINE.json configurations, each timed like the headline
+    (same warm-up and step counts, CUDA events, e2e through the C ABI, recall,
+    the reference's own GPU build on the same inputs), folded into the N=1
+    line.  Their CPU-oracle samples are left to their own --workload lines."""
+    import copy
+    import torch
+    out = {}
+    plan = [("cfg0_f32_quality", run_cfg0, {"cfg0_storage": "f32"}),
+            ("cfg0_f16_fast_small", run_cfg0, {"cfg0_storage": "f16"}),
+            ("cfg2_filtered", run_filtered, {}),
+            ("cfg3_stitched", run_stitched, {})]
+    keys = ("metric", "value", "unit", "ms_per_step", "steps", "warmup", "dtype", "config", "e2e", "recall_at_10",
+            "reference_gpu", "roofline", "graph", "gpu_launches", "stage_seconds", "clocks")
+    for name, fn, extra in plan:
+        sub = copy.copy(args)
+        sub.collect = []
+        sub.no_cpu_baseline = True
+        sub.n = WORKLOAD["N"]  # each workload's own default size
+        for k, v in extra.items():
+            setattr(sub, k, v)
+        t0 = time.perf_counter()
+        try:
+            fn(sub)
+            got = sub.collect[0]
+            entry = {k: got[k] for k in keys if k in got}
+        except Exception as e:  # recorded, not fatal: the headline line still prints
+            entry = {"error": f"{type(e).__name__}: {e}"}
+        entry["wall_s"] = time.perf_counter() - t0
+        out[name] = entry
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+    return out
 
 
 def reference_gpu(x, store, stride, our_medoid, args):
@@ -506,7 +582,7 @@ def run_sharded(args):
             line["e2e"] = e2e
         if rec is not None:
             line["recall_at_10"] = {"L_search": 100, "queries": WORKLOAD["queries"], "ours": rec}
-        print(json.dumps(line), flush=True)
+        emit(args, line)
     del ws
     comm.close()
     dist.barrier()
@@ -533,8 +609,13 @@ def cfg0_inputs(n):
     return x, q
 
 
-def cfg0_config(n):
+def cfg0_config(n, storage="f16"):
     C0 = CFG0
+    if storage == "f32":
+        return {"workload": "cfg0_f32_1M", "N": n, "dim": C0["dim"], "R": C0["R"], "L": C0["L"], "C": C0["C"],
+                "STEPS": C0["STEPS"], "alpha": C0["alpha"], "iters": C0["iters"], "seed": C0["seed"],
+                "storage": "fp32 (the reference's QUALITY profile: ENABLE_FLOAT16_BUILD=0)",
+                "l2": "inputs larger than L2 (384 MB fp32 vector store + graph rows), no flush"}
     return {"workload": C0["name"], "N": n, "dim": C0["dim"], "R": C0["R"], "L": C0["L"], "C": C0["C"],
             "STEPS": C0["STEPS"], "alpha": C0["alpha"], "iters": C0["iters"], "seed": C0["seed"],
             "storage": "fp16 (the reference's FAST_SMALL profile: ENABLE_FLOAT16_BUILD=1)",
@@ -543,7 +624,8 @@ def cfg0_config(n):
 
 def run_cfg0(args):
     """1M x 96 normalised Gaussian mixture, float input
-    stored and searched in fp16 like the reference's FAST_SMALL profile."""
+    stored and searched in fp16 like the reference's FAST_SMALL profile
+    (--cfg0-storage f16, the default) or in fp32 like its QUALITY profile."""
     import torch
     import dance_b200
     from dance_b200 import vamana, workloads
@@ -556,7 +638,8 @@ def run_cfg0(args):
     n = args.n if args.n != WORKLOAD["N"] else C0["N"]
     R, L, C, S = C0["R"], C0["L"], C0["C"], C0["STEPS"]
     x, q = cfg0_inputs(n)
-    store, stride = vamana.padded_store(x.half())
+    f32 = getattr(args, "cfg0_storage", "f16") == "f32"
+    store, stride = vamana.padded_store(x if f32 else x.half())
     ws = vamana.Workspace.create(n, R, L, C, S)
     prm = dance_b200.default_params()
     graph = torch.empty((n, R), dtype=torch.int32, device="cuda")
@@ -596,9 +679,9 @@ def run_cfg0(args):
     line = {
         "metric": "vamana_build_vectors_per_s", "value": n * args.steps / elapsed, "unit": "vectors/s",
         "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3,
-        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32" if f32 else "f16",
         "data": "synthetic (seeded GPU generator, BASELINE.json configs[0] recipe)",
-        "config": cfg0_config(n),
+        "config": cfg0_config(n, "f32" if f32 else "f16"),
         "roofline": {"kernel": "search_kernel", "bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_source": peak_kind, "traffic": None,
                      "algorithmic_bytes_per_launch": alg / (len(reports) * C0["iters"]),
@@ -611,8 +694,9 @@ def run_cfg0(args):
         "published_reference": CFG0_PUBLISHED,
     }
     if not args.no_e2e:
-        # the reference's float entry point; fp16 storage selected at run time
-        os.environ["DANCE_FLOAT16_BUILD"] = "1"
+        # the reference's float entry point; the storage is selected at run time
+        saved_env = os.environ.get("DANCE_FLOAT16_BUILD")
+        os.environ["DANCE_FLOAT16_BUILD"] = "0" if f32 else "1"
         hx = x.cpu().pin_memory()
         hg = torch.empty((n, R), dtype=torch.int32).pin_memory()
         hd = torch.empty((n,), dtype=torch.int32).pin_memory()
@@ -632,36 +716,46 @@ def run_cfg0(args):
         e2e_dt = time.perf_counter() - t0
         line["e2e"] = {"value": n * args.steps / e2e_dt, "unit": "vectors/s", "h2d_bytes_per_step": int(hx.numel() * 4),
                        "d2h_bytes_per_step": int(hg.numel() * 4 + hd.numel() * 4),
-                       "api": "gpu_vamana_vnew2_build_float (reference C ABI, DANCE_FLOAT16_BUILD=1), pinned host "
-                              "buffers, wall clock", "warmup": 1,
+                       "api": f"gpu_vamana_vnew2_build_float (reference C ABI, DANCE_FLOAT16_BUILD="
+                              f"{0 if f32 else 1}), pinned host buffers, wall clock", "warmup": 1,
                        "matches_resident_build": bool(torch.equal(hg.cuda(), graph))}
+        if saved_env is None:
+            os.environ.pop("DANCE_FLOAT16_BUILD", None)
+        else:
+            os.environ["DANCE_FLOAT16_BUILD"] = saved_env
     if not args.no_recall:
         gt, _ = workloads.brute_force_knn(x, q, 10)
-        ids, _ = vamana.search_queries(store, C0["dim"], stride, graph, R, medoid, q.half(), 100, 10)
+        ids, _ = vamana.search_queries(store, C0["dim"], stride, graph, R, medoid, q if f32 else q.half(), 100, 10)
         line["recall_at_10"] = {"L_search": 100, "queries": int(q.shape[0]),
                                 "ours": vamana.recall_at_k(ids.cpu().numpy(), gt.cpu().numpy()),
                                 "ground_truth": "brute force on the float32 vectors"}
     if not args.no_cpu_baseline:
-        sample = x[:min(CFG0_CPU_SAMPLE, n)].half().cpu().numpy()
+        sample = (x[:min(CFG0_CPU_SAMPLE, n)] if f32 else x[:min(CFG0_CPU_SAMPLE, n)].half()).cpu().numpy()
         threads = os.cpu_count() or 1
         rate, secs = oracle_sample_rate(sample, threads)
         line["cpu_baseline"] = {"value": rate, "unit": "vectors/s", "cores": threads, "kind": "port",
-                                "sample": f"first {len(sample)} vectors of the workload (fp16), full 4-round "
+                                "sample": f"first {len(sample)} vectors of the workload ({sample.dtype}), full 4-round "
                                           f"build ({secs:.1f} s)"}
+    deg = degree.cpu().numpy()
+    line["graph"] = {"medoid": int(medoid), "avg_degree": float(deg.mean()), "max_degree": int(deg.max()),
+                     "min_degree": int(deg.min()), "digest": graph_digest(graph, degree, n)}
     if args.ref_gpu:
-        line["reference_gpu"] = reference_gpu_cfg0(x, q, store, stride)
-    print(json.dumps(line), flush=True)
+        ref = reference_gpu_cfg0(x, q, store, stride, f32)
+        line["reference_gpu"] = ref
+        add_recall_delta(line, ref)
+    emit(args, line)
     ws.close()
     return 0
 
 
-def reference_gpu_cfg0(x, q, store, stride):
-    """The reference's vnew2 builder in its FAST_SMALL profile (fp16 storage),
-    compiled for sm_100a, on the same float vectors through its C ABI."""
+def reference_gpu_cfg0(x, q, store, stride, f32=False):
+    """The reference's vnew2 builder in its FAST_SMALL profile (fp16 storage) or,
+    with f32, its QUALITY profile (fp32), compiled for sm_100a, on the same
+    float vectors through its C ABI."""
     import numpy as np
     import torch
     from dance_b200 import vamana, workloads
-    lib_path = ROOT / "oracle" / "_ref" / "libref_vnew2_fast_small.so"
+    lib_path = ROOT / "oracle" / "_ref" / ("libref_vnew2_quality.so" if f32 else "libref_vnew2_fast_small.so")
     if not lib_path.exists():
         return {"unavailable": f"{lib_path.name} not built"}
     lib = ctypes.CDLL(str(lib_path))
@@ -685,11 +779,12 @@ def reference_gpu_cfg0(x, q, store, stride):
     med = int(lib.gpu_vamana_vnew2_get_last_medoid())
     gt, _ = workloads.brute_force_knn(x, q, 10)
     gd = torch.from_numpy(g.view(np.int32)).cuda()
-    ids, _ = vamana.search_queries(store, C0["dim"], stride, gd, R, med, q.half(), 100, 10)
+    ids, _ = vamana.search_queries(store, C0["dim"], stride, gd, R, med, q if f32 else q.half(), 100, 10)
     return {"e2e_vectors_per_s": n / dt, "seconds": dt,
             "recall_at_10": vamana.recall_at_k(ids.cpu().numpy(), gt.cpu().numpy()), "medoid": med,
             "avg_degree": float(d.mean()),
-            "build": "DANCE vnew2 FAST_SMALL profile (fp16 storage, VAMANA_ITERS=4), nvcc 12.9 sm_100a"}
+            "build": ("DANCE vnew2 QUALITY profile (fp32 storage" if f32 else
+                      "DANCE vnew2 FAST_SMALL profile (fp16 storage") + ", VAMANA_ITERS=4), nvcc 12.9 sm_100a"}
 
 
 def run_cfg0_reference(args):
@@ -722,7 +817,7 @@ def run_cfg0_reference(args):
         "cpu_baseline": {"value": value, "unit": "vectors/s", "cores": threads, "kind": "port", "sample": desc},
         "e2e": {"value": value, "unit": "vectors/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
-    print(json.dumps(line), flush=True)
+    emit(args, line)
     return 0
 
 
@@ -976,6 +1071,8 @@ def run_stitched(args):
         line["cpu_baseline"] = {"value": tot / secs, "unit": "vectors/s", "cores": threads, "kind": "port",
                                 "sample": f"the {len(chosen)} smallest labels ({tot} points), per-label builds and "
                                           f"remap ({secs:.1f} s)"}
+    import hashlib
+    line["graph"]["digest"] = hashlib.sha256(row_offsets.tobytes() + row_ids[:E].tobytes()).hexdigest()[:16]
     if args.ref_gpu:
         ref = reference_gpu_stitched(hx, label_points)
         if "rows" in ref:
@@ -985,7 +1082,8 @@ def run_stitched(args):
                                                                                                row_ids[:E]))
             ref["medoids_equal_ours"] = ref.pop("medoids") == medoids
         line["reference_gpu"] = ref
-    print(json.dumps(line), flush=True)
+        add_recall_delta(line, ref)
+    emit(args, line)
     return 0
 
 
@@ -1205,8 +1303,9 @@ def run_filtered(args):
     if not args.no_recall:
         line["recall_at_10"] = {"L_search": 100, "queries": F["queries"], "search": "label-filtered, from the label start",
                                 "ours": filtered_recall(x, store, stride, offs, labs, graph, starts, R, q, qlabels)}
-        deg = degree.cpu().numpy()
-        line["graph"] = {"avg_degree": float(deg.mean()), "max_degree": int(deg.max()), "min_degree": int(deg.min())}
+    deg = degree.cpu().numpy()
+    line["graph"] = {"avg_degree": float(deg.mean()), "max_degree": int(deg.max()), "min_degree": int(deg.min()),
+                     "digest": graph_digest(graph, degree, n)}
     if not args.no_cpu_baseline:
         import oracle
         m = min(FILTERED_CPU_SAMPLE, n)
@@ -1222,9 +1321,10 @@ def run_filtered(args):
         line["cpu_baseline"] = {"value": m / secs, "unit": "vectors/s", "cores": threads, "kind": "port",
                                 "sample": f"first {m} points with their labels, 3-round canonical build ({secs:.1f} s)"}
     if args.ref_gpu:
-        line["reference_gpu"] = reference_gpu_filtered(hx, offs, labs, starts, gstart, x, store, stride, q, qlabels,
-                                                       graph)
-    print(json.dumps(line), flush=True)
+        ref = reference_gpu_filtered(hx, offs, labs, starts, gstart, x, store, stride, q, qlabels, graph)
+        line["reference_gpu"] = ref
+        add_recall_delta(line, ref)
+    emit(args, line)
     return 0
 
 

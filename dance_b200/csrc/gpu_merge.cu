@@ -22,6 +22,7 @@
 // spreads buckets over several GPUs, one host thread each, like the
 // reference's round-robin (:643-650).
 
+#include <cuda.h> // CUcontext / CUresult types for the context id lookup
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -359,22 +360,56 @@ constexpr uint32_t kNaWords = kNaSeg + na_align(kNoAllocMaxEdges);
 
 static __device__ __align__(256) uint32_t g_merge_noalloc_scratch[kNaWords];
 
-// Address of this device's copy of the scratch array, looked up once per
-// device (cudaGetSymbolAddress loads the module on first use).
+// Unique id of the calling thread's current CUDA context (cuCtxGetId, reached
+// through the runtime's driver entry-point table so the library needs no
+// libcuda link), or 0 when there is none yet or the driver lacks the call.
+static unsigned long long current_context_id()
+{
+    using GetCurrent = CUresult (*)(CUcontext *);
+    using GetId = CUresult (*)(CUcontext, unsigned long long *);
+    static GetCurrent get_current = nullptr;
+    static GetId get_id = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q{};
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<GetCurrent>(p);
+        p = nullptr;
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<GetId>(p);
+    });
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS)
+        return 0;
+    return id;
+}
+
+// Address of this device's copy of the scratch array.  It is looked up with
+// cudaGetSymbolAddress (which loads the module on first use) at the first
+// call on a device and again whenever that device's context has changed
+// since, e.g. after cudaDeviceReset: a new context loads the module afresh
+// and the array moves.
 static int merge_noalloc_scratch(uint32_t **out)
 {
     static std::mutex mu;
     static uint32_t *addr[64] = {};
+    static unsigned long long ctx_of[64] = {};
     int dev = 0;
     DANCE_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64)
         return fail(-1, "device ordinal %d out of range for the merge scratch table", dev);
     std::lock_guard<std::mutex> lock(mu);
-    if (!addr[dev])
+    const unsigned long long ctx = current_context_id();
+    if (!addr[dev] || ctx == 0 || ctx != ctx_of[dev])
     {
         void *p = nullptr;
         DANCE_CUDA(cudaGetSymbolAddress(&p, g_merge_noalloc_scratch));
         addr[dev] = static_cast<uint32_t *>(p);
+        ctx_of[dev] = current_context_id(); // the lookup made the device's context current
     }
     *out = addr[dev];
     return 0;

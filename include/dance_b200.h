@@ -180,11 +180,14 @@ DANCE_API int dance_merge_edges_device(const uint32_t *d_src, const uint32_t *d_
  * Scratch is one fixed array in the library's device memory (about 4.3 MiB
  * per device): at most 16384 sources (node_count) and 1048576 edges
  * (n_edges); larger requests return -5 before any work is issued.  The
- * first call on a device looks the array up (cudaGetSymbolAddress); if the
- * calls are to be made inside stream capture, make one call on that device
- * before capture begins.  All calls on one device share the array, so calls
- * that overlap in time (from several host threads, or on several streams)
- * race on it and give wrong results: run them one after another. */
+ * first call on a device (and the first after that device's context was
+ * re-created, e.g. by cudaDeviceReset) looks the array's device address up
+ * with cudaGetSymbolAddress; make that first call before any stream
+ * capture begins.  Every call waits for its stream to finish before it
+ * returns, to read the kernels' error word.  All calls on one device share
+ * the array, so calls that overlap in time (from several host threads, or
+ * on several streams) race on it and give wrong results: run them one after
+ * another. */
 DANCE_API int dance_merge_edges_device_noalloc(const uint32_t *d_src, const uint32_t *d_dst, uint64_t n_edges,
                                                uint32_t node_begin, uint32_t node_count, uint32_t max_degree,
                                                uint64_t seed, uint32_t *d_out_neighbors, uint32_t *d_out_degrees,

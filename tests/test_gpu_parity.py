@@ -321,7 +321,66 @@ def test_full_build_config_shape_u8():
     assert g[3] == o[3] and np.array_equal(g[0], o[0]) and np.array_equal(g[1], o[1])
 
 
-@pytest.mark.parametrize("dtype,dim", [(np.float32, 100), (np.uint8, 100), (np.float32, 20), (np.float16, 90)])
+@pytest.mark.parametrize("dtype", [np.float32, np.float16])
+def test_full_build_config_shape_float(dtype):
+    # float32 (QUALITY) and float16 storage (FAST_SMALL) whole builds at the
+    # benchmarked shape R64 L100 C80 STEPS64: the four-lane float prune and
+    # replay at C=80, the last-round fill to 64, the heavy-cap-off merge
+    x = make(dtype, 8000, centroids=64)
+    R, L, C, S = 64, 100, 80, 64
+    g = _gpu_build(x, R, L, C, S)
+    o = oracle.build_graph(x, R, L, C, S)
+    assert g[3] == o[3] and np.array_equal(g[1], o[1]) and np.array_equal(g[0], o[0])
+    assert np.array_equal(g[2], o[2])
+
+
+def _golden_cfgshape_cases():
+    import json
+    from pathlib import Path
+    m = Path(__file__).resolve().parent / "golden" / "manifest.json"
+    cases = json.loads(m.read_text()) if m.exists() else []
+    return [c for c in cases if "data_spec" in c and c.get("builder", "vnew2") == "vnew2"]
+
+
+@pytest.mark.parametrize("case", _golden_cfgshape_cases(), ids=lambda c: c["file"])
+def test_config_shape_build_against_reference_golden(case):
+    """The GPU build at R64 L100 C80 STEPS64 (N=20000) against the reference's
+    own build of the same input: bit-exact to the oracle (product rule), row
+    agreement with the reference no worse than the reference's agreement with
+    itself over two runs, minus the pool tie-break margin, and recall@10 at
+    L=100 within 0.005 of the reference graph's on the same queries."""
+    import torch
+    from pathlib import Path
+    from tests.golden.make_golden import case_data, case_graph, agreement, gen_queries
+    z = np.load(Path(__file__).resolve().parent / "golden" / case["file"])
+    x = case_data(case, z)
+    if case["storage"] == "f16":
+        x = x.astype(np.float16)
+    R, L, C, S = case["R"], case["L"], case["C"], case["STEPS"]
+    prm = default_params()
+    prm.iters = case["iters"]
+    g = _gpu_build(x, R, L, C, S, prm)
+    o = oracle.build_graph(x, R, L, C, S, oracle.params(iters=case["iters"]))
+    assert g[3] == o[3] and np.array_equal(g[0], o[0]) and np.array_equal(g[1], o[1])
+    rg, rd = case_graph(z), z["degree"].astype(np.uint32)
+    rows, sets = agreement(g[0], g[1], rg, rd)
+    selfagr = case["reference_self_agreement"]
+    assert rows >= selfagr["rows"] - 0.02, (rows, selfagr)
+    assert sets >= selfagr["row_sets"] - 0.02, (sets, selfagr)
+    if case["iters"] == 4:
+        q = torch.from_numpy(gen_queries(case["data_spec"], 1000, seed=77).astype(x.dtype))
+        xt = torch.from_numpy(np.ascontiguousarray(x))
+        gt, _ = workloads.brute_force_knn(xt.cuda(), q.cuda(), 10)
+        st, stride, _ = store(x)
+        ours, _ = vamana.search_queries(st, x.shape[1], stride, dev(g[0]), R, g[3], q.cuda(), 100, 10)
+        theirs, _ = vamana.search_queries(st, x.shape[1], stride, dev(rg), R, int(z["medoid"]), q.cuda(), 100, 10)
+        r_ours = vamana.recall_at_k(ours.cpu().numpy(), gt.cpu().numpy())
+        r_ref = vamana.recall_at_k(theirs.cpu().numpy(), gt.cpu().numpy())
+        assert abs(r_ours - r_ref) <= 0.005, (r_ours, r_ref)
+
+
+@pytest.mark.parametrize("dtype,dim", [(np.float32, 100), (np.uint8, 100), (np.float32, 20), (np.float16, 90),
+                                       (np.float32, 128), (np.float16, 256)])
 def test_padded_rows(dtype, dim):
     x = make(dtype, 2000, dim=dim)
     g = _gpu_build(x, 16, 32, 24, 16)

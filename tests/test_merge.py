@@ -170,3 +170,55 @@ def test_merge_error_codes(tmp_path, dance_lib):
     (tmp_path / "bad0.idx").write_bytes(bytes(blob))
     assert call("bad") == -4
     assert call("shard") == 0
+
+
+# ---------------------------------------------------------------- reference goldens
+GOLDEN = __import__("pathlib").Path(__file__).resolve().parent / "golden"
+
+
+def _merge_golden_cases():
+    import json
+    m = GOLDEN / "manifest_merge.json"
+    return json.loads(m.read_text()) if m.exists() else []
+
+
+def _golden_inputs(tmp_path, case):
+    from tests.golden.make_golden_merge import write_shards
+    recipe = dict(case["shards"])
+    if "hubs" in recipe:
+        recipe["hubs"] = tuple(recipe["hubs"])
+    src, dst, medoids, digest = write_shards(tmp_path, **recipe)
+    assert digest == case["inputs_sha256"], "regenerated shard files differ from the golden's inputs"
+    z = np.load(GOLDEN / case["file"])
+    return src, dst, medoids, z["graph_file"].tobytes(), z["medoids_file"].tobytes()
+
+
+@pytest.mark.parametrize("case", _merge_golden_cases(), ids=lambda c: c["file"])
+def test_oracle_merge_matches_reference_goldens(tmp_path, case):
+    """The oracle's merge rule reproduces the files the reference's own
+    merge_shards_gpu wrote (tests/golden/make_golden_merge.py), byte for byte."""
+    src, dst, medoids, gfile, mfile = _golden_inputs(tmp_path, case)
+    R = case["max_degree"]
+    seed = int(case["env"].get("DISKANN_GPU_MERGE_HASH_SEED", SEED))
+    nnodes = int(max(src.max(initial=0), dst.max(initial=0))) + 1
+    keep = src != dst
+    rows, deg = oracle.merge_edges(src[keep], dst[keep], nnodes, R, seed=seed)
+    expected = formats.encode_graph(rows, deg, medoids[-1])
+    expected = expected[:8] + struct.pack("<I", R) + expected[12:]
+    assert expected == gfile
+    assert mfile == struct.pack("<II", len(medoids), 1) + np.array(medoids, np.uint32).tobytes()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("case", _merge_golden_cases(), ids=lambda c: c["file"])
+def test_merge_shards_gpu_matches_reference_goldens(tmp_path, case, dance_lib, monkeypatch):
+    _, _, medoids, gfile, mfile = _golden_inputs(tmp_path, case)
+    for k, v in case["env"].items():
+        monkeypatch.setenv(k, v)
+    out, med = tmp_path / "merged.idx", tmp_path / "medoids.bin"
+    pre = str(tmp_path / "shard").encode()
+    rc = dance_lib.dance_merge_shards_gpu(pre, b".idx", pre, b"_ids.bin", case["shards"]["nshards"],
+                                          case["max_degree"], str(out).encode(), str(med).encode())
+    assert rc == 0
+    assert out.read_bytes() == gfile
+    assert med.read_bytes() == mfile
