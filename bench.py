@@ -510,11 +510,13 @@ def run_sharded(args):
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     reports = []
+    sreports = []
     torch.cuda.synchronize()
     ev0.record(stream)
     for _ in range(args.steps):
         _, _, medoid = one_build()
         reports.append(dance_b200.last_build_report())
+        sreports.append(dance_b200.last_sharded_report())
     ev1.record(stream)
     torch.cuda.synchronize()
     launches = lib.dance_kernel_launch_count() - launches0
@@ -530,6 +532,16 @@ def run_sharded(args):
     dist.all_reduce(kmax, op=dist.ReduceOp.MAX)
     ksum = kt.clone()
     dist.all_reduce(ksum, op=dist.ReduceOp.SUM)
+    # per-stage device time per build on every rank (mean over the timed builds), max and min over ranks
+    skeys = [k for k in sreports[0] if k.endswith("_seconds")]
+    sv = torch.tensor([statistics.mean(r[k] for r in sreports) for k in skeys], dtype=torch.float64, device="cuda")
+    smax, smin = sv.clone(), sv.clone()
+    dist.all_reduce(smax, op=dist.ReduceOp.MAX)
+    dist.all_reduce(smin, op=dist.ReduceOp.MIN)
+    stage_table = {k: {"max": float(smax[i]), "min": float(smin[i])} for i, k in enumerate(skeys)}
+    stage_table["edge_bytes_received_per_rank"] = int(sreports[-1]["edge_bytes_received"])
+    stage_table["graph_bytes_received_per_rank"] = int(sreports[-1]["graph_bytes_received"])
+    digest = graph_digest(graph, degree, n) if rank == 0 else None
     # e2e: every rank copies the vectors from pinned host memory, builds, rank 0 reads the graph back
     e2e = None
     if not args.no_e2e:
@@ -577,6 +589,8 @@ def run_sharded(args):
                          "traffic": None},
             "gpu_launches": int(launches), "gpu_launches_scope": "rank 0",
             "clocks": clk,
+            "stage_seconds_per_build": stage_table,
+            "graph": {"medoid": int(medoid), "digest": digest},
         }
         if e2e:
             line["e2e"] = e2e

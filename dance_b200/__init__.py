@@ -73,6 +73,15 @@ class DanceBuildReport(ctypes.Structure):
         ("reserved", ctypes.c_uint64 * 3)]
 
 
+class DanceShardedReport(ctypes.Structure):
+    """Mirror of ``DanceShardedReport`` in include/dance_b200.h."""
+    _fields_ = [(n, ctypes.c_double) for n in (
+        "medoid_init_seconds", "search_seconds", "replay_seconds", "edge_exchange_seconds", "reverse_seconds",
+        "prune_seconds", "graph_exchange_seconds", "total_seconds")] + [(n, ctypes.c_uint64) for n in (
+            "edge_bytes_sent", "edge_bytes_received", "graph_bytes_received", "rounds")] + [
+        ("reserved", ctypes.c_uint64 * 4)]
+
+
 class GPUFilteredVamanaStats(ctypes.Structure):
     """Mirror of ``GPUFilteredVamanaStats`` in include/gpu_vamana_filtered.h."""
     _fields_ = ([(n, ctypes.c_double) for n in (
@@ -161,6 +170,7 @@ SIGNATURES = {
     "dance_last_error": (ctypes.c_char_p, []),
     "dance_kernel_launch_count": (_U64, []),
     "dance_last_build_report": (_I, [_P]),
+    "dance_last_sharded_report": (_I, [_P]),
     "dance_workspace_create": (_I, [_U32, _U32, _U32, _U32, _U32, _P]),
     "dance_workspace_destroy": (None, [_P]),
     "dance_vamana_build_resident": (_I, [_I, _P, _U64, _U32, _U32, _U32, _U32, _U32, _U32, _P, _P, _P, _P, _P,
@@ -186,6 +196,10 @@ SIGNATURES = {
     "dance_stitched_label_graphs": (_I, [_I, _P, _U64, _U32, _U32, _U32, _P, _P, _P, _U32, _U32, _U32, _U32, _P,
                                          _U32, _P, _P, _P, _P]),
     "dance_stitched_remap": (_I, [_U32, _U32, _P, _P, _P, _P, _U32, _U32, _P, _P, _U64, _P, _P]),
+    "dance_calculate_entry_point": (_I, [_I, _P, _U64, _U32, _U32, _PU32, _P]),
+    "dance_select_label_starts": (_I, [_P, _P, _U32, _U32, _U32, _U64, _P, _P]),
+    "dance_stitched_global_prune": (_I, [_I, _P, _U64, _U32, _U32, _P, _P, _P, _P, _U32, _U32, _F, _P, _P, _P,
+                                         _P]),
     "dance_shard_range": (None, [_U32, _I, _I, _PU32, _PU32, _PU32]),
     "dance_nccl_unique_id": (_I, [_P, ctypes.c_size_t]),
     "dance_comm_create": (_I, [_I, _I, _P, ctypes.c_size_t, ctypes.c_double, _P]),
@@ -239,6 +253,12 @@ def check(rc: int, what: str = "libdance_b200") -> None:
 def last_build_report() -> dict:
     r = DanceBuildReport()
     check(load().dance_last_build_report(ctypes.byref(r)), "dance_last_build_report")
+    return {n: getattr(r, n) for n, _ in r._fields_ if n != "reserved"}
+
+
+def last_sharded_report() -> dict:
+    r = DanceShardedReport()
+    check(load().dance_last_sharded_report(ctypes.byref(r)), "dance_last_sharded_report")
     return {n: getattr(r, n) for n, _ in r._fields_ if n != "reserved"}
 
 

@@ -13,6 +13,7 @@ import os
 import shutil
 import subprocess
 import sys
+import time
 from pathlib import Path
 
 PKG = Path(__file__).resolve().parent
@@ -20,9 +21,9 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libdance_b200.so"
 
-SOURCES = ["vamana_build.cu", "vamana_sharded.cu", "gpu_merge.cu", "stitched.cu", "filtered.cu"]
+SOURCES = ["vamana_build.cu", "vamana_sharded.cu", "gpu_merge.cu", "stitched.cu", "filtered.cu", "label_starts.cu"]
 HEADERS = ["dance_common.cuh", "vamana_kernels.cuh", "host_common.cuh", "filtered_kernels.cuh",
-           "gram_u8.cuh", "prune_quad.cuh"]
+           "gram_u8.cuh", "prune_quad.cuh", "stitched_prune.cuh"]
 PUBLIC_HEADERS = ["dance_b200.h", "gpu_vamana_builder.h", "gpu_vamana_config.h", "gpu_merge.h",
                   "gpu_vamana_filtered.h"]
 
@@ -56,6 +57,7 @@ def up_to_date() -> bool:
 def build(force: bool = False, ptxas_v: bool = False, verbose: bool = False) -> Path:
     if not force and up_to_date():
         return LIB
+    started = time.time()
     cmd = [nvcc(), *host_compiler(), *ARCH, "-O3", "-std=c++17", "-lineinfo",
            "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
            "--expt-relaxed-constexpr", "-shared",
@@ -76,6 +78,9 @@ def build(force: bool = False, ptxas_v: bool = False, verbose: bool = False) -> 
     if ptxas_v or verbose:
         sys.stderr.write(res.stderr)
     os.replace(str(LIB) + ".tmp", LIB)
+    # stamp the library with the time the compile started, so a source edited
+    # while nvcc ran leaves it stale
+    os.utime(LIB, (started, started))
     return LIB
 
 

@@ -34,6 +34,7 @@
 
 #include "../../include/dance_b200.h"
 #include "host_common.cuh"
+#include "stitched_prune.cuh"
 
 namespace dance
 {
@@ -547,6 +548,56 @@ int dance_stitched_remap(uint32_t N, uint32_t num_labels, const uint64_t *label_
     if (!rc && stats)
         stats->local_to_global_remap_seconds = wall() - t0;
     return rc;
+}
+
+int dance_stitched_global_prune(int dtype, const void *d_data, uint64_t stride, uint32_t N, uint32_t dim,
+                                const uint64_t *d_row_offsets, const uint32_t *d_row_ids,
+                                const uint32_t *d_point_label_offsets, const uint32_t *d_point_labels,
+                                uint32_t range, uint32_t max_candidates, float alpha, uint32_t *d_out_rows,
+                                uint32_t *d_out_degree, uint64_t *pruned_rows_out, void *stream)
+{
+    int rc = check_store(dtype, d_data, stride, N, dim);
+    if (rc)
+        return rc;
+    if (!d_row_offsets || !d_row_ids || !d_out_rows || !d_out_degree || range == 0 || max_candidates == 0 ||
+        !(alpha >= 1.0f) || (!d_point_label_offsets) != (!d_point_labels))
+        return fail(-1, "[GPU stitched prune] invalid arguments");
+    cudaStream_t s = as_stream(stream);
+    DevBuf scratch;
+    DANCE_CUDA(scratch.ensure(16));
+    uint32_t *d_max = scratch.as<uint32_t>();
+    unsigned long long *d_pruned = reinterpret_cast<unsigned long long *>(scratch.as<uint8_t>() + 8);
+    DANCE_CUDA(cudaMemsetAsync(scratch.p, 0, 16, s));
+    csr_max_degree_kernel<<<std::max<int>(1, std::min<int>((int)((N + 255) / 256), sm_count() * 8)), 256, 0, s>>>(
+        d_row_offsets, N, d_max);
+    DANCE_LAUNCHED();
+    uint32_t maxdeg = 0;
+    DANCE_CUDA(cudaMemcpyAsync(&maxdeg, d_max, 4, cudaMemcpyDeviceToHost, s));
+    DANCE_CUDA(cudaStreamSynchronize(s));
+    if (maxdeg > kStitchedPruneMaxDegree)
+        return fail(-1, "[GPU stitched prune] a row has %u neighbours; this build prunes rows of at most %u", maxdeg,
+                    kStitchedPruneMaxDegree);
+    StitchedPruneParams pp{};
+    pp.st = make_view(d_data, stride, N, dim, dtype);
+    pp.row_off = d_row_offsets;
+    pp.row_ids = d_row_ids;
+    pp.lab_off = d_point_label_offsets;
+    pp.labs = d_point_labels;
+    pp.range = range;
+    pp.maxc = max_candidates;
+    pp.pcap = (uint32_t)std::max(32, next_pow2((int)std::max(maxdeg, 1u)));
+    pp.alpha = alpha;
+    pp.out_rows = d_out_rows;
+    pp.out_deg = d_out_degree;
+    pp.pruned_rows = d_pruned;
+    if ((rc = dispatch<LaunchStitchedPrune>(dtype, pp.st.nchunks, pp, s)))
+        return rc;
+    if (pruned_rows_out)
+    {
+        DANCE_CUDA(cudaMemcpyAsync(pruned_rows_out, d_pruned, 8, cudaMemcpyDeviceToHost, s));
+        DANCE_CUDA(cudaStreamSynchronize(s));
+    }
+    return 0;
 }
 
 int dance_stitched_build(int dtype, const void *h_data, uint32_t N, uint32_t dim, uint32_t num_labels,

@@ -106,6 +106,58 @@ static Clock::time_point deadline_of(const DanceComm *c)
     return Clock::now() + std::chrono::duration_cast<Clock::duration>(std::chrono::duration<double>(c->timeout_s));
 }
 
+// Events recorded on the build stream at stage boundaries; the time between
+// consecutive marks is charged to the stage of the later mark.
+enum ShardStage
+{
+    kStMedoidInit = 0,
+    kStSearch,
+    kStReplay,
+    kStEdgeExchange,
+    kStReverse,
+    kStPrune,
+    kStGraphExchange,
+    kStCount
+};
+
+struct StageClock
+{
+    std::vector<cudaEvent_t> ev;
+    std::vector<int> stage;
+    ~StageClock()
+    {
+        for (auto e : ev)
+            cudaEventDestroy(e);
+    }
+    int mark(int st, cudaStream_t s)
+    {
+        cudaEvent_t e = nullptr;
+        DANCE_CUDA(cudaEventCreate(&e));
+        ev.push_back(e);
+        stage.push_back(st);
+        DANCE_CUDA(cudaEventRecord(e, s));
+        return 0;
+    }
+    void sum(double *acc) const // acc[kStCount], seconds
+    {
+        for (size_t i = 1; i < ev.size(); ++i)
+        {
+            float ms = 0;
+            if (cudaEventElapsedTime(&ms, ev[i - 1], ev[i]) == cudaSuccess)
+                acc[stage[i]] += ms * 1e-3;
+        }
+    }
+    double total() const
+    {
+        float ms = 0;
+        if (ev.size() >= 2 && cudaEventElapsedTime(&ms, ev.front(), ev.back()) == cudaSuccess)
+            return ms * 1e-3;
+        return 0;
+    }
+};
+
+thread_local DanceShardedReport g_sharded_report;
+
 // In-place all-gather of rows [rank*chunk, (rank+1)*chunk) of a table with
 // `width` uint32 per row.
 static int allgather_rows(DanceComm *c, uint32_t *table, uint64_t chunk, uint64_t width, cudaStream_t s)
@@ -247,21 +299,11 @@ DANCE_API int dance_vamana_build_sharded(DanceComm *comm, int dtype, const void 
     uint32_t *tdeg = d_table_degree; // world * chunk: degrees of the gathered edge table
     float *cur_dists = ws->cur_dists.as<float>(); // own rows only
     DANCE_CUDA(cudaMemsetAsync(ws->counters.p, 0, 64, s));
-    // events: build start/end and search-kernel start/end of every round
-    std::vector<cudaEvent_t> ev(2 + 2 * (size_t)prm.iters, nullptr);
-    struct EvGuard
-    {
-        std::vector<cudaEvent_t> &e;
-        ~EvGuard()
-        {
-            for (auto x : e)
-                if (x)
-                    cudaEventDestroy(x);
-        }
-    } guard{ev};
-    for (auto &e : ev)
-        DANCE_CUDA(cudaEventCreate(&e));
-    DANCE_CUDA(cudaEventRecord(ev[0], s));
+    StageClock clk;
+    uint64_t edge_sent = 0, edge_recv = 0, graph_recv = 0;
+    const uint64_t peer_rows = (uint64_t)chunk * (uint64_t)(comm->world - 1);
+    if ((rc = clk.mark(kStMedoidInit, s)))
+        return rc;
 
     // medoid: every rank computes the same entry point
     const uint32_t nc = std::min<uint32_t>(prm.medoid_candidates, std::min<uint32_t>(N, 4096u));
@@ -283,6 +325,9 @@ DANCE_API int dance_vamana_build_sharded(DanceComm *comm, int dtype, const void 
             return rc;
     }
     if ((rc = allgather_rows(comm, cur_ids, chunk, R, s)) || (rc = allgather_rows(comm, degree, chunk, 1, s)))
+        return rc;
+    graph_recv += peer_rows * (R + 1) * 4;
+    if ((rc = clk.mark(kStMedoidInit, s)))
         return rc;
 
     for (uint32_t it = 0; it < prm.iters; ++it)
@@ -311,10 +356,10 @@ DANCE_API int dance_vamana_build_sharded(DanceComm *comm, int dtype, const void 
             sp.v1 = v1;
             sp.lrow0 = v0;
             sp.counters = ws->counters.as<unsigned long long>();
-            DANCE_CUDA(cudaEventRecord(ev[2 + 2 * it], s));
             if ((rc = dispatch<LaunchSearch>(dtype, st.nchunks, sp, s)))
                 return rc;
-            DANCE_CUDA(cudaEventRecord(ev[3 + 2 * it], s));
+            if ((rc = clk.mark(kStSearch, s)))
+                return rc;
             ReplayParams rp{};
             rp.st = st;
             rp.R = R;
@@ -344,13 +389,21 @@ DANCE_API int dance_vamana_build_sharded(DanceComm *comm, int dtype, const void 
             pack_work_rows_kernel<<<grid, 256, 0, s>>>(rp.work_ids, rp.work_deg, C, R, v0, v1, cur_ids, tdeg);
             DANCE_LAUNCHED();
         }
+        if ((rc = clk.mark(kStReplay, s)))
+            return rc;
         if ((rc = allgather_rows(comm, cur_ids, chunk, R, s)) || (rc = allgather_rows(comm, tdeg, chunk, 1, s)))
+            return rc;
+        edge_sent += (uint64_t)chunk * (R + 1) * 4 * (uint64_t)(comm->world - 1);
+        edge_recv += peer_rows * (R + 1) * 4;
+        if ((rc = clk.mark(kStEdgeExchange, s)))
             return rc;
         if (nloc)
         {
             rc = reverse_merge_impl(dtype, st, R, C, prm, *ws, cur_ids, R, tdeg, 0, N, ws->work_ids.as<uint32_t>(),
                                     ws->work_dists.as<float>(), ws->work_deg.as<uint32_t>(), v0, v1, s);
             if (rc)
+                return rc;
+            if ((rc = clk.mark(kStReverse, s)))
                 return rc;
             PruneParams pp{};
             pp.st = st;
@@ -372,27 +425,47 @@ DANCE_API int dance_vamana_build_sharded(DanceComm *comm, int dtype, const void 
             if ((rc = dispatch<LaunchPrune>(dtype, st.nchunks, pp, s)))
                 return rc;
         }
+        if ((rc = clk.mark(kStPrune, s)))
+            return rc;
         if ((rc = allgather_rows(comm, cur_ids, chunk, R, s)) || (rc = allgather_rows(comm, degree, chunk, 1, s)))
+            return rc;
+        graph_recv += peer_rows * (R + 1) * 4;
+        if ((rc = clk.mark(kStGraphExchange, s)))
             return rc;
         if ((rc = stream_wait(comm, s, deadline_of(comm))))
             return rc;
     }
     if (medoid_out)
         DANCE_CUDA(cudaMemcpyAsync(medoid_out, d_medoid, 4, cudaMemcpyDeviceToHost, s));
-    DANCE_CUDA(cudaEventRecord(ev[1], s));
+    if ((rc = clk.mark(kStGraphExchange, s)))
+        return rc;
     if ((rc = stream_wait(comm, s, deadline_of(comm))))
         return rc;
+    double acc[kStCount] = {0};
+    clk.sum(acc);
+    DanceShardedReport &sr = g_sharded_report;
+    std::memset(&sr, 0, sizeof(sr));
+    sr.medoid_init_seconds = acc[kStMedoidInit];
+    sr.search_seconds = acc[kStSearch];
+    sr.replay_seconds = acc[kStReplay];
+    sr.edge_exchange_seconds = acc[kStEdgeExchange];
+    sr.reverse_seconds = acc[kStReverse];
+    sr.prune_seconds = acc[kStPrune];
+    sr.graph_exchange_seconds = acc[kStGraphExchange];
+    sr.total_seconds = clk.total();
+    sr.edge_bytes_sent = edge_sent;
+    sr.edge_bytes_received = edge_recv;
+    sr.graph_bytes_received = graph_recv;
+    sr.rounds = prm.iters;
     DanceBuildReport &r = g_report;
     std::memset(&r, 0, sizeof(r));
-    float a = 0;
-    cudaEventElapsedTime(&a, ev[0], ev[1]);
-    r.total_seconds = a * 1e-3;
-    if (nloc)
-        for (uint32_t it = 0; it < prm.iters; ++it)
-        {
-            cudaEventElapsedTime(&a, ev[2 + 2 * it], ev[3 + 2 * it]);
-            r.search_kernel_seconds += a * 1e-3;
-        }
+    r.total_seconds = sr.total_seconds;
+    r.medoid_seconds = sr.medoid_init_seconds;
+    r.search_kernel_seconds = sr.search_seconds;
+    r.search_seconds = sr.search_seconds + sr.replay_seconds;
+    r.replay_seconds = sr.replay_seconds;
+    r.reverse_seconds = sr.edge_exchange_seconds + sr.reverse_seconds;
+    r.prune_seconds = sr.prune_seconds + sr.graph_exchange_seconds;
     uint64_t ctr[8] = {0};
     DANCE_CUDA(cudaMemcpy(ctr, ws->counters.p, 64, cudaMemcpyDeviceToHost));
     r.search_evals = ctr[0];
@@ -400,6 +473,14 @@ DANCE_API int dance_vamana_build_sharded(DanceComm *comm, int dtype, const void 
     r.replay_pairs = ctr[2];
     r.reverse_evals = ctr[3];
     r.prune_pairs = ctr[4];
+    return 0;
+}
+
+DANCE_API int dance_last_sharded_report(DanceShardedReport *report)
+{
+    if (!report)
+        return fail(-1, "null report");
+    *report = g_sharded_report;
     return 0;
 }
 

@@ -90,3 +90,52 @@ def build_resident(store, dim: int, stride: int, R: int, L: int, filtered_L: int
                                            _d(degree), ctypes.byref(st), s)
     check(rc, "dance_filtered_build_resident")
     return graph, degree, st.as_dict()
+
+
+def label_points_csr(point_label_offsets, point_labels, num_labels: int, universal_label_id: int = INVALID):
+    """Per-label point lists (offsets u32[num_labels+1], points ascending) from
+    the per-point label CSR; a point carrying the universal label is listed
+    under every label, as DiskANN's label_to_points is built."""
+    offs = np.asarray(point_label_offsets, np.int64)
+    labs = np.asarray(point_labels, np.int64)
+    n = len(offs) - 1
+    pnt = np.repeat(np.arange(n, dtype=np.int64), np.diff(offs))
+    keep = (labs != universal_label_id) & (labs < num_labels)
+    pairs = [labs[keep] * (n + 1) + pnt[keep]]
+    keep = labs != universal_label_id
+    if universal_label_id != INVALID:
+        upts = np.unique(pnt[~keep])
+        if len(upts):
+            pairs.append((np.arange(num_labels, dtype=np.int64)[:, None] * (n + 1) + upts[None, :]).ravel())
+    key = np.unique(np.concatenate(pairs)) if pairs else np.zeros(0, np.int64)
+    lab_of, pt_of = key // (n + 1), key % (n + 1)
+    loff = np.zeros(num_labels + 1, np.uint32)
+    loff[1:] = np.cumsum(np.bincount(lab_of, minlength=num_labels)[:num_labels])
+    return loff, pt_of.astype(np.uint32)
+
+
+def calculate_entry_point(store, dim: int, stride: int) -> int:
+    """DiskANN's calculate_entry_point on a padded CUDA store
+    (``dance_calculate_entry_point``)."""
+    import torch
+    from .vamana import dtype_code
+    out = ctypes.c_uint32(0)
+    rc = load().dance_calculate_entry_point(dtype_code(store), _d(store), stride, store.shape[0], dim,
+                                            ctypes.byref(out), None)
+    check(rc, "dance_calculate_entry_point")
+    return int(out.value)
+
+
+def select_label_starts(label_offsets, label_points, num_points: int, num_candidates: int = 25,
+                        seed: int = 42) -> np.ndarray:
+    """One start point per label (``dance_select_label_starts``; DiskANN's
+    least-chosen-of-25 rule with hashed draws).  Inputs from label_points_csr."""
+    import torch
+    loff = torch.from_numpy(np.ascontiguousarray(label_offsets, np.uint32).view(np.int32)).cuda()
+    pts = np.ascontiguousarray(label_points, np.uint32)
+    dpts = torch.from_numpy((pts if len(pts) else np.zeros(1, np.uint32)).view(np.int32)).cuda()
+    nl = len(label_offsets) - 1
+    starts = torch.empty(max(nl, 1), dtype=torch.int32, device="cuda")
+    rc = load().dance_select_label_starts(_d(loff), _d(dpts), nl, num_points, num_candidates, seed, _d(starts), None)
+    check(rc, "dance_select_label_starts")
+    return starts[:nl].cpu().numpy().view(np.uint32).copy()

@@ -9,10 +9,12 @@ flags (:43-63).  ``python -m dance_b200.stitched --help`` runs it as a CLI.
 
 The reference finishes multi-label inputs (and Rsmall > Rstitched, which its
 argument parser already rules out) with DiskANN's CPU label-aware prune
-(:353-372).  That prune belongs to DiskANN, which is not part of this
-library, so ``build_gpu_stitched`` refuses such inputs unless
-``allow_unpruned`` is set, in which case it writes the union graph (what the
-reference saves as ``<prefix>_full`` before pruning).
+(:353-372: ``Index::prune_all_neighbors(Rstitched, 750, alpha)`` with the
+DANCE patch's coverage rule and label-balanced shortlist).  Here that prune
+runs on the GPU (``global_prune``, ``dance_stitched_global_prune``): the
+union graph is kept as ``<prefix>_full``, as the reference keeps it, and the
+pruned graph is the index.  ``allow_unpruned`` writes the union graph as the
+index instead.
 """
 from __future__ import annotations
 
@@ -134,6 +136,57 @@ def stitched_build(data: np.ndarray, label_offsets: np.ndarray, label_points: np
     check(rc, "dance_stitched_build")
     E = int(row_offsets[-1])
     return row_offsets, row_ids[:E].copy(), medoids[:nl].copy(), st.as_dict()
+
+
+def point_label_csr(label_points, n: int):
+    """Per-point label CSR (offsets u32[n+1], labels u32 ascending per point)
+    from per-label point lists; label l of the lists is label id l."""
+    pts = [np.asarray(p, dtype=np.int64) for p in label_points]
+    if not pts or sum(len(p) for p in pts) == 0:
+        return np.zeros(n + 1, np.uint32), np.zeros(0, np.uint32)
+    pp = np.concatenate(pts)
+    ll = np.concatenate([np.full(len(p), l, np.int64) for l, p in enumerate(pts)])
+    pairs = np.unique(pp * (len(pts) + 1) + ll)
+    pp, ll = pairs // (len(pts) + 1), pairs % (len(pts) + 1)
+    offs = np.zeros(n + 1, np.uint32)
+    offs[1:] = np.cumsum(np.bincount(pp, minlength=n))
+    return offs, ll.astype(np.uint32)
+
+
+def global_prune(data: np.ndarray, row_offsets: np.ndarray, row_ids: np.ndarray, point_label_offsets, point_labels,
+                 r_stitched: int, max_candidates: int = 750, alpha: float = 1.2):
+    """Label-aware global prune of a stitched union graph on the GPU
+    (``dance_stitched_global_prune``; DiskANN's patched prune_all_neighbors).
+    Returns (row_offsets u64[N+1], row_ids u32[E], rows pruned)."""
+    import torch
+    from .vamana import dtype_code, padded_store
+    lib = load()
+    data = np.ascontiguousarray(data)
+    n, dim = data.shape
+    x = torch.from_numpy(data).cuda()
+    store, stride = padded_store(x)
+    ro = torch.from_numpy(np.ascontiguousarray(row_offsets, np.uint64).view(np.int64)).cuda()
+    ri = torch.from_numpy(np.ascontiguousarray(row_ids, np.uint32).view(np.int32)).cuda()
+    if point_label_offsets is not None:
+        lo = torch.from_numpy(np.ascontiguousarray(point_label_offsets, np.uint32).view(np.int32)).cuda()
+        lb = torch.from_numpy(np.ascontiguousarray(point_labels, np.uint32).view(np.int32)).cuda()
+        lo_p, lb_p = ctypes.c_void_p(lo.data_ptr()), ctypes.c_void_p(lb.data_ptr() if lb.numel() else lo.data_ptr())
+    else:
+        lo_p = lb_p = None
+    out = torch.empty((n, r_stitched), dtype=torch.int32, device="cuda")
+    deg = torch.empty((n,), dtype=torch.int32, device="cuda")
+    pruned = ctypes.c_uint64(0)
+    rc = lib.dance_stitched_global_prune(dtype_code(x), ctypes.c_void_p(store.data_ptr()), stride, n, dim,
+                                         ctypes.c_void_p(ro.data_ptr()), ctypes.c_void_p(ri.data_ptr()), lo_p, lb_p,
+                                         r_stitched, max_candidates, alpha, ctypes.c_void_p(out.data_ptr()),
+                                         ctypes.c_void_p(deg.data_ptr()), ctypes.byref(pruned), None)
+    check(rc, "dance_stitched_global_prune")
+    rows = out.cpu().numpy().view(np.uint32)
+    d = deg.cpu().numpy().view(np.uint32).astype(np.int64)
+    offs = np.zeros(n + 1, np.uint64)
+    offs[1:] = np.cumsum(d)
+    ids = rows[np.arange(r_stitched)[None, :] < d[:, None]]
+    return offs, ids.astype(np.uint32), int(pruned.value)
 
 
 def lpt_assignment(label_offsets: np.ndarray, world: int) -> np.ndarray:
@@ -354,14 +407,22 @@ def build_gpu_stitched(data_type: str, data_path, label_file, index_path_prefix,
     if len(names) != data.shape[0]:
         raise ValueError("number of label rows does not match data points")
     single = all(len(r) == 1 for r in names)
-    if not (single and Rsmall <= Rstitched) and not allow_unpruned:
-        raise DanceError("multi-label rows need DiskANN's CPU label-aware prune, which this library does not "
-                         "include; pass allow_unpruned to write the union graph")
+    needs_prune = not (single and Rsmall <= Rstitched)
     offs, pts = labels_csr(label_points)
     print(f"[GPU stitched] enabled labels={len(id_to_label)} N={data.shape[0]} dim={data.shape[1]} "
           f"Rsmall={Rsmall} Lsmall={Lsmall} Rstitched={Rstitched} C={C}")
     row_offsets, row_ids, medoids, st = stitched_build(data, offs, pts, Rsmall, Lsmall, Rstitched, C, steps,
                                                        streams=streams)
+    prune_seconds = 0.0
+    if needs_prune and not allow_unpruned:
+        # the union graph is kept as <prefix>_full (:360), the pruned graph is the index
+        full = Path(str(index_path_prefix) + "_full")
+        _publish(full, encode_csr_graph(row_offsets, row_ids, 0))
+        pt0 = time.perf_counter()
+        lo, lb = point_label_csr(label_points, data.shape[0])
+        row_offsets, row_ids, pruned = global_prune(data, row_offsets, row_ids, lo, lb, Rstitched, 750, alpha)
+        prune_seconds = time.perf_counter() - pt0
+        print(f"[GPU stitched] global label-aware prune on the GPU: rows_pruned={pruned} seconds={prune_seconds}")
     io = write_stitched_index(index_path_prefix, data_path, row_offsets, row_ids, names, label_to_id, id_to_label,
                               medoids)
     deg = np.diff(row_offsets.astype(np.int64))
@@ -370,7 +431,7 @@ def build_gpu_stitched(data_type: str, data_path, label_file, index_path_prefix,
           f"max_degree={int(deg.max()) if len(deg) else 0}")
     timing = {k: st.get(k, 0) for k in TIMING_KEYS}
     timing.update(io)
-    timing["final_prune_seconds"] = 0.0
+    timing["final_prune_seconds"] = prune_seconds
     timing["total_seconds"] = time.perf_counter() - t0
     timing["label_build_wall_seconds"] = st["label_build_wall_seconds"]
     timing["streams"] = st["streams"]

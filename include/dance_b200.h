@@ -159,6 +159,19 @@ DANCE_API int dance_vamana_build_sharded(DanceComm *comm, int dtype, const void 
                                          uint32_t *d_graph, uint32_t *d_degree, uint32_t *d_table_degree,
                                          uint32_t *medoid_out, void *stream);
 
+/* Device time of this rank's last sharded build per stage, summed over the
+ * rounds (CUDA events on the build stream): the exchange stages include the
+ * time spent waiting for the slowest rank.  Bytes are this rank's own
+ * traffic over the build. */
+typedef struct DanceShardedReport
+{
+    double medoid_init_seconds, search_seconds, replay_seconds, edge_exchange_seconds, reverse_seconds,
+        prune_seconds, graph_exchange_seconds, total_seconds;
+    uint64_t edge_bytes_sent, edge_bytes_received, graph_bytes_received, rounds;
+    uint64_t reserved[4];
+} DanceShardedReport;
+DANCE_API int dance_last_sharded_report(DanceShardedReport *report);
+
 /* ---- shard merge (C form of diskann::merge_shards_gpu, include/gpu_merge.h) */
 DANCE_API int dance_merge_shards_gpu(const char *vamana_prefix, const char *vamana_suffix, const char *idmaps_prefix,
                                      const char *idmaps_suffix, uint64_t nshards, uint32_t max_degree,
@@ -263,6 +276,44 @@ DANCE_API int dance_stitched_remap(uint32_t num_points, uint32_t num_labels, con
                                    const uint32_t *d_local_degree, uint32_t r_small, uint32_t r_stitched,
                                    uint64_t *row_offsets, uint32_t *row_ids, uint64_t row_ids_capacity,
                                    DanceStitchedStats *stats, void *stream);
+/* Label-aware global prune of a stitched union graph: the DiskANN CPU step
+ * (Index::prune_all_neighbors(Rstitched, 750, alpha) as patched by DANCE)
+ * that the reference app runs when rows carry several labels or Rsmall >
+ * Rstitched (apps/utils/gpu_stitched_vamana_index.cpp:353-372; coverage rule
+ * integration patch lines 20009-20047, label-balanced shortlist 20055-20100).
+ * Device inputs: the union graph as a CSR (d_row_offsets N+1, d_row_ids) and
+ * the points' labels as a CSR with ascending labels per point (both label
+ * pointers NULL = unlabelled: plain occlusion).  Rows with at most `range`
+ * neighbours are copied; longer rows are pruned to at most `range`.
+ * Output: d_out_rows (N x range, 0xFFFFFFFF padded) and d_out_degree.
+ * Rows longer than 2048 neighbours are refused (-1).  Synchronises stream
+ * (it reads the longest row's length back to size the per-warp pools). */
+DANCE_API int dance_stitched_global_prune(int dtype, const void *d_data, uint64_t row_stride_bytes,
+                                          uint32_t num_points, uint32_t dim, const uint64_t *d_row_offsets,
+                                          const uint32_t *d_row_ids, const uint32_t *d_point_label_offsets,
+                                          const uint32_t *d_point_labels, uint32_t range,
+                                          uint32_t max_candidates, float alpha, uint32_t *d_out_rows,
+                                          uint32_t *d_out_degree, uint64_t *pruned_rows_out, void *stream);
+
+/* ---- inputs DiskANN computes before the filtered build hook --------------- */
+/* Index entry point (DiskANN Index::calculate_entry_point, called by the
+ * filtered hook at integration patch line 20267): the centroid of all points
+ * (float, summed point by point in point order, divided by N), then the
+ * point nearest to it by squared L2 (dimensions summed in order, no fused
+ * multiply-add; lowest index on ties).  Synchronises stream. */
+DANCE_API int dance_calculate_entry_point(int dtype, const void *d_data, uint64_t row_stride_bytes,
+                                          uint32_t num_points, uint32_t dim, uint32_t *entry_out, void *stream);
+/* One start point per label (DiskANN's _label_to_start_id, computed before
+ * the hook, patch lines 20238-20241): labels in ascending id order; each
+ * draws num_candidates of its points (DiskANN uses 25) and takes the one
+ * chosen as a start the fewest times so far (first draw on ties).  Draw k of
+ * label l is point hash(seed, l, k) mod |points of l| (DiskANN uses rand()).
+ * d_label_offsets (num_labels + 1) / d_label_points: each label's points in
+ * ascending order, universal-label points included in every label.  Empty
+ * labels get 0xFFFFFFFF.  Synchronises stream. */
+DANCE_API int dance_select_label_starts(const uint32_t *d_label_offsets, const uint32_t *d_label_points,
+                                        uint32_t num_labels, uint32_t num_points, uint32_t num_candidates,
+                                        uint64_t seed, uint32_t *d_starts, void *stream);
 
 /* ---- GPU-FilteredVamana on resident vectors ------------------------------- */
 /* The canonical filtered build of gpu_vamana_filtered.h on a padded store

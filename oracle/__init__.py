@@ -52,6 +52,9 @@ _SIGS = {
                                          _P, _P, _P, _I]),
     "oracle_filtered_ordinary_search": (_I, [_I, _P, _U64, _U32, _U32, _U32, _U32, _U32, _U32, _P, _P, _P, _U32,
                                              _U32, _U32, _P, _P, _P, _P, _I]),
+    "oracle_entry_point": (_U32, [_I, _P, _U64, _U32, _U32]),
+    "oracle_label_starts": (None, [_P, _P, _U32, _U32, _U32, _U64, _P]),
+    "oracle_stitched_global_prune": (_I, [_I, _P, _U64, _U32, _U32, _P, _P, _P, _P, _U32, _U32, _F, _P, _P]),
     "oracle_filtered_prune_lists": (_I, [_I, _P, _U64, _U32, _U32, _U32, _F, _P, _P, _U32, _P, _U32, _P, _P, _P,
                                          _P, _P]),
 }
@@ -299,6 +302,40 @@ def stitched(data, label_points, r_small, l_small, r_out, C, steps, prm=None):
         medoids.append(ids[med] if med < len(ids) else ids[0])
         stitched_remap(rows, ids, g, deg, r_small, r_out, counters)
     return rows, medoids, counters
+
+
+def entry_point(data) -> int:
+    """DiskANN's calculate_entry_point as label_starts.cu restates it."""
+    d, stride, dt = _store(data)
+    n, dim = data.shape
+    return int(load().oracle_entry_point(dt, _p(d), stride, n, dim))
+
+
+def label_starts(label_offsets, label_points, num_points, num_candidates=25, seed=42):
+    off = np.ascontiguousarray(label_offsets, np.uint32)
+    pts = np.ascontiguousarray(label_points, np.uint32)
+    out = np.zeros(max(len(off) - 1, 1), np.uint32)
+    load().oracle_label_starts(_p(off), _p(pts), len(off) - 1, num_points, num_candidates, seed, _p(out))
+    return out[:len(off) - 1]
+
+
+def stitched_global_prune(data, row_offsets, row_ids, point_label_offsets, point_labels, range_, maxc=750,
+                          alpha=1.2):
+    """DiskANN's patched prune_all_neighbors over a union CSR graph (see the C
+    restatement); labels as a per-point CSR with ascending labels, or None.
+    Returns (rows N x range with 0xFFFFFFFF padding, degrees)."""
+    d, stride, dt = _store(data)
+    n, dim = data.shape
+    ro = np.ascontiguousarray(row_offsets, np.uint64)
+    ri = np.ascontiguousarray(row_ids, np.uint32)
+    lo = None if point_label_offsets is None else np.ascontiguousarray(point_label_offsets, np.uint32)
+    lb = None if point_labels is None else np.ascontiguousarray(point_labels, np.uint32)
+    out = np.zeros((n, range_), np.uint32)
+    deg = np.zeros(n, np.uint32)
+    rc = load().oracle_stitched_global_prune(dt, _p(d), stride, n, dim, _p(ro), _p(ri), _p(lo), _p(lb), range_, maxc,
+                                             np.float32(alpha), _p(out), _p(deg))
+    assert rc == 0, rc
+    return out, deg
 
 
 # ---------------------------------------------------------------- GPU-FilteredVamana

@@ -2006,3 +2006,217 @@ int oracle_filtered_prune_lists(int dtype, const void *data, uint64_t stride, ui
 }
 
 } // extern "C"
+
+// ====================================================================== stitched global prune
+// DiskANN's Index::prune_all_neighbors(range, maxc, alpha) as the DANCE
+// integration patch changes it, which the reference stitched app runs on
+// multi-label union graphs (apps/utils/gpu_stitched_vamana_index.cpp:353-372):
+// rows longer than `range` are pruned; pool = distinct neighbours other than
+// the row with d(row, x), sorted by (distance, id); for a labelled row whose
+// pool exceeds `range`, the label-balanced shortlist of patch lines
+// 20055-20100 (per row label its first max(1, range / #labels) carriers, then
+// pool order up to `range`), which the following prune re-sorts; then
+// occlude_list: truncate to maxc, occlusion factors from 0, passes
+// a = 1, 1.2, ... <= alpha selecting entries with factor <= a, each selection
+// s raising every later entry x with factor <= alpha to
+// max(factor, d(row,x) / d(s,x)) (FLT_MAX when d(s,x) = 0) when s covers the
+// labels row and x share (patch lines 20009-20047).  DiskANN itself is not
+// available here, so this restatement is pinned only by hand cases.
+namespace
+{
+bool has_label(const uint32_t *off, const uint32_t *lab, uint32_t p, uint32_t l)
+{
+    return std::binary_search(lab + off[p], lab + off[p + 1], l);
+}
+
+bool covers(const uint32_t *off, const uint32_t *lab, uint32_t t, uint32_t s, uint32_t x)
+{
+    uint32_t i = off[t], ie = off[t + 1], j = off[x], je = off[x + 1];
+    while (i < ie && j < je)
+    {
+        if (lab[i] < lab[j])
+            ++i;
+        else if (lab[j] < lab[i])
+            ++j;
+        else
+        {
+            if (!has_label(off, lab, s, lab[i]))
+                return false;
+            ++i;
+            ++j;
+        }
+    }
+    return true;
+}
+} // namespace
+
+extern "C" int oracle_stitched_global_prune(int dtype, const void *data, uint64_t stride, uint32_t N, uint32_t dim,
+                                            const uint64_t *row_off, const uint32_t *row_ids, const uint32_t *lab_off,
+                                            const uint32_t *labs, uint32_t range, uint32_t maxc, float alpha,
+                                            uint32_t *out_rows, uint32_t *out_deg)
+{
+    const Store st = make_store(dtype, data, stride, dim);
+#pragma omp parallel for schedule(dynamic, 64)
+    for (int64_t vv = 0; vv < (int64_t)N; ++vv)
+    {
+        const uint32_t v = (uint32_t)vv;
+        const uint32_t deg = (uint32_t)(row_off[v + 1] - row_off[v]);
+        const uint32_t *row = row_ids + row_off[v];
+        uint32_t *out = out_rows + (uint64_t)v * range;
+        for (uint32_t i = 0; i < range; ++i)
+            out[i] = kInvalid;
+        if (deg <= range)
+        {
+            std::copy(row, row + deg, out);
+            out_deg[v] = deg;
+            continue;
+        }
+        std::vector<uint64_t> pool;
+        for (uint32_t i = 0; i < deg; ++i)
+            if (row[i] < N && row[i] != v)
+                pool.push_back(make_key(dist(st, v, row[i]), row[i]));
+        std::sort(pool.begin(), pool.end());
+        pool.erase(std::unique(pool.begin(), pool.end()), pool.end());
+        const uint32_t nlab = lab_off ? lab_off[v + 1] - lab_off[v] : 0;
+        if (nlab > 0 && pool.size() > range)
+        {
+            const uint32_t quota = std::max<uint32_t>(1, range / nlab);
+            std::vector<char> kept(pool.size(), 0);
+            for (uint32_t li = 0; li < nlab; ++li)
+            {
+                const uint32_t l = labs[lab_off[v] + li];
+                uint32_t admitted = 0;
+                for (size_t i = 0; i < pool.size() && admitted < quota; ++i)
+                    if (has_label(lab_off, labs, (uint32_t)pool[i], l))
+                    {
+                        kept[i] = 1;
+                        ++admitted;
+                    }
+            }
+            size_t nk = std::count(kept.begin(), kept.end(), 1);
+            for (size_t i = 0; i < pool.size() && nk < range; ++i)
+                if (!kept[i])
+                {
+                    kept[i] = 1;
+                    ++nk;
+                }
+            std::vector<uint64_t> shortlist;
+            for (size_t i = 0; i < pool.size(); ++i)
+                if (kept[i])
+                    shortlist.push_back(pool[i]); // already in (distance, id) order
+            pool.swap(shortlist);
+        }
+        if (pool.size() > maxc)
+            pool.resize(maxc);
+        std::vector<float> occ(pool.size(), 0.0f);
+        uint32_t nres = 0;
+        float cur = 1.0f;
+        while (cur <= alpha && nres < range)
+        {
+            for (size_t i = 0; i < pool.size() && nres < range; ++i)
+            {
+                if (occ[i] > cur)
+                    continue;
+                occ[i] = FLT_MAX;
+                const uint32_t s = (uint32_t)pool[i];
+                if (s != v)
+                    out[nres++] = s;
+                for (size_t j = i + 1; j < pool.size(); ++j)
+                {
+                    if (occ[j] > alpha)
+                        continue;
+                    const uint32_t x = (uint32_t)pool[j];
+                    if (lab_off && !covers(lab_off, labs, v, s, x))
+                        continue;
+                    const float djk = dist(st, s, x);
+                    float dj;
+                    const uint32_t bits = (uint32_t)(pool[j] >> 32);
+                    std::memcpy(&dj, &bits, 4);
+                    occ[j] = djk == 0.0f ? FLT_MAX : std::max(occ[j], dj / djk);
+                }
+            }
+            cur *= 1.2f;
+        }
+        out_deg[v] = nres;
+    }
+    return 0;
+}
+
+// ====================================================================== entry point, label starts
+// The inputs DiskANN computes before the filtered build hook (integration
+// patch lines 20238-20267), restated as dance_b200/csrc/label_starts.cu
+// defines them: centroid summed point by point in float, nearest point by
+// squared L2 summed over dimensions in order (lowest index on ties); per
+// label in ascending order, the least-chosen of num_cands hashed draws.
+namespace
+{
+float elem_of(const Store &st, uint32_t i, uint32_t j)
+{
+    const uint8_t *row = st.row(i);
+    switch (st.dtype)
+    {
+    case DANCE_U8:
+        return (float)row[j];
+    case DANCE_F16:
+        return half_to_float(reinterpret_cast<const uint16_t *>(row)[j]);
+    default:
+        return reinterpret_cast<const float *>(row)[j];
+    }
+}
+
+uint32_t start_draw(uint64_t seed, uint32_t label, uint32_t k)
+{
+    uint32_t h = hash_u32((uint32_t)seed ^ hash_u32(label * 0x9e3779b1u + 0x7f4a7c15u));
+    return hash_u32(h ^ (uint32_t)(seed >> 32) ^ (k * 0x85ebca6bu + 0x165667b1u));
+}
+} // namespace
+
+extern "C" uint32_t oracle_entry_point(int dtype, const void *data, uint64_t stride, uint32_t N, uint32_t dim)
+{
+    const Store st = make_store(dtype, data, stride, dim);
+    std::vector<float> c(dim, 0.0f);
+    for (uint32_t i = 0; i < N; ++i)
+        for (uint32_t j = 0; j < dim; ++j)
+            c[j] += elem_of(st, i, j);
+    for (uint32_t j = 0; j < dim; ++j)
+        c[j] /= (float)N;
+    uint64_t best = ~0ull;
+    for (uint32_t i = 0; i < N; ++i)
+    {
+        float d = 0.0f;
+        for (uint32_t j = 0; j < dim; ++j)
+        {
+            const float diff = c[j] - elem_of(st, i, j);
+            d += diff * diff;
+        }
+        best = std::min(best, make_key(d, i));
+    }
+    return (uint32_t)best;
+}
+
+extern "C" void oracle_label_starts(const uint32_t *off, const uint32_t *pts, uint32_t num_labels, uint32_t N,
+                                    uint32_t num_cands, uint64_t seed, uint32_t *starts)
+{
+    std::vector<uint32_t> counts(N, 0);
+    for (uint32_t l = 0; l < num_labels; ++l)
+    {
+        const uint32_t n = off[l + 1] - off[l];
+        if (n == 0)
+        {
+            starts[l] = kInvalid;
+            continue;
+        }
+        uint32_t best = kInvalid, best_count = 0;
+        for (uint32_t k = 0; k < num_cands; ++k)
+        {
+            const uint32_t p = pts[off[l] + start_draw(seed, l, k) % n];
+            if (best == kInvalid || counts[p] < best_count)
+            {
+                best = p;
+                best_count = counts[p];
+            }
+        }
+        starts[l] = best;
+        counts[best] += 1;
+    }
+}

@@ -308,3 +308,62 @@ def test_gpu_resident_build_with_given_graph_matches_oracle(dance_lib):
     torch.cuda.synchronize()
     og, od = oracle.filtered_build(x, lab, R, 32, 24, 40, 16, 1.2, graph=g0, degree=d0, rounds=2)
     assert rows_equal(go.cpu().numpy().view(np.uint32), do.cpu().numpy().view(np.uint32), og, od).all()
+
+
+# ---------------------------------------------------------------- inputs computed before the hook
+def test_label_points_csr_with_universal_label():
+    from dance_b200 import filtered as F
+    offs, labs = F.labels_csr([[0, 2], [1], [2, 5], [5], [0]])
+    lo, lp = F.label_points_csr(offs, labs, 3)
+    assert lo.tolist() == [0, 2, 3, 5] and lp.tolist() == [0, 4, 1, 0, 2]
+    lo, lp = F.label_points_csr(offs, labs, 3, universal_label_id=5)
+    assert lo.tolist() == [0, 4, 7, 10] and lp.tolist() == [0, 2, 3, 4, 1, 2, 3, 0, 2, 3]
+
+
+def test_oracle_entry_point_and_label_start_rules():
+    rng = np.random.default_rng(4)
+    x = rng.normal(size=(500, 12)).astype(np.float32)
+    c = np.zeros(12, np.float32)
+    for row in x:  # point by point, in float
+        c = (c + row).astype(np.float32)
+    c = (c / np.float32(500)).astype(np.float32)
+    assert oracle.entry_point(x) == int(np.argmin(((x.astype(np.float64) - c) ** 2).sum(1)))
+    # least-chosen rule: with one candidate point per label every start is that point
+    lo = np.array([0, 1, 2, 4], np.uint32)
+    lp = np.array([7, 7, 3, 9], np.uint32)
+    s = oracle.label_starts(lo, lp, 10, 25, 42)
+    assert s[0] == 7 and s[1] == 7 and s[2] in (3, 9)
+    # two labels over the same two points: the second label avoids the first's start
+    lo = np.array([0, 2, 4], np.uint32)
+    lp = np.array([1, 2, 1, 2], np.uint32)
+    s = oracle.label_starts(lo, lp, 3, 25, 42)
+    assert sorted(s.tolist()) == [1, 2]
+    assert oracle.label_starts(np.array([0, 0], np.uint32), np.zeros(0, np.uint32), 3)[0] == 0xFFFFFFFF
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", [np.uint8, np.float16, np.float32])
+def test_gpu_entry_point_matches_oracle(dance_lib, dtype):
+    import torch
+    from dance_b200 import filtered as F, vamana, workloads
+    if dtype == np.uint8:
+        x = workloads.clustered_u8(20000, 64, centroids=50, seed=8).numpy()
+    else:
+        x = workloads.gaussian_mixture_f32(20000, 96, centroids=50, seed=8).numpy().astype(dtype)
+    st, stride = vamana.padded_store(torch.from_numpy(x).cuda())
+    assert F.calculate_entry_point(st, x.shape[1], stride) == oracle.entry_point(x)
+
+
+@pytest.mark.gpu
+def test_gpu_label_starts_match_oracle(dance_lib):
+    from dance_b200 import filtered as F, workloads
+    n, vocab = 30000, 300
+    offs, labs = workloads.zipf_multilabels(n, vocab, seed=5)
+    lo, lp = F.label_points_csr(offs, labs, vocab + 2)  # two empty labels at the end
+    got = F.select_label_starts(lo, lp, n, 25, 42)
+    want = oracle.label_starts(lo, lp, n, 25, 42)
+    assert np.array_equal(got, want)
+    assert (got[-2:] == 0xFFFFFFFF).all() and (got[:vocab] < n).all()
+    # every start carries its label
+    for l in range(0, vocab, 17):
+        assert got[l] in set(lp[lo[l]:lo[l + 1]].tolist())

@@ -89,6 +89,65 @@ def _zipf_labels(n, nl, rng, min_size=1):
     return assign
 
 
+def _line_store(pos, dim=16):
+    x = np.zeros((len(pos), dim), np.uint8)
+    x[:, 0] = pos
+    return x
+
+
+def test_point_label_csr():
+    offs, labs = S.point_label_csr([[2, 0], [], [0, 1, 1]], 4)
+    assert offs.tolist() == [0, 2, 3, 4, 4] and labs.tolist() == [0, 2, 2, 0]
+
+
+def test_oracle_global_prune_rules():
+    """Hand cases for the restated DiskANN prune_all_neighbors (patched)."""
+    # points on a line; row 0 at 0 has neighbours 1..5
+    x = _line_store([0, 10, 12, 30, 31, 60])
+    offs = np.array([0, 5, 5, 5, 5, 5, 5], np.uint64)
+    ids = np.array([5, 1, 3, 2, 4], np.uint32)
+    # no labels, alpha 1: 1 (d=100) occludes 2 (d(1,2)=4 < 144), 3 and 4 and 5 -> [1]
+    rows, deg = oracle.stitched_global_prune(x, offs, ids, None, None, 4, 750, 1.0)
+    assert deg[0] == 1 and rows[0, 0] == 1
+    # rows with at most `range` neighbours are copied as they are
+    rows, deg = oracle.stitched_global_prune(x, offs, ids, None, None, 5, 750, 1.0)
+    assert deg[0] == 5 and rows[0].tolist() == [5, 1, 3, 2, 4]
+    # labels: row 0 and point 2 share label 7 which point 1 lacks, so 1 cannot
+    # occlude 2 any more (patch rule (F_p n F_x) in F_s)
+    lo = np.array([0, 2, 3, 5, 6, 7, 8], np.uint32)
+    lb = np.array([3, 7, 3, 3, 7, 3, 3, 3], np.uint32)
+    rows, deg = oracle.stitched_global_prune(x, offs, ids, lo, lb, 4, 750, 1.0)
+    assert rows[0, :deg[0]].tolist() == [1, 2]
+    # later passes: entries whose occlusion factor lies in (1, a] enter in the
+    # pass with that a (a = 1, 1.2, 1.44, ... while a <= alpha)
+    z = np.zeros((4, 16), np.uint8)
+    z[1, 0] = 100            # s, d(0,s) = 10000
+    z[2, 0], z[2, 1] = 100, 200  # x: d(0,x) = 50000, d(s,x) = 40000 -> factor 1.25
+    z[3, 0], z[3, 1] = 100, 210  # w: d(0,w) = 54100, d(s,w) = 44100 -> factor 1.2268
+    o2 = np.array([0, 3, 3, 3, 3], np.uint64)
+    i2 = np.array([1, 2, 3], np.uint32)
+    rows, deg = oracle.stitched_global_prune(z, o2, i2, None, None, 2, 750, 1.2)
+    assert rows[0, :deg[0]].tolist() == [1]  # both factors above 1.2
+    rows, deg = oracle.stitched_global_prune(z, o2, i2, None, None, 2, 750, 1.3)
+    # pass 2 (a = 1.2): nothing new; a = 1.44 > 1.3 stops: still [1]
+    assert rows[0, :deg[0]].tolist() == [1]
+    rows, deg = oracle.stitched_global_prune(z, o2, i2, None, None, 2, 750, 1.5)
+    # a = 1.44 <= 1.5: x (1.25) is selected, then the range of 2 is full
+    assert rows[0, :deg[0]].tolist() == [1, 2]
+    # shortlist: row 0 with labels {1, 2}; its three nearest carry only label 1,
+    # so with range 2 the quota (1 per label) admits the nearest label-2 carrier
+    w = _line_store([0, 1, 2, 3, 10, 50])
+    o3 = np.array([0, 5, 5, 5, 5, 5, 5], np.uint64)
+    i3 = np.array([1, 2, 3, 4, 5], np.uint32)
+    lo3 = np.array([0, 2, 3, 4, 5, 6, 7], np.uint32)
+    lb3 = np.array([1, 2, 1, 1, 1, 2, 2], np.uint32)
+    rows, deg = oracle.stitched_global_prune(w, o3, i3, lo3, lb3, 2, 750, 1.2)
+    assert rows[0, :deg[0]].tolist() == [1, 4]
+    rows, deg = oracle.stitched_global_prune(w, o3, i3, None, None, 2, 750, 1.2)
+    # unlabelled: 1 occludes 2, 3 and 4 (factor 100/81 > 1.2); 5 (2500/2401) enters at a = 1.2
+    assert rows[0, :deg[0]].tolist() == [1, 5]
+
+
 def test_write_and_audit_index(tmp_path):
     names, l2i, i2l, pts = S.parse_label_lines(["a", "b", "a", "b"])
     offs = np.array([0, 1, 2, 3, 4], np.uint64)
@@ -256,9 +315,72 @@ def test_stitched_app_end_to_end(dance_lib, tmp_path):
     _, _, _, label_points = S.parse_labels(lf)
     orows, omed, _ = oracle.stitched(x, label_points, 16, 32, 16, 24, 16)
     assert [r.tolist() for r in rows] == orows
-    # multi-label input is refused rather than written unpruned
-    lf2 = tmp_path / "labels2.txt"
-    lf2.write_text("a,b\n" + "a\n" * (n - 1))
-    from dance_b200 import DanceError
-    with pytest.raises(DanceError, match="label-aware prune"):
-        S.build_gpu_stitched("uint8", dp, lf2, tmp_path / "s2", Rsmall=16, Lsmall=32, Rstitched=16, C=24, steps=16)
+
+
+@pytest.mark.gpu
+def test_stitched_app_multi_label_prunes_on_gpu(dance_lib, tmp_path):
+    """Multi-label input: the union graph is kept as <prefix>_full and the
+    index is the label-aware global prune of it (the DiskANN step of the
+    reference app, run here on the GPU), equal to the oracle's."""
+    rng = np.random.default_rng(19)
+    n, dim = 2500, 16
+    x = _dataset(np.uint8, n, dim, rng)
+    dp = tmp_path / "base.u8bin"
+    write_bin(dp, x)
+    lines = [",".join(f"t{int(v)}" for v in rng.choice(7, 1 + int(rng.integers(0, 3)), replace=False))
+             for _ in range(n)]
+    lf = tmp_path / "labels.txt"
+    lf.write_text("".join(ln + "\n" for ln in lines))
+    prefix = tmp_path / "multi"
+    timing = S.build_gpu_stitched("uint8", dp, lf, prefix, Rsmall=16, Lsmall=32, Rstitched=16, C=24, steps=16)
+    assert timing["final_prune_seconds"] > 0
+    full, _, _, _ = read_graph(str(prefix) + "_full")
+    pruned, _, _, _ = read_graph(prefix)
+    _, _, _, label_points = S.parse_labels(lf)
+    urows, _, _ = oracle.stitched(x, label_points, 16, 32, 16, 24, 16)
+    assert [r.tolist() for r in full] == urows
+    assert max(len(r) for r in full) > 16
+    offs = np.zeros(n + 1, np.uint64)
+    offs[1:] = np.cumsum([len(r) for r in urows])
+    ids = np.array([v for r in urows for v in r], np.uint32)
+    lo, lb = S.point_label_csr(label_points, n)
+    orows, odeg = oracle.stitched_global_prune(x, offs, ids, lo, lb, 16, 750, 1.2)
+    assert [r.tolist() for r in pruned] == [orows[v, :odeg[v]].tolist() for v in range(n)]
+    audit = S.audit_stitched_index(prefix, 16)
+    for k in ("invalid_ids", "self_loops", "duplicate_edges", "degree_overflow_rows"):
+        assert audit[k] == 0, (k, audit)
+    # allow_unpruned writes the union graph as the index
+    S.build_gpu_stitched("uint8", dp, lf, tmp_path / "u", Rsmall=16, Lsmall=32, Rstitched=16, C=24, steps=16,
+                         allow_unpruned=True)
+    assert [r.tolist() for r in read_graph(tmp_path / "u")[0]] == urows
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype,dim", [(np.uint8, 32), (np.float32, 24), (np.float32, 100)])
+def test_global_prune_kernel_matches_oracle(dance_lib, dtype, dim):
+    """dance_stitched_global_prune against the oracle restatement on a random
+    multi-label union graph with long rows (up to 300 neighbours, duplicate
+    and self ids), with and without labels."""
+    rng = np.random.default_rng(23)
+    n = 3000
+    x = _dataset(dtype, n, dim, rng)
+    deg = rng.integers(0, 300, n)
+    deg[:50] = rng.integers(40, 80, 50)
+    offs = np.zeros(n + 1, np.uint64)
+    offs[1:] = np.cumsum(deg)
+    ids = rng.integers(0, n, int(offs[-1])).astype(np.uint32)
+    ids[rng.random(len(ids)) < 0.01] = 0  # repeated ids (and self loops on row 0)
+    label_points = [sorted(rng.choice(n, int(rng.integers(200, 1500)), replace=False).tolist()) for _ in range(9)]
+    lo, lb = S.point_label_csr(label_points, n)
+    for labels in (True, False):
+        L0, L1 = (lo, lb) if labels else (None, None)
+        for R, alpha in ((32, 1.2), (64, 1.5), (17, 1.0)):
+            go, gi, npr = S.global_prune(x, offs, ids, L0, L1, R, 750, alpha)
+            orows, odeg = oracle.stitched_global_prune(x, offs, ids, L0, L1, R, 750, alpha)
+            assert np.array_equal(np.diff(go.astype(np.int64)), odeg.astype(np.int64)), (labels, R)
+            assert gi.tolist() == orows[np.arange(R)[None, :] < odeg[:, None]].tolist(), (labels, R)
+            assert npr == int((deg > R).sum())
+    # shorter pool cap (max_candidates) on the unlabelled path
+    go, gi, _ = S.global_prune(x, offs, ids, None, None, 32, 40, 1.2)
+    orows, odeg = oracle.stitched_global_prune(x, offs, ids, None, None, 32, 40, 1.2)
+    assert gi.tolist() == orows[np.arange(32)[None, :] < odeg[:, None]].tolist()
