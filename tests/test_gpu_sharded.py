@@ -41,3 +41,19 @@ def test_stitched_sharded_build_matches_single_gpu(dance_lib):
     res = subprocess.run(cmd, capture_output=True, text=True, env=env)
     assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
     assert "identical=True" in res.stdout
+
+
+def test_sharded_build_aborts_when_a_rank_leaves(dance_lib):
+    """A rank that never joins the build: the other rank's bounded wait runs
+    out, the communicator is aborted and the call returns -4 (NVLS off, plain
+    NCCL; nothing is faulted on the GPU)."""
+    import torch
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = ["timeout", "-k", "30", "180", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           "--nproc-per-node", "2", "--master-addr", "127.0.0.1", "--master-port", str(_port()),
+           os.path.join(HERE, "sharded_abort_check.py")]
+    res = subprocess.run(cmd, capture_output=True, text=True, env=env)
+    assert res.returncode == 0, res.stdout[-3000:] + res.stderr[-3000:]
+    assert "abort_ok=True" in res.stdout
