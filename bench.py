@@ -60,11 +60,15 @@ def parse():
                     help="cfg0_f32 vector storage: f16 (the reference's FAST_SMALL) or f32 (QUALITY)")
     ap.add_argument("--ref-gpu", action="store_true", default=True,
                     help="also time the reference's own GPU builder (oracle/_ref, sm_100a) once on the workload")
-    ap.add_argument("--workload", choices=["cfg1_u8_10M", "cfg0_f32", "cfg2_filtered", "cfg3_stitched"],
+    ap.add_argument("--workload", choices=["cfg1_u8_10M", "cfg0_f32", "cfg2_filtered", "cfg3_stitched",
+                                           "cfg4_f32_100M"],
                     default="cfg1_u8_10M",
                     help="cfg1_u8_10M: the headline standard build; cfg0_f32: configs[0], 1M float vectors "
                          "stored in fp16 (FAST_SMALL); cfg2_filtered: the GPU-FilteredVamana build of "
-                         "BASELINE.json configs[2]; cfg3_stitched: the per-label stitched build of configs[3]")
+                         "BASELINE.json configs[2]; cfg3_stitched: the per-label stitched build of configs[3]; "
+                         "cfg4_f32_100M: configs[4], 100M x 96 float32 over the GPUs of one box (torchrun)")
+    ap.add_argument("--index-dir", default="",
+                    help="cfg4: where to write (and read back) the DiskANN graph file; default: a temp dir")
     return ap.parse_args()
 
 
@@ -136,6 +140,19 @@ def emit(args, line):
         args.collect.append(line)
     else:
         print(json.dumps(line), flush=True)
+
+
+def graph_digest_device(graph, degree, n):
+    """64-bit polynomial digest of the first n rows and degrees, computed on
+    the GPU (for graphs too large to hash on the host quickly); equal graphs
+    give equal digests."""
+    import torch
+    g = graph[:n].to(torch.int64)
+    w = (torch.arange(g.shape[1], device=g.device, dtype=torch.int64) * 2654435761 + 97) | 1
+    row = (g * w[None, :]).sum(1) + degree[:n].to(torch.int64) * 40503
+    rw = (torch.arange(n, device=g.device, dtype=torch.int64) * 6364136223846793005) | 1
+    h = int((row * rw).sum().item()) & ((1 << 64) - 1)
+    return f"poly:{h:016x}"
 
 
 def graph_digest(graph, degree, n):
@@ -463,9 +480,78 @@ def reference_gpu(x, store, stride, our_medoid, args):
             "build": "DANCE vnew2 QUALITY profile (fp32/u8 distances, VAMANA_ITERS=4), nvcc 12.9 sm_100a"}
 
 
+CFG4 = dict(name="cfg4_f32_100M", N=100_000_000, dim=96, centroids=16384, sigma=0.3, R=64, L=100, C=80, STEPS=64,
+            alpha=1.2, iters=4, seed=42, queries=10_000)
+
+
+def sharded_ground_truth(x, q, k, rank, world):
+    """Exact top-k of the queries over the whole store, each rank taking one
+    slice of the base vectors; rank 0 merges the slices by (distance, id)."""
+    import torch
+    import torch.distributed as dist
+    from dance_b200 import workloads
+    n = x.shape[0]
+    per = (n + world - 1) // world
+    b0, b1 = min(n, rank * per), min(n, (rank + 1) * per)
+    ids, d = workloads.brute_force_knn(x[b0:b1], q, k)
+    ids = ids + b0
+    all_i = [torch.empty_like(ids) for _ in range(world)]
+    all_d = [torch.empty_like(d) for _ in range(world)]
+    dist.all_gather(all_i, ids)
+    dist.all_gather(all_d, d)
+    ci, cd = torch.cat(all_i, 1), torch.cat(all_d, 1)
+    o = torch.argsort(ci, dim=1)
+    ci, cd = torch.gather(ci, 1, o), torch.gather(cd, 1, o)
+    o2 = torch.argsort(cd, dim=1, stable=True)
+    return torch.gather(ci, 1, o2)[:, :k]
+
+
+def write_and_check_graph_file(path, graph, degree, n, start, rows_per_chunk=1 << 21):
+    """Streams the graph to a DiskANN graph file (formats.GRAPH_HEADER layout,
+    rows as u32 degree + ids) in row chunks, then reads it back in chunks and
+    checks every row against the device graph.  Returns sizes and seconds."""
+    import numpy as np
+    import torch
+    from dance_b200 import formats
+    t0 = time.perf_counter()
+    deg_all = degree[:n].to(torch.int64)
+    R = graph.shape[1]
+    total = formats.GRAPH_HEADER.size + 4 * n + 4 * int(deg_all.clamp(max=R).sum().item())
+    max_degree = int(deg_all.max().item())
+    with open(path, "wb") as f:
+        f.write(formats.GRAPH_HEADER.pack(total, max_degree, int(start), 0))
+        for a in range(0, n, rows_per_chunk):
+            e = min(n, a + rows_per_chunk)
+            rows = graph[a:e].cpu().numpy().view(np.uint32)
+            dg = degree[a:e].cpu().numpy().view(np.uint32)
+            f.write(formats.encode_graph(rows, dg, 0)[formats.GRAPH_HEADER.size:])
+    t1 = time.perf_counter()
+    ok = True
+    with open(path, "rb") as f:
+        hdr = formats.GRAPH_HEADER.unpack(f.read(formats.GRAPH_HEADER.size))
+        ok &= hdr == (total, max_degree, int(start), 0)
+        for a in range(0, n, rows_per_chunk):
+            e = min(n, a + rows_per_chunk)
+            dg = degree[a:e].cpu().numpy().view(np.uint32).astype(np.int64)
+            words = np.frombuffer(f.read(4 * int((dg + 1).sum())), dtype=np.uint32)
+            offs = np.concatenate([[0], np.cumsum(dg + 1)[:-1]])
+            ok &= bool(np.array_equal(words[offs], dg.astype(np.uint32)))
+            rows = graph[a:e].cpu().numpy().view(np.uint32)
+            mask = np.arange(R)[None, :] < dg[:, None]
+            keep = np.ones(len(words), bool)
+            keep[offs] = False
+            ok &= bool(np.array_equal(words[keep], rows[mask]))
+        ok &= f.read(1) == b""
+    t2 = time.perf_counter()
+    return {"path": str(path), "bytes": total, "write_seconds": t1 - t0, "read_back_seconds": t2 - t1,
+            "read_back_equal": bool(ok), "max_degree": max_degree, "start": int(start)}
+
+
 def run_sharded(args):
     """N > 1: one graph, vertex batches sharded over the ranks (strong scaling);
-    edge deltas exchanged with NCCL all-gathers inside libdance_b200."""
+    every edge goes to the rank that owns its target (grouped NCCL send/recv)
+    and the pruned rows are all-gathered, inside libdance_b200.  cfg1 by
+    default; --workload cfg4_f32_100M runs BASELINE.json configs[4]."""
     import datetime
     import numpy as np
     import torch
@@ -477,10 +563,19 @@ def run_sharded(args):
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
                             device_id=torch.device("cuda", local))
     lib = dance_b200.load()
-    n = args.n
-    R, L, C, S = WORKLOAD["R"], WORKLOAD["L"], WORKLOAD["C"], WORKLOAD["STEPS"]
-    x = make_workload("cuda", n)  # the same seeded vectors on every rank
+    big = args.workload == "cfg4_f32_100M"
+    spec = CFG4 if big else WORKLOAD
+    n = args.n if (args.n != WORKLOAD["N"] or not big) else CFG4["N"]
+    R, L, C, S = spec["R"], spec["L"], spec["C"], spec["STEPS"]
+    dim = spec["dim"]
+    t_gen = time.perf_counter()
+    if big:  # the same seeded vectors on every rank
+        x = workloads.gaussian_mixture_f32(n, dim, CFG4["centroids"], CFG4["sigma"], seed=CFG4["seed"], device="cuda")
+    else:
+        x = make_workload("cuda", n)
     store, stride = vamana.padded_store(x)
+    torch.cuda.synchronize()
+    gen_seconds = time.perf_counter() - t_gen
     uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
     if rank == 0:
         uid.copy_(torch.tensor(list(vamana.nccl_unique_id()), dtype=torch.uint8))
@@ -496,7 +591,7 @@ def run_sharded(args):
 
     def one_build():
         with torch.cuda.stream(stream):
-            return vamana.build_sharded(comm, store, WORKLOAD["dim"], stride, R, L, C, S, params=prm, workspace=ws,
+            return vamana.build_sharded(comm, store, dim, stride, R, L, C, S, params=prm, workspace=ws,
                                         graph=graph, degree=degree, table_degree=tdeg, stream=stream)
 
     for _ in range(args.warmup):
@@ -526,7 +621,7 @@ def run_sharded(args):
     clk = clocks.stop() if clocks else None
     # per-rank search-kernel roofline (max kernel time over ranks, summed bytes)
     alg = sum(search_algorithmic_bytes(r, 0, stride, R, 0) for r in reports)
-    alg += args.steps * WORKLOAD["iters"] * (n // world) * (stride + R * 8 + 8)
+    alg += args.steps * spec["iters"] * (n // world) * (stride + R * 8 + 8)
     kt = torch.tensor([sum(r["search_kernel_seconds"] for r in reports), alg], dtype=torch.float64, device="cuda")
     kmax = kt.clone()
     dist.all_reduce(kmax, op=dist.ReduceOp.MAX)
@@ -541,10 +636,18 @@ def run_sharded(args):
     stage_table = {k: {"max": float(smax[i]), "min": float(smin[i])} for i, k in enumerate(skeys)}
     stage_table["edge_bytes_received_per_rank"] = int(sreports[-1]["edge_bytes_received"])
     stage_table["graph_bytes_received_per_rank"] = int(sreports[-1]["graph_bytes_received"])
-    digest = graph_digest(graph, degree, n) if rank == 0 else None
+    if rank == 0:
+        digest = graph_digest_device(graph, degree, n) if big else graph_digest(graph, degree, n)
+    else:
+        digest = None
+    free_b, total_b = torch.cuda.mem_get_info()
+    used_gb = (total_b - free_b) / 1e9
     # e2e: every rank copies the vectors from pinned host memory, builds, rank 0 reads the graph back
     e2e = None
-    if not args.no_e2e:
+    if big:
+        e2e = {"value": None, "unit": "vectors/s",
+               "note": "not measured at 100M: each rank would pin a 38.4 GB host copy of the store"}
+    if not args.no_e2e and not big:
         hx = x.cpu().pin_memory()
         hg = torch.empty((n, R), dtype=torch.int32).pin_memory()
         hd = torch.empty((n,), dtype=torch.int32).pin_memory()
@@ -556,7 +659,7 @@ def run_sharded(args):
             dx.copy_(hx, non_blocking=True)
             st2, _ = vamana.padded_store(dx)
             torch.cuda.synchronize()
-            vamana.build_sharded(comm, st2, WORKLOAD["dim"], stride, R, L, C, S, params=prm, workspace=ws,
+            vamana.build_sharded(comm, st2, dim, stride, R, L, C, S, params=prm, workspace=ws,
                                  graph=graph, degree=degree, table_degree=tdeg)
             if rank == 0:
                 hg.copy_(graph[:n])
@@ -570,20 +673,58 @@ def run_sharded(args):
                       "on every rank, graph read back on rank 0; wall clock, max over ranks",
                "warmup": 0}
     rec = None
-    if rank == 0 and not args.no_recall:
-        q = make_queries("cuda")
-        gt, _ = workloads.brute_force_knn(x, q, 10)
-        ids, _ = vamana.search_queries(store, WORKLOAD["dim"], stride, graph, R, medoid, q, 100, 10)
-        rec = vamana.recall_at_k(ids.cpu().numpy(), gt.cpu().numpy())
+    index_file = None
+    if not args.no_recall:
+        t_gt = time.perf_counter()
+        if big:
+            q = workloads.gaussian_mixture_f32(CFG4["queries"], dim, CFG4["centroids"], CFG4["sigma"],
+                                               seed=CFG4["seed"], device="cuda", stream_offset=1)
+            gt = sharded_ground_truth(x, q, 10, rank, world)
+        else:
+            q = make_queries("cuda")
+            gt = sharded_ground_truth(x, q, 10, rank, world)
+        gt_seconds = time.perf_counter() - t_gt
+        if rank == 0:
+            ids, _ = vamana.search_queries(store, dim, stride, graph, R, medoid, q, 100, 10)
+            rec = vamana.recall_at_k(ids.cpu().numpy(), gt.cpu().numpy())
+    if big and rank == 0:
+        import tempfile
+        from dance_b200 import formats
+        deg = degree[:n]
+        g = graph[:n]
+        audit = {"invalid": int(((g < 0) | (g >= n)).logical_and(
+            torch.arange(R, device="cuda")[None, :] < deg[:, None]).sum().item()),
+            "min_degree": int(deg.min().item()), "max_degree": int(deg.max().item()),
+            "avg_degree": float(deg.double().mean().item())}
+        try:
+            d = args.index_dir or tempfile.mkdtemp(prefix="cfg4_index_")
+            path = os.path.join(d, "cfg4_f32_100M_R64")
+            index_file = write_and_check_graph_file(path, graph, degree, n, medoid)
+            os.remove(path)
+            if not args.index_dir:
+                os.rmdir(d)
+        except OSError as e:
+            index_file = {"error": f"{type(e).__name__}: {e}"}
+        index_file["audit"] = audit
     if rank == 0:
         peak, peak_kind = measured_peaks()
         achieved = float(ksum[1].item()) / float(kmax[0].item()) / 1e9
+        if big:
+            cfg = {"workload": CFG4["name"], "N": n, "dim": dim, "R": R, "L": L, "C": C, "STEPS": S,
+                   "alpha": CFG4["alpha"], "iters": CFG4["iters"], "seed": CFG4["seed"],
+                   "centroids": CFG4["centroids"], "storage": "fp32",
+                   "l2": "inputs larger than L2 (38.4 GB vector store), no flush"}
+        else:
+            cfg = config_dict(n)
+        cfg["parallelism"] = (f"vertex shards x{world}; edges to their target's owner by grouped NCCL send/recv; "
+                              "pruned rows all-gathered")
         line = {
             "metric": "vamana_build_vectors_per_s", "value": n * args.steps / elapsed, "unit": "vectors/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8",
-            "data": "synthetic (seeded GPU generator, BASELINE.json configs[1] recipe)",
-            "config": dict(config_dict(n), parallelism=f"vertex shards x{world}, NCCL all-gather of edge deltas"),
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32" if big else "u8",
+            "data": ("synthetic (seeded GPU generator, BASELINE.json configs[4] recipe)" if big else
+                     "synthetic (seeded GPU generator, BASELINE.json configs[1] recipe)"),
+            "config": cfg,
             "roofline": {"kernel": "search_kernel", "bound": "hbm", "achieved": achieved, "peak": peak * world,
                          "unit": "GB/s", "frac": achieved / (peak * world), "peak_source": peak_kind + f" x{world}",
                          "traffic": None},
@@ -595,7 +736,12 @@ def run_sharded(args):
         if e2e:
             line["e2e"] = e2e
         if rec is not None:
-            line["recall_at_10"] = {"L_search": 100, "queries": WORKLOAD["queries"], "ours": rec}
+            line["recall_at_10"] = {"L_search": 100, "queries": int(q.shape[0]), "ours": rec,
+                                    "ground_truth_seconds": gt_seconds}
+        if big:
+            line["index_file"] = index_file
+            line["data_generation_seconds"] = gen_seconds
+            line["device_memory_used_gb_rank0"] = used_gb
         emit(args, line)
     del ws
     comm.close()
@@ -1151,30 +1297,18 @@ FILTERED_CPU_SAMPLE = 6_000  # points built by the oracle for cpu_baseline
 
 
 def filtered_label_starts(x, offs, labs, vocab):
-    """Start point of each label: the member nearest to the label's mean (a
-    stand-in for DiskANN's label start selection, which lives outside the
-    reference); the global start is the point nearest to the overall mean."""
-    import numpy as np
-    import torch
+    """Label start points and the global start as DiskANN sets them before
+    the GPU hook (integration patch lines 20238-20267), computed on the GPU
+    by the library: per label the least-chosen of 25 hashed member draws
+    (dance_select_label_starts), and the point nearest to the centroid
+    (dance_calculate_entry_point)."""
+    from dance_b200 import filtered as FL, vamana
     n = x.shape[0]
-    rows = torch.from_numpy(np.repeat(np.arange(n), np.diff(offs.astype(np.int64)))).cuda()
-    lab = torch.from_numpy(labs.astype(np.int64)).cuda()
-    xf = x.float()
-    sums = torch.zeros((vocab, x.shape[1]), dtype=torch.float64, device="cuda")
-    sums.index_add_(0, lab, xf[rows].double())
-    cnt = torch.bincount(lab, minlength=vocab).clamp(min=1).double()
-    mean = (sums / cnt[:, None]).float()
-    d = ((xf[rows] - mean[lab]) ** 2).sum(1)
-    key = d.double()
-    best = torch.full((vocab,), float("inf"), dtype=torch.float64, device="cuda")
-    best.scatter_reduce_(0, lab, key, reduce="amin")
-    hit = key == best[lab]
-    starts = torch.full((vocab,), n, dtype=torch.int64, device="cuda")
-    starts.scatter_reduce_(0, lab[hit], rows[hit], reduce="amin")
-    starts = starts.cpu().numpy()
-    starts[starts >= n] = 0xFFFFFFFF
-    g = int(((xf - xf.mean(0)) ** 2).sum(1).argmin())
-    return starts.astype(np.uint32), g
+    loff, lpts = FL.label_points_csr(offs, labs, vocab)
+    starts = FL.select_label_starts(loff, lpts, n, 25, FILTERED["seed"])
+    store, stride = vamana.padded_store(x)
+    g = FL.calculate_entry_point(store, x.shape[1], stride)
+    return starts, g
 
 
 def filtered_recall(x, store, stride, offs, labs, graph, starts, R, queries, qlabels, L_search=100, K=10):
@@ -1279,7 +1413,7 @@ def run_filtered(args):
                    "label_memberships": int(offs[-1]), "R": R, "L": L, "FilteredL": FL, "C": C, "STEPS": S,
                    "alpha": alpha, "rounds": 3, "pools": [min(FL, 32), min(FL, 32, 8), min(64, FL)],
                    "l2": "inputs larger than L2 (192 MB fp16 vectors + graphs), no flush",
-                   "label_starts": "member nearest to the label mean (stand-in for DiskANN's selection)"},
+                   "label_starts": "DiskANN's rule on the GPU: least-chosen of 25 hashed member draws per label; global start = point nearest the centroid"},
         "roofline": {"kernel": "fl_union_search_kernel", "bound": "hbm", "achieved": achieved, "peak": peak,
                      "unit": "GB/s", "frac": achieved / peak, "peak_source": peak_kind, "traffic": None,
                      "algorithmic_bytes_per_launch": alg / 3, "avg_launch_ms": ksec / 3 * 1e3},
@@ -1431,6 +1565,15 @@ def main():
         if args.impl == "reference":
             return run_stitched_reference(args, args.n if args.n != WORKLOAD["N"] else STITCHED["N"])
         return run_stitched(args)
+    if args.workload == "cfg4_f32_100M":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "workload": "cfg4_f32_100M",
+                              "unavailable": "the reference has no multi-GPU build and its one-GPU build does not "
+                                             "hold 100M float32 vectors with N x C work rows"}), flush=True)
+            return 0
+        if dist_env()[1] < 2:
+            raise SystemExit("cfg4_f32_100M runs sharded: launch with torchrun --nproc-per-node N (N >= 2)")
+        return run_sharded(args)
     if args.impl == "reference":
         return run_reference(args)
     return run_ours(args)

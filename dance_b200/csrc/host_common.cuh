@@ -419,6 +419,8 @@ struct DanceWorkspace
     static constexpr int kHugeBlocks = 4;
     DevBuf med_scores, med_cand, medoid;
     DevBuf counters;
+    // sharded build: edge exchange (per-rank counts, send/receive pairs)
+    DevBuf xcnt, xmat, xoff, xcur, xsend, xrecv;
 
     // n: vertices of the whole graph; local: vertices whose work rows,
     // expansion lists and own distance rows live here (n on one GPU, the
@@ -453,7 +455,9 @@ struct DanceWorkspace
         DANCE_CUDA(rev_cnt.ensure((uint64_t)local * 4));
         DANCE_CUDA(rev_off.ensure(((uint64_t)local + 1) * 4));
         DANCE_CUDA(rev_cursor.ensure((uint64_t)local * 4));
-        DANCE_CUDA(rev.ensure(nr * 4));
+        // one GPU: every edge may target this GPU's vertices; sharded: the
+        // exchange grows the array to the edges a round actually delivers
+        DANCE_CUDA(rev.ensure((graph ? nr : lr) * 4));
         DANCE_CUDA(tiles.ensure(ntiles * 4));
         DANCE_CUDA(heavy_list.ensure((uint64_t)local * 4));
         DANCE_CUDA(heavy_count.ensure(16));
@@ -480,6 +484,10 @@ namespace dance
 // targets [t0, t1) are merged into the work rows, which are indexed by
 // t - t0.  Sorting inside the merge kernels puts every target's sources in
 // ascending order, so the merge is deterministic.
+inline int merge_from_csr(int dtype, const StoreView &st, uint32_t C, const DanceVamanaParams &prm,
+                          DanceWorkspace &ws, uint32_t *work_ids, float *work_dists, uint32_t *work_deg, uint32_t t0,
+                          uint32_t t1, cudaStream_t s);
+
 inline int reverse_merge_impl(int dtype, const StoreView &st, uint32_t R, uint32_t C, const DanceVamanaParams &prm,
                               DanceWorkspace &ws, const uint32_t *src_ids, uint64_t src_stride,
                               const uint32_t *src_deg, uint32_t s0, uint32_t s1, uint32_t *work_ids, float *work_dists,
@@ -509,6 +517,15 @@ inline int reverse_merge_impl(int dtype, const StoreView &st, uint32_t R, uint32
     rev_fill_kernel<<<grid, 256, 0, s>>>(src_ids, src_stride, src_deg, N, R, s0, s1, t0, t1,
                                          ws.rev_cursor.as<uint32_t>(), ws.rev.as<uint32_t>());
     DANCE_LAUNCHED();
+    return merge_from_csr(dtype, st, C, prm, ws, work_ids, work_dists, work_deg, t0, t1, s);
+}
+
+// Reverse merge of targets [t0, t1) from the CSR already in ws.rev_off /
+// ws.rev (sources of target t at rev[rev_off[t - t0] .. rev_off[t - t0 + 1])).
+inline int merge_from_csr(int dtype, const StoreView &st, uint32_t C, const DanceVamanaParams &prm,
+                          DanceWorkspace &ws, uint32_t *work_ids, float *work_dists, uint32_t *work_deg, uint32_t t0,
+                          uint32_t t1, cudaStream_t s)
+{
     DANCE_CUDA(cudaMemsetAsync(ws.heavy_count.p, 0, 8, s)); // heavy and huge counts
     MergeParams mp{};
     mp.st = st;

@@ -7,9 +7,10 @@
 // [rank*chunk, min(N, (rank+1)*chunk)), chunk = ceil(N / world); vectors and
 // the current graph are replicated.  Each round:
 //   search + insert replay of own vertices  (reads the replicated graph)
-//   pack the first R slots of own work rows into rows [v0, v1) of an
-//   N x R edge table, ncclAllGather it (in place) with the work degrees
-//   reverse CSR of the edges that target own vertices + merge (local)
+//   every edge of the own work rows (first R slots) goes to the rank that
+//   owns its target: per-owner counts, an all-gather of the world x world
+//   count matrix, grouped ncclSend/ncclRecv of (target, source) pairs
+//   reverse CSR of the received edges + merge (local)
 //   prune own vertices into rows [v0, v1) of the graph, ncclAllGather the
 //   graph and degrees (in place) for the next round.
 // Every rank runs the same kernels as the one-GPU build on the same inputs,
@@ -167,6 +168,210 @@ static int allgather_rows(DanceComm *c, uint32_t *table, uint64_t chunk, uint64_
     return nccl_settle(c, deadline_of(c));
 }
 
+// ---------------------------------------------------------------- edge exchange
+// Every reverse edge (s -> t) of a round goes from the rank that owns s to
+// the rank that owns t, as a pair (t - owner's first vertex, s).  Edges are
+// the first min(work degree, R) slots of the own work rows with t < N and
+// t != s -- the edges the one-GPU reverse CSR counts.
+constexpr int kMaxWorld = 64;
+constexpr int kXchThreads = 256;
+constexpr int kXchItems = 8; // edges per thread and tile
+
+__device__ __forceinline__ bool xch_edge(const uint32_t *work_ids, const uint32_t *work_deg, uint32_t C, uint32_t R,
+                                         uint32_t N, uint32_t v0, uint64_t e, uint32_t &src, uint32_t &t)
+{
+    const uint64_t lv = e / R;
+    const uint32_t slot = (uint32_t)(e % R);
+    src = v0 + (uint32_t)lv;
+    if (slot >= min(work_deg[lv], R))
+        return false;
+    t = work_ids[lv * C + slot];
+    return t < N && t != src;
+}
+
+static __global__ void __launch_bounds__(kXchThreads) xch_count_kernel(const uint32_t *work_ids,
+                                                                       const uint32_t *work_deg, uint32_t C,
+                                                                       uint32_t R, uint32_t N, uint32_t v0,
+                                                                       uint32_t nloc, uint32_t chunk, int world,
+                                                                       uint32_t *counts)
+{
+    __shared__ uint32_t sc[kMaxWorld];
+    for (int i = threadIdx.x; i < world; i += blockDim.x)
+        sc[i] = 0;
+    __syncthreads();
+    const uint64_t total = (uint64_t)nloc * R;
+    for (uint64_t e = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; e < total; e += (uint64_t)gridDim.x * blockDim.x)
+    {
+        uint32_t src, t;
+        if (xch_edge(work_ids, work_deg, C, R, N, v0, e, src, t))
+            atomicAdd(&sc[t / chunk], 1u);
+    }
+    __syncthreads();
+    for (int i = threadIdx.x; i < world; i += blockDim.x)
+        if (sc[i])
+            atomicAdd(&counts[i], sc[i]);
+}
+
+// Tiles of kXchThreads * kXchItems edges: positions inside the tile come from
+// shared-memory counters, each tile reserves its range per owner with one
+// global atomic, then every edge is written to its owner's bucket.
+static __global__ void __launch_bounds__(kXchThreads) xch_fill_kernel(const uint32_t *work_ids,
+                                                                      const uint32_t *work_deg, uint32_t C, uint32_t R,
+                                                                      uint32_t N, uint32_t v0, uint32_t nloc,
+                                                                      uint32_t chunk, int world,
+                                                                      const uint32_t *send_off, uint32_t *cursor,
+                                                                      uint2 *send)
+{
+    __shared__ uint32_t sc[kMaxWorld], sbase[kMaxWorld];
+    const uint64_t total = (uint64_t)nloc * R;
+    const uint64_t tile = (uint64_t)kXchThreads * kXchItems;
+    for (uint64_t t0 = blockIdx.x * tile; t0 < total; t0 += (uint64_t)gridDim.x * tile)
+    {
+        for (int i = threadIdx.x; i < world; i += blockDim.x)
+            sc[i] = 0;
+        __syncthreads();
+        uint32_t owner[kXchItems], pos[kXchItems], tl[kXchItems], sv[kXchItems];
+#pragma unroll
+        for (int k = 0; k < kXchItems; ++k)
+        {
+            const uint64_t e = t0 + (uint64_t)k * kXchThreads + threadIdx.x;
+            uint32_t src = 0, t = 0;
+            owner[k] = 0xFFFFFFFFu;
+            if (e < total && xch_edge(work_ids, work_deg, C, R, N, v0, e, src, t))
+            {
+                owner[k] = t / chunk;
+                tl[k] = t - owner[k] * chunk;
+                sv[k] = src;
+                pos[k] = atomicAdd(&sc[owner[k]], 1u);
+            }
+        }
+        __syncthreads();
+        for (int i = threadIdx.x; i < world; i += blockDim.x)
+            sbase[i] = sc[i] ? send_off[i] + atomicAdd(&cursor[i], sc[i]) : 0u;
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < kXchItems; ++k)
+            if (owner[k] != 0xFFFFFFFFu)
+                send[sbase[owner[k]] + pos[k]] = make_uint2(tl[k], sv[k]);
+        __syncthreads();
+    }
+}
+
+static __global__ void rev_count_pairs_kernel(const uint2 *pairs, uint64_t n, uint32_t *cnt)
+{
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+        atomicAdd(&cnt[pairs[i].x], 1u);
+}
+
+static __global__ void rev_fill_pairs_kernel(const uint2 *pairs, uint64_t n, uint32_t *cursor, uint32_t *rev)
+{
+    for (uint64_t i = blockIdx.x * (uint64_t)blockDim.x + threadIdx.x; i < n; i += (uint64_t)gridDim.x * blockDim.x)
+    {
+        const uint2 p = pairs[i];
+        rev[atomicAdd(&cursor[p.x], 1u)] = p.y;
+    }
+}
+
+// Sends every own edge to the owner of its target and builds the reverse
+// CSR of the own targets [v0, v0 + nloc) from what arrives: counts by
+// owner, an all-gather of the world x world count matrix, grouped
+// ncclSend/ncclRecv of (target, source) pairs, then count / scan / fill.
+static int exchange_edges(DanceComm *c, DanceWorkspace &ws, uint32_t N, uint32_t R, uint32_t C, uint32_t v0,
+                          uint32_t nloc, uint32_t chunk, cudaStream_t s, uint64_t &sent_bytes, uint64_t &recv_bytes)
+{
+    const int W = c->world, me = c->rank;
+    const uint32_t *work_ids = ws.work_ids.as<uint32_t>();
+    const uint32_t *work_deg = ws.work_deg.as<uint32_t>();
+    DANCE_CUDA(ws.xcnt.ensure((uint64_t)W * 4));
+    DANCE_CUDA(ws.xmat.ensure((uint64_t)W * W * 4));
+    DANCE_CUDA(ws.xoff.ensure((uint64_t)W * 4));
+    DANCE_CUDA(ws.xcur.ensure((uint64_t)W * 4));
+    DANCE_CUDA(cudaMemsetAsync(ws.xcnt.p, 0, (uint64_t)W * 4, s));
+    const uint64_t total = (uint64_t)nloc * R;
+    const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((total + kXchThreads - 1) / kXchThreads,
+                                                                    (uint64_t)sm_count() * 8));
+    if (total)
+    {
+        xch_count_kernel<<<grid, kXchThreads, 0, s>>>(work_ids, work_deg, C, R, N, v0, nloc, chunk, W,
+                                                      ws.xcnt.as<uint32_t>());
+        DANCE_LAUNCHED();
+    }
+    DANCE_NCCL(ncclAllGather(ws.xcnt.as<uint32_t>(), ws.xmat.as<uint32_t>(), (size_t)W, ncclUint32, c->comm, s));
+    int rc = nccl_settle(c, deadline_of(c));
+    if (rc)
+        return rc;
+    std::vector<uint32_t> mat((size_t)W * W);
+    DANCE_CUDA(cudaMemcpyAsync(mat.data(), ws.xmat.p, (uint64_t)W * W * 4, cudaMemcpyDeviceToHost, s));
+    if ((rc = stream_wait(c, s, deadline_of(c))))
+        return rc;
+    // row r of mat: what rank r sends to each owner
+    std::vector<uint32_t> send_off(W + 1, 0), recv_off(W + 1, 0);
+    for (int o = 0; o < W; ++o)
+        send_off[o + 1] = send_off[o] + mat[(size_t)me * W + o];
+    for (int r = 0; r < W; ++r)
+        recv_off[r + 1] = recv_off[r] + mat[(size_t)r * W + me];
+    const uint64_t nsend = send_off[W], nrecv = recv_off[W];
+    DANCE_CUDA(ws.xsend.ensure(std::max<uint64_t>(nsend, 1) * 8));
+    DANCE_CUDA(ws.xrecv.ensure(std::max<uint64_t>(nrecv, 1) * 8));
+    DANCE_CUDA(ws.rev.ensure(std::max<uint64_t>(nrecv, 1) * 4));
+    DANCE_CUDA(cudaMemcpyAsync(ws.xoff.p, send_off.data(), (uint64_t)W * 4, cudaMemcpyHostToDevice, s));
+    DANCE_CUDA(cudaMemsetAsync(ws.xcur.p, 0, (uint64_t)W * 4, s));
+    uint2 *send = ws.xsend.as<uint2>(), *recv = ws.xrecv.as<uint2>();
+    if (total)
+    {
+        const uint64_t tiles = (total + (uint64_t)kXchThreads * kXchItems - 1) / ((uint64_t)kXchThreads * kXchItems);
+        xch_fill_kernel<<<(int)std::max<uint64_t>(1, std::min<uint64_t>(tiles, (uint64_t)sm_count() * 8)),
+                          kXchThreads, 0, s>>>(work_ids, work_deg, C, R, N, v0, nloc, chunk, W,
+                                               ws.xoff.as<uint32_t>(), ws.xcur.as<uint32_t>(), send);
+        DANCE_LAUNCHED();
+    }
+    const uint32_t own = mat[(size_t)me * W + me];
+    if (own)
+        DANCE_CUDA(cudaMemcpyAsync(recv + recv_off[me], send + send_off[me], (uint64_t)own * 8,
+                                   cudaMemcpyDeviceToDevice, s));
+    DANCE_NCCL(ncclGroupStart());
+    for (int o = 0; o < W; ++o)
+    {
+        if (o == me)
+            continue;
+        const uint32_t ns = mat[(size_t)me * W + o], nr = mat[(size_t)o * W + me];
+        if (ns)
+            DANCE_NCCL(ncclSend(send + send_off[o], (size_t)ns * 2, ncclUint32, o, c->comm, s));
+        if (nr)
+            DANCE_NCCL(ncclRecv(recv + recv_off[o], (size_t)nr * 2, ncclUint32, o, c->comm, s));
+    }
+    DANCE_NCCL(ncclGroupEnd());
+    if ((rc = nccl_settle(c, deadline_of(c))))
+        return rc;
+    sent_bytes += (nsend - own) * 8 + (uint64_t)W * 4;
+    recv_bytes += (nrecv - own) * 8 + (uint64_t)W * W * 4;
+    // reverse CSR of the own targets from the pairs that arrived
+    DANCE_CUDA(cudaMemsetAsync(ws.rev_cnt.p, 0, (uint64_t)nloc * 4, s));
+    const int g2 = (int)std::max<uint64_t>(1, std::min<uint64_t>((nrecv + 255) / 256, (uint64_t)sm_count() * 16));
+    if (nrecv)
+    {
+        rev_count_pairs_kernel<<<g2, 256, 0, s>>>(recv, nrecv, ws.rev_cnt.as<uint32_t>());
+        DANCE_LAUNCHED();
+    }
+    const uint32_t ntiles = (nloc + kScanTile - 1) / kScanTile;
+    if (ntiles > 0)
+    {
+        scan_tile_sums_kernel<<<ntiles, kScanThreads, 0, s>>>(ws.rev_cnt.as<uint32_t>(), nloc, ws.tiles.as<uint32_t>());
+        DANCE_LAUNCHED();
+        scan_tile_offsets_kernel<<<1, kScanThreads, 0, s>>>(ws.tiles.as<uint32_t>(), ntiles);
+        DANCE_LAUNCHED();
+        scan_apply_kernel<<<ntiles, kScanThreads, 0, s>>>(ws.rev_cnt.as<uint32_t>(), nloc, ws.tiles.as<uint32_t>(),
+                                                          ws.rev_off.as<uint32_t>(), ws.rev_cursor.as<uint32_t>());
+        DANCE_LAUNCHED();
+    }
+    if (nrecv)
+    {
+        rev_fill_pairs_kernel<<<g2, 256, 0, s>>>(recv, nrecv, ws.rev_cursor.as<uint32_t>(), ws.rev.as<uint32_t>());
+        DANCE_LAUNCHED();
+    }
+    return 0;
+}
+
 } // namespace dance
 
 extern "C" {
@@ -258,6 +463,8 @@ DANCE_API int dance_vamana_build_sharded(DanceComm *comm, int dtype, const void 
         return rc;
     if (!d_graph || !d_degree || !d_table_degree)
         return fail(-1, "null graph buffers");
+    if (comm->world > kMaxWorld)
+        return fail(-1, "at most %d ranks", kMaxWorld);
     if (R == 0 || L == 0 || C == 0 || STEPS == 0 || C < R || C > 1024 || L > (uint32_t)kMaxL)
         return fail(-1, "invalid parameters: R=%u L=%u C=%u STEPS=%u", R, L, C, STEPS);
     if (STEPS > L)
@@ -296,7 +503,7 @@ DANCE_API int dance_vamana_build_sharded(DanceComm *comm, int dtype, const void 
     const StoreView st = make_view(d_data, stride, N, dim, dtype);
     uint32_t *cur_ids = d_graph;   // (world * chunk) x R, replicated
     uint32_t *degree = d_degree;   // world * chunk, replicated
-    uint32_t *tdeg = d_table_degree; // world * chunk: degrees of the gathered edge table
+    (void)d_table_degree; // kept in the signature; the edge exchange no longer needs a gathered table
     float *cur_dists = ws->cur_dists.as<float>(); // own rows only
     DANCE_CUDA(cudaMemsetAsync(ws->counters.p, 0, 64, s));
     StageClock clk;
@@ -383,24 +590,17 @@ DANCE_API int dance_vamana_build_sharded(DanceComm *comm, int dtype, const void 
             rp.counters = sp.counters;
             if ((rc = dispatch<LaunchReplay>(dtype, st.nchunks, rp, s)))
                 return rc;
-            // own work rows (first R slots) -> rows [v0, v1) of the edge table
-            const uint64_t total = (uint64_t)nloc * R;
-            const int grid = (int)std::max<uint64_t>(1, std::min<uint64_t>((total + 255) / 256, sm_count() * 16));
-            pack_work_rows_kernel<<<grid, 256, 0, s>>>(rp.work_ids, rp.work_deg, C, R, v0, v1, cur_ids, tdeg);
-            DANCE_LAUNCHED();
         }
         if ((rc = clk.mark(kStReplay, s)))
             return rc;
-        if ((rc = allgather_rows(comm, cur_ids, chunk, R, s)) || (rc = allgather_rows(comm, tdeg, chunk, 1, s)))
+        if ((rc = exchange_edges(comm, *ws, N, R, C, v0, nloc, chunk, s, edge_sent, edge_recv)))
             return rc;
-        edge_sent += (uint64_t)chunk * (R + 1) * 4 * (uint64_t)(comm->world - 1);
-        edge_recv += peer_rows * (R + 1) * 4;
         if ((rc = clk.mark(kStEdgeExchange, s)))
             return rc;
         if (nloc)
         {
-            rc = reverse_merge_impl(dtype, st, R, C, prm, *ws, cur_ids, R, tdeg, 0, N, ws->work_ids.as<uint32_t>(),
-                                    ws->work_dists.as<float>(), ws->work_deg.as<uint32_t>(), v0, v1, s);
+            rc = merge_from_csr(dtype, st, C, prm, *ws, ws->work_ids.as<uint32_t>(), ws->work_dists.as<float>(),
+                                ws->work_deg.as<uint32_t>(), v0, v1, s);
             if (rc)
                 return rc;
             if ((rc = clk.mark(kStReverse, s)))

@@ -152,7 +152,10 @@ DANCE_API int dance_workspace_create_sharded(uint32_t num_points, int world, uin
  * ranks; d_data is the full store on every rank.  d_graph (world*chunk x R),
  * d_degree and d_table_degree (world*chunk) are caller buffers; on return
  * every rank holds the whole graph, bit-identical to the one-GPU build.
- * Edge deltas are exchanged with ncclAllGather twice per round. */
+ * Per round each new edge goes to the rank that owns its target (grouped
+ * ncclSend/ncclRecv of (target, source) pairs after an all-gather of the
+ * per-owner counts), and the pruned rows are all-gathered.  d_table_degree
+ * is no longer written (kept for the signature).  At most 64 ranks. */
 DANCE_API int dance_vamana_build_sharded(DanceComm *comm, int dtype, const void *d_data, uint64_t row_stride_bytes,
                                          uint32_t num_points, uint32_t dim, uint32_t R, uint32_t L, uint32_t C,
                                          uint32_t STEPS, const DanceVamanaParams *params, DanceWorkspace *ws,
