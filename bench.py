@@ -48,7 +48,8 @@ def parse():
     ap.add_argument("--steps", type=int, default=3)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    ap.add_argument("--n", type=int, default=WORKLOAD["N"], help="override N (profiling small cases)")
+    ap.add_argument("--n", "--num-points", dest="n", type=int, default=WORKLOAD["N"],
+                    help="override N (profiling small cases); under torchrun spell it --num-points")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-recall", action="store_true")
@@ -522,9 +523,10 @@ def write_and_check_graph_file(path, graph, degree, n, start, rows_per_chunk=1 <
         f.write(formats.GRAPH_HEADER.pack(total, max_degree, int(start), 0))
         for a in range(0, n, rows_per_chunk):
             e = min(n, a + rows_per_chunk)
-            rows = graph[a:e].cpu().numpy().view(np.uint32)
-            dg = degree[a:e].cpu().numpy().view(np.uint32)
-            f.write(formats.encode_graph(rows, dg, 0)[formats.GRAPH_HEADER.size:])
+            # [degree, ids...] per row: an (rows, R + 1) block masked to each row's length
+            blk = torch.cat([degree[a:e, None], graph[a:e]], 1).cpu().numpy().view(np.uint32)
+            dg = blk[:, 0].astype(np.int64)
+            f.write(blk[np.arange(R + 1)[None, :] <= dg[:, None]].tobytes())
     t1 = time.perf_counter()
     ok = True
     with open(path, "rb") as f:
