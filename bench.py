@@ -1094,12 +1094,80 @@ def reference_gpu_stitched(hx, label_points):
             "build": "DANCE vnew2 QUALITY profile via gpu_vamana_vnew2_build_float, nvcc 12.9 sm_100a"}
 
 
+def run_stitched_sharded(args):
+    """configs[3] over the GPUs of one box (torchrun): dance_stitched_build_sharded
+    (labels spread largest first over the ranks, local graphs to rank 0 over
+    NCCL, rank 0 stitches).  Host vectors in, host CSR out, so the timed call
+    is end to end; wall clock around each call, max over ranks."""
+    import datetime
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import dance_b200
+    from dance_b200 import stitched, vamana
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600), device_id=torch.device("cuda", local))
+    dance_b200.load()
+    n = args.n if args.n != WORKLOAD["N"] else STITCHED["N"]
+    rs, ls, rst, C, steps = (STITCHED[k] for k in ("r_small", "l_small", "r_stitched", "C", "steps"))
+    x, assign, label_points, offs, pts = stitched_inputs(n)
+    hx = np.ascontiguousarray(x.cpu().numpy())
+    uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+    if rank == 0:
+        uid.copy_(torch.tensor(list(vamana.nccl_unique_id()), dtype=torch.uint8))
+    dist.broadcast(uid, 0)
+    comm = vamana.Comm(rank, world, bytes(uid.cpu().tolist()), timeout_s=600.0)
+
+    def one():
+        return stitched.stitched_build_sharded(comm, hx, offs, pts, rs, ls, rst, C, steps)
+
+    for _ in range(args.warmup):
+        one()
+    times, out = [], None
+    for _ in range(args.steps):
+        dist.barrier()
+        t0 = time.perf_counter()
+        out = one()
+        times.append(time.perf_counter() - t0)
+    mine = torch.tensor([sum(times)], dtype=torch.float64, device="cuda")
+    dist.all_reduce(mine, op=dist.ReduceOp.MAX)
+    elapsed = float(mine.item())
+    if rank == 0:
+        ro, ri, med, st = out
+        import hashlib
+        line = {
+            "metric": "stitched_build_vectors_per_s", "value": n * args.steps / elapsed, "unit": "vectors/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup, "ms_per_step": elapsed / args.steps * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (seeded GPU generator, BASELINE.json configs[3] recipe)",
+            "config": {"workload": STITCHED["name"], "N": n, "labels": len(offs) - 1, "Rsmall": rs, "Lsmall": ls,
+                       "Rstitched": rst, "C": C, "steps": steps,
+                       "parallelism": f"labels over {world} ranks (largest first to the least loaded), local "
+                                      "graphs to rank 0 by NCCL send/recv",
+                       "timed": "dance_stitched_build_sharded, host vectors in, host CSR out (wall clock)"},
+            "e2e": {"value": n * args.steps / elapsed, "unit": "vectors/s", "h2d_bytes_per_step": int(hx.nbytes),
+                    "d2h_bytes_per_step": int(ro.nbytes + 4 * len(ri) + med.nbytes)},
+            "stage_seconds_rank0": {k: st[k] for k in ("label_build_wall_seconds", "label_graph_exchange_seconds",
+                                                        "local_to_global_remap_seconds", "total_seconds")},
+            "graph": {"edges": int(ro[-1]),
+                      "digest": hashlib.sha256(ro.tobytes() + ri.tobytes()).hexdigest()[:16]},
+        }
+        emit(args, line)
+    comm.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    return 0
+
+
 def run_stitched(args):
     import numpy as np
     import torch
     import dance_b200
     from dance_b200 import stitched, vamana
     rank, world, local = dist_env()
+    if world > 1:
+        return run_stitched_sharded(args)
     torch.cuda.set_device(local)
     lib = dance_b200.load()
     n = args.n if args.n != WORKLOAD["N"] else STITCHED["N"]

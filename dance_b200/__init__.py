@@ -126,7 +126,8 @@ class DanceStitchedStats(ctypes.Structure):
                 "per_label_gpu_build_max_seconds", "label_build_wall_seconds", "local_to_global_remap_seconds",
                 "total_seconds", "peak_gpu_mem_gb", "search_kernel_seconds")] + [
         ("search_evals", ctypes.c_uint64), ("search_expansions", ctypes.c_uint64),
-        ("streams", ctypes.c_uint32), ("reserved0", ctypes.c_uint32), ("reserved", ctypes.c_uint64 * 4)]
+        ("streams", ctypes.c_uint32), ("reserved0", ctypes.c_uint32),
+        ("label_graph_exchange_seconds", ctypes.c_double), ("reserved", ctypes.c_uint64 * 3)]
 
     def as_dict(self) -> dict:
         return {k: getattr(self, k) for k, _ in self._fields_ if not k.startswith("reserved")}
@@ -198,6 +199,8 @@ SIGNATURES = {
     "dance_stitched_remap": (_I, [_U32, _U32, _P, _P, _P, _P, _U32, _U32, _P, _P, _U64, _P, _P]),
     "dance_calculate_entry_point": (_I, [_I, _P, _U64, _U32, _U32, _PU32, _P]),
     "dance_select_label_starts": (_I, [_P, _P, _U32, _U32, _U32, _U64, _P, _P]),
+    "dance_stitched_build_sharded": (_I, [_P, _I, _P, _U32, _U32, _U32, _P, _P, _U32, _U32, _U32, _U32, _U32, _P,
+                                          _U32, _P, _P, _U64, _P, _P]),
     "dance_stitched_global_prune": (_I, [_I, _P, _U64, _U32, _U32, _P, _P, _P, _P, _U32, _U32, _F, _P, _P, _P,
                                          _P]),
     "dance_shard_range": (None, [_U32, _I, _I, _PU32, _PU32, _PU32]),

@@ -33,6 +33,7 @@
 #include <vector>
 
 #include "../../include/dance_b200.h"
+#include "comm.cuh"
 #include "host_common.cuh"
 #include "stitched_prune.cuh"
 
@@ -600,11 +601,76 @@ int dance_stitched_global_prune(int dtype, const void *d_data, uint64_t stride, 
     return 0;
 }
 
-int dance_stitched_build(int dtype, const void *h_data, uint32_t N, uint32_t dim, uint32_t num_labels,
-                         const uint64_t *label_offsets, const uint32_t *label_points, uint32_t r_small,
-                         uint32_t l_small, uint32_t r_out, uint32_t C, uint32_t steps,
-                         const DanceVamanaParams *params, uint32_t streams, uint64_t *row_offsets, uint32_t *row_ids,
-                         uint64_t row_ids_capacity, uint32_t *label_medoids, DanceStitchedStats *stats)
+} // extern "C"
+
+namespace dance
+{
+namespace
+{
+// Labels largest first to the least-loaded rank (ties: lower label id, lower
+// rank), the assignment stitched.lpt_assignment also uses.
+std::vector<int> lpt_owner(uint32_t num_labels, const uint64_t *label_offsets, int world)
+{
+    std::vector<uint32_t> order(num_labels);
+    std::iota(order.begin(), order.end(), 0u);
+    std::stable_sort(order.begin(), order.end(), [&](uint32_t a, uint32_t b) {
+        return label_offsets[a + 1] - label_offsets[a] > label_offsets[b + 1] - label_offsets[b];
+    });
+    std::vector<uint64_t> load((size_t)world, 0);
+    std::vector<int> owner(num_labels, 0);
+    for (uint32_t l : order)
+    {
+        int r = 0;
+        for (int k = 1; k < world; ++k)
+            if (load[(size_t)k] < load[(size_t)r])
+                r = k;
+        owner[l] = r;
+        load[(size_t)r] += label_offsets[l + 1] - label_offsets[l];
+    }
+    return owner;
+}
+
+// Sends every label's local graph, degrees (label-major segments) and medoid
+// from its owner to rank 0: grouped ncclSend/ncclRecv per label segment, and
+// a sum-reduce of the medoid array (zero where a rank does not own the label).
+int gather_label_graphs(DanceComm *c, uint32_t num_labels, const uint64_t *label_offsets, const std::vector<int> &owner,
+                        uint32_t r_small, uint32_t *d_lgraph, uint32_t *d_ldeg, uint32_t *d_med, cudaStream_t s)
+{
+    DANCE_NCCL(ncclGroupStart());
+    for (uint32_t l = 0; l < num_labels; ++l)
+    {
+        const uint64_t a = label_offsets[l], n = label_offsets[l + 1] - a;
+        const int o = owner[l];
+        if (n == 0 || o == 0)
+            continue;
+        if (c->rank == o)
+        {
+            DANCE_NCCL(ncclSend(d_lgraph + a * r_small, n * r_small, ncclUint32, 0, c->comm, s));
+            DANCE_NCCL(ncclSend(d_ldeg + a, n, ncclUint32, 0, c->comm, s));
+        }
+        else if (c->rank == 0)
+        {
+            DANCE_NCCL(ncclRecv(d_lgraph + a * r_small, n * r_small, ncclUint32, o, c->comm, s));
+            DANCE_NCCL(ncclRecv(d_ldeg + a, n, ncclUint32, o, c->comm, s));
+        }
+    }
+    DANCE_NCCL(ncclGroupEnd());
+    int rc = nccl_settle(c, deadline_of(c));
+    if (rc)
+        return rc;
+    DANCE_NCCL(ncclReduce(d_med, d_med, num_labels, ncclUint32, ncclSum, 0, c->comm, s));
+    if ((rc = nccl_settle(c, deadline_of(c))))
+        return rc;
+    return stream_wait(c, s, deadline_of(c));
+}
+
+// The stitched build, on one GPU (comm == nullptr) or label-parallel over the
+// communicator's ranks (outputs written on rank 0 only).
+int stitched_build_impl(DanceComm *comm, int dtype, const void *h_data, uint32_t N, uint32_t dim,
+                        uint32_t num_labels, const uint64_t *label_offsets, const uint32_t *label_points,
+                        uint32_t r_small, uint32_t l_small, uint32_t r_out, uint32_t C, uint32_t steps,
+                        const DanceVamanaParams *params, uint32_t streams, uint64_t *row_offsets, uint32_t *row_ids,
+                        uint64_t row_ids_capacity, uint32_t *label_medoids, DanceStitchedStats *stats)
 {
     DanceStitchedStats local_stats;
     DanceStitchedStats *st = stats ? stats : &local_stats;
@@ -619,8 +685,11 @@ int dance_stitched_build(int dtype, const void *h_data, uint32_t N, uint32_t dim
         rc = validate_labels(N, num_labels, label_offsets, label_points);
     if (rc)
         return rc;
-    if (!row_offsets || !label_medoids || (!row_ids && row_ids_capacity))
+    const bool root = !comm || comm->rank == 0;
+    if (root && (!row_offsets || !label_medoids || (!row_ids && row_ids_capacity)))
         return fail(-1, "[GPU stitched] null output pointer");
+    if (comm && comm->aborted)
+        return fail(-1, "[GPU stitched] communicator aborted");
     if (r_out < r_small)
         r_out = r_small;
     const uint64_t M = label_offsets[num_labels];
@@ -663,17 +732,46 @@ int dance_stitched_build(int dtype, const void *h_data, uint32_t N, uint32_t dim
     label_size_stats(num_labels, label_offsets, st);
 
     std::vector<uint32_t> med_local(num_labels, 0);
-    rc = build_label_graphs(store_dtype, d_seg.as<uint8_t>(), stride, dim, num_labels, label_offsets, nullptr,
-                            r_small, l_small, C, steps, prm, streams ? streams : 4u, d_lgraph.as<uint32_t>(),
-                            d_ldeg.as<uint32_t>(), med_local.data(), st);
+    std::vector<uint8_t> mask;
+    std::vector<int> owner;
+    if (comm)
+    {
+        owner = lpt_owner(num_labels, label_offsets, comm->world);
+        mask.resize(num_labels);
+        for (uint32_t l = 0; l < num_labels; ++l)
+            mask[l] = owner[l] == comm->rank;
+    }
+    rc = build_label_graphs(store_dtype, d_seg.as<uint8_t>(), stride, dim, num_labels, label_offsets,
+                            comm ? mask.data() : nullptr, r_small, l_small, C, steps, prm, streams ? streams : 4u,
+                            d_lgraph.as<uint32_t>(), d_ldeg.as<uint32_t>(), med_local.data(), st);
     if (rc)
         return rc;
+    d_seg.release();
+    if (comm)
+    {
+        DevBuf d_med;
+        DANCE_CUDA(d_med.ensure(std::max<uint64_t>(num_labels, 1) * 4));
+        for (uint32_t l = 0; l < num_labels; ++l)
+            if (owner[l] != comm->rank)
+                med_local[l] = 0;
+        DANCE_CUDA(cudaMemcpyAsync(d_med.p, med_local.data(), (uint64_t)num_labels * 4, cudaMemcpyHostToDevice, s));
+        const double xt0 = wall();
+        if ((rc = gather_label_graphs(comm, num_labels, label_offsets, owner, r_small, d_lgraph.as<uint32_t>(),
+                                      d_ldeg.as<uint32_t>(), d_med.as<uint32_t>(), s)))
+            return rc;
+        DANCE_CUDA(cudaMemcpy(med_local.data(), d_med.p, (uint64_t)num_labels * 4, cudaMemcpyDeviceToHost));
+        st->label_graph_exchange_seconds = wall() - xt0;
+        if (!root)
+        {
+            st->total_seconds = wall() - t0;
+            return 0;
+        }
+    }
     for (uint32_t l = 0; l < num_labels; ++l)
     {
         const uint64_t n = label_offsets[l + 1] - label_offsets[l];
         label_medoids[l] = n ? label_points[label_offsets[l] + (med_local[l] < n ? med_local[l] : 0u)] : 0u;
     }
-    d_seg.release();
     const double rt0 = wall();
     rc = remap_impl(N, num_labels, label_offsets, label_points, d_pts.as<uint32_t>(), d_lgraph.as<uint32_t>(),
                     d_ldeg.as<uint32_t>(), r_small, r_out, row_offsets, row_ids, row_ids_capacity, st, s);
@@ -682,6 +780,35 @@ int dance_stitched_build(int dtype, const void *h_data, uint32_t N, uint32_t dim
     st->local_to_global_remap_seconds = wall() - rt0;
     st->total_seconds = wall() - t0;
     return 0;
+}
+} // namespace
+} // namespace dance
+
+extern "C" {
+
+int dance_stitched_build(int dtype, const void *h_data, uint32_t N, uint32_t dim, uint32_t num_labels,
+                         const uint64_t *label_offsets, const uint32_t *label_points, uint32_t r_small,
+                         uint32_t l_small, uint32_t r_out, uint32_t C, uint32_t steps,
+                         const DanceVamanaParams *params, uint32_t streams, uint64_t *row_offsets, uint32_t *row_ids,
+                         uint64_t row_ids_capacity, uint32_t *label_medoids, DanceStitchedStats *stats)
+{
+    return stitched_build_impl(nullptr, dtype, h_data, N, dim, num_labels, label_offsets, label_points, r_small,
+                               l_small, r_out, C, steps, params, streams, row_offsets, row_ids, row_ids_capacity,
+                               label_medoids, stats);
+}
+
+int dance_stitched_build_sharded(DanceComm *comm, int dtype, const void *h_data, uint32_t N, uint32_t dim,
+                                 uint32_t num_labels, const uint64_t *label_offsets, const uint32_t *label_points,
+                                 uint32_t r_small, uint32_t l_small, uint32_t r_out, uint32_t C, uint32_t steps,
+                                 const DanceVamanaParams *params, uint32_t streams, uint64_t *row_offsets,
+                                 uint32_t *row_ids, uint64_t row_ids_capacity, uint32_t *label_medoids,
+                                 DanceStitchedStats *stats)
+{
+    if (!comm)
+        return fail(-1, "[GPU stitched] null communicator");
+    return stitched_build_impl(comm, dtype, h_data, N, dim, num_labels, label_offsets, label_points, r_small,
+                               l_small, r_out, C, steps, params, streams, row_offsets, row_ids, row_ids_capacity,
+                               label_medoids, stats);
 }
 
 } // extern "C"

@@ -201,68 +201,45 @@ def lpt_assignment(label_offsets: np.ndarray, world: int) -> np.ndarray:
     return owner
 
 
-def stitched_build_sharded(store, dim: int, stride: int, label_offsets: np.ndarray, label_points: np.ndarray,
-                           rank: int, world: int, r_small: int = 32, l_small: int = 100, r_stitched: int = 64,
-                           C: int = 96, steps: int = 64, params=None, streams: int = 4, remap_on_all: bool = False,
-                           group=None):
-    """Label-parallel build over torch.distributed ranks (one GPU each).
-
-    Labels are spread by size (largest first to the least-loaded rank); each
-    rank builds its labels from its own copy of the padded store; one
-    all-reduce (sum over zero-initialised buffers, so each entry keeps its
-    owner's value) hands every local graph and medoid to every rank; rank 0
-    (or every rank with remap_on_all) stitches.  Returns the stitched
-    (row_offsets, row_ids, label_medoids, stats) on stitching ranks, else
-    (None, None, label_medoids, stats).
-    """
-    import torch
-    import torch.distributed as dist
-
+def stitched_build_sharded(comm, data: np.ndarray, label_offsets: np.ndarray, label_points: np.ndarray,
+                           r_small: int = 32, l_small: int = 100, r_stitched: int = 64, C: int = 96, steps: int = 64,
+                           params=None, streams: int = 4):
+    """Label-parallel build over the GPUs of one box (``dance_stitched_build_sharded``):
+    labels largest first to the least-loaded rank, each rank builds its labels,
+    the local graphs go to rank 0 over NCCL and rank 0 stitches.  ``comm`` is a
+    ``vamana.Comm``.  Returns (row_offsets, row_ids, label_medoids, stats) on
+    rank 0 and (None, None, None, stats) on the other ranks."""
     lib = load()
-    dt = {torch.uint8: DANCE_U8, torch.float16: 1, torch.float32: DANCE_F32}[store.dtype]
+    data = np.ascontiguousarray(data)
+    if data.dtype == np.uint8:
+        dt = DANCE_U8
+    elif data.dtype == np.float32:
+        dt = DANCE_F32
+    else:
+        raise ValueError("GPU StitchedMVP supports uint8 and float in this version")
+    n, dim = data.shape
     offs = np.ascontiguousarray(label_offsets, dtype=np.uint64)
     pts = np.ascontiguousarray(label_points, dtype=np.uint32)
     nl = len(offs) - 1
-    M = int(offs[-1])
-    n = store.shape[0]
-    owner = lpt_assignment(offs, world)
-    mask = np.ascontiguousarray((owner == rank).astype(np.uint8))
-    dev = store.device
-    lgraph = torch.zeros(max(M * r_small, 1), dtype=torch.int32, device=dev)
-    ldeg = torch.zeros(max(M, 1), dtype=torch.int32, device=dev)
-    med_local = np.zeros(max(nl, 1), dtype=np.uint32)
+    root = comm.rank == 0
+    cap = int(offs[-1]) * int(r_small)
+    row_offsets = np.zeros(n + 1, dtype=np.uint64) if root else None
+    row_ids = np.zeros(max(cap, 1), dtype=np.uint32) if root else None
+    medoids = np.zeros(max(nl, 1), dtype=np.uint32) if root else None
     st = DanceStitchedStats()
     prm = params if params is not None else default_params()
-    torch.cuda.synchronize(dev)
-    rc = lib.dance_stitched_label_graphs(dt, _ptr(store), stride, n, dim, nl, _ptr(offs), _ptr(pts), _ptr(mask),
-                                         r_small, l_small, C, steps, ctypes.byref(prm), streams, _ptr(lgraph),
-                                         _ptr(ldeg), _ptr(med_local), ctypes.byref(st))
-    check(rc, "dance_stitched_label_graphs")
-    med_t = torch.from_numpy(np.where(mask[:nl] != 0, med_local[:nl], 0).astype(np.int64)).to(dev)
-    for t in (lgraph, ldeg, med_t):
-        dist.all_reduce(t, op=dist.ReduceOp.SUM, group=group)
-    med_local = med_t.cpu().numpy().astype(np.uint32)
-    medoids = np.array([pts[int(offs[l]) + (int(med_local[l]) if med_local[l] < offs[l + 1] - offs[l] else 0)]
-                        if offs[l + 1] > offs[l] else 0 for l in range(nl)], dtype=np.uint32)
-    stats = st.as_dict()
-    if rank != 0 and not remap_on_all:
-        return None, None, medoids, stats
-    row_offsets = np.zeros(n + 1, dtype=np.uint64)
-    cap = M * int(r_small)
-    row_ids = np.zeros(max(cap, 1), dtype=np.uint32)
-    st2 = DanceStitchedStats()
-    torch.cuda.synchronize(dev)
-    rc = lib.dance_stitched_remap(n, nl, _ptr(offs), _ptr(pts), _ptr(lgraph), _ptr(ldeg), r_small, r_stitched,
-                                  _ptr(row_offsets), _ptr(row_ids), cap, ctypes.byref(st2), None)
-    check(rc, "dance_stitched_remap")
-    for k in ("remap_invalid_local_ids", "remap_self_loops", "remap_duplicate_edges", "output_edges", "max_degree",
-              "processed_label_memberships", "local_to_global_remap_seconds"):
-        stats[k] = getattr(st2, k)
+    opt = (lambda a: _ptr(a) if a is not None else None)  # noqa: E731
+    rc = lib.dance_stitched_build_sharded(comm.handle, dt, _ptr(data), n, dim, nl, _ptr(offs), _ptr(pts), r_small,
+                                          l_small, r_stitched, C, steps, ctypes.byref(prm), streams,
+                                          opt(row_offsets), opt(row_ids), cap if root else 0, opt(medoids),
+                                          ctypes.byref(st))
+    check(rc, "dance_stitched_build_sharded")
+    if not root:
+        return None, None, None, st.as_dict()
     E = int(row_offsets[-1])
-    return row_offsets, row_ids[:E].copy(), medoids, stats
+    return row_offsets, row_ids[:E].copy(), medoids[:nl].copy(), st.as_dict()
 
 
-# ----------------------------------------------------------------- files
 def encode_csr_graph(row_offsets: np.ndarray, row_ids: np.ndarray, start: int = 0) -> bytes:
     """DiskANN graph bytes of a CSR graph; max_degree is the largest row (:200-227)."""
     offs = np.asarray(row_offsets, dtype=np.int64)

@@ -219,7 +219,8 @@ DANCE_API int dance_merge_edges_device_noalloc(const uint32_t *d_src, const uint
  * mapped to global ids, skipping invalid ids and self loops and not
  * repeating an id (:276-341).  Rstitched below Rsmall is raised to Rsmall,
  * as the reference app does (:86-87).  The global label-aware prune that the
- * reference runs for multi-label rows (:353-372) is not part of this call. */
+ * reference runs for multi-label rows (:353-372) is a separate call,
+ * dance_stitched_global_prune. */
 typedef struct DanceStitchedStats
 {
     uint32_t num_labels;
@@ -245,7 +246,8 @@ typedef struct DanceStitchedStats
     uint64_t search_expansions;
     uint32_t streams; /* label builds in flight at once */
     uint32_t reserved0;
-    uint64_t reserved[4];
+    double label_graph_exchange_seconds; /* sharded build: local graphs to rank 0 */
+    uint64_t reserved[3];
 } DanceStitchedStats;
 
 /* Host in, host out.  dtype DANCE_U8 or DANCE_F32 (fp16 storage when the
@@ -260,6 +262,21 @@ DANCE_API int dance_stitched_build(int dtype, const void *h_data, uint32_t num_p
                                    uint32_t steps, const DanceVamanaParams *params, uint32_t streams,
                                    uint64_t *row_offsets, uint32_t *row_ids, uint64_t row_ids_capacity,
                                    uint32_t *label_medoids, DanceStitchedStats *stats);
+/* The same build spread over the GPUs of one box (one process per GPU, a
+ * communicator from dance_comm_create): labels go largest first to the
+ * least-loaded rank, every rank builds its labels from its own copy of the
+ * vectors, the local graphs, degrees and medoids go to rank 0 (grouped
+ * ncclSend/ncclRecv per label segment, a sum-reduce of the medoids), and
+ * rank 0 stitches.  The outputs are written on rank 0 only and equal
+ * dance_stitched_build's; the other ranks' output pointers may be NULL.
+ * Every wait is bounded by the communicator's timeout (-4 after it). */
+DANCE_API int dance_stitched_build_sharded(DanceComm *comm, int dtype, const void *h_data, uint32_t num_points,
+                                           uint32_t dim, uint32_t num_labels, const uint64_t *label_offsets,
+                                           const uint32_t *label_points, uint32_t r_small, uint32_t l_small,
+                                           uint32_t r_stitched, uint32_t C, uint32_t steps,
+                                           const DanceVamanaParams *params, uint32_t streams, uint64_t *row_offsets,
+                                           uint32_t *row_ids, uint64_t row_ids_capacity, uint32_t *label_medoids,
+                                           DanceStitchedStats *stats);
 /* Device-resident first half, for label-parallel multi-GPU builds: builds
  * the labels with label_mask[l] != 0 (all when label_mask is NULL) from the
  * padded store d_data into d_local_graph (memberships x Rsmall, membership m

@@ -1,9 +1,10 @@
 """Worker for the multi-GPU stitched check (launched by torchrun, one rank per GPU).
 
-Builds the per-label graphs spread over the ranks (stitched_build_sharded)
-and, on rank 0, compares the stitched CSR graph and the label medoids with
-the one-GPU stitched build of the same data: they must be identical (the
-label graphs are independent, so where a label is built cannot change it).
+Builds the per-label graphs spread over the ranks through the C ABI
+(dance_stitched_build_sharded: local graphs to rank 0 over NCCL) and, on
+rank 0, compares the stitched CSR graph and the label medoids with the
+one-GPU stitched build of the same data: they must be identical (the label
+graphs are independent, so where a label is built cannot change it).
     python -m torch.distributed.run --nproc-per-node 2 --master-addr 127.0.0.1 \
         --master-port 29513 tests/stitched_sharded_check.py [N]
 """
@@ -38,13 +39,19 @@ def main():
         rng.shuffle(assign)
         offs, pts = S.labels_csr(S.labels_from_assignment(assign, nl))
         args = dict(r_small=16, l_small=40, r_stitched=24, C=32, steps=24)
-        store, stride = vamana.padded_store(torch.from_numpy(x).cuda())
-        ro, ri, med, _ = S.stitched_build_sharded(store, dim, stride, offs, pts, rank, world, **args)
+        uid = torch.zeros(128, dtype=torch.uint8, device="cuda")
+        if rank == 0:
+            uid.copy_(torch.tensor(list(vamana.nccl_unique_id()), dtype=torch.uint8))
+        dist.broadcast(uid, 0)
+        comm = vamana.Comm(rank, world, bytes(uid.cpu().tolist()), timeout_s=60.0)
+        ro, ri, med, st = S.stitched_build_sharded(comm, x, offs, pts, **args)
         torch.cuda.synchronize()
+        comm.close()
         if rank == 0:
             so, si, smed, _ = S.stitched_build(x, offs, pts, **args)
             ok = (np.array_equal(ro, so) and np.array_equal(ri, si) and np.array_equal(med, smed))
-            print(f"stitched x{world} vs one GPU: edges {len(ri)} vs {len(si)}, identical={ok}", flush=True)
+            print(f"stitched x{world} vs one GPU: edges {len(ri)} vs {len(si)}, exchange "
+                  f"{st['label_graph_exchange_seconds']:.3f} s, identical={ok}", flush=True)
         flag = torch.tensor([1 if ok else 0], device="cuda")
         dist.broadcast(flag, 0)
         ok = bool(flag.item())
