@@ -148,11 +148,13 @@ def graph_digest_device(graph, degree, n):
     the GPU (for graphs too large to hash on the host quickly); equal graphs
     give equal digests."""
     import torch
-    g = graph[:n].to(torch.int64)
-    w = (torch.arange(g.shape[1], device=g.device, dtype=torch.int64) * 2654435761 + 97) | 1
-    row = (g * w[None, :]).sum(1) + degree[:n].to(torch.int64) * 40503
-    rw = (torch.arange(n, device=g.device, dtype=torch.int64) * 6364136223846793005) | 1
-    h = int((row * rw).sum().item()) & ((1 << 64) - 1)
+    w = (torch.arange(graph.shape[1], device=graph.device, dtype=torch.int64) * 2654435761 + 97) | 1
+    h = 0
+    for a in range(0, n, 1 << 22):  # row chunks keep the int64 temporaries near 2 GB
+        e = min(n, a + (1 << 22))
+        row = (graph[a:e].to(torch.int64) * w[None, :]).sum(1) + degree[a:e].to(torch.int64) * 40503
+        rw = (torch.arange(a, e, device=graph.device, dtype=torch.int64) * 6364136223846793005) | 1
+        h = (h + int((row * rw).sum().item())) & ((1 << 64) - 1)
     return f"poly:{h:016x}"
 
 
@@ -638,10 +640,12 @@ def run_sharded(args):
     stage_table = {k: {"max": float(smax[i]), "min": float(smin[i])} for i, k in enumerate(skeys)}
     stage_table["edge_bytes_received_per_rank"] = int(sreports[-1]["edge_bytes_received"])
     stage_table["graph_bytes_received_per_rank"] = int(sreports[-1]["graph_bytes_received"])
+    digest = None
     if rank == 0:
-        digest = graph_digest_device(graph, degree, n) if big else graph_digest(graph, degree, n)
-    else:
-        digest = None
+        try:
+            digest = graph_digest_device(graph, degree, n) if big else graph_digest(graph, degree, n)
+        except Exception as e:
+            digest = f"unavailable: {type(e).__name__}: {e}"
     free_b, total_b = torch.cuda.mem_get_info()
     used_gb = (total_b - free_b) / 1e9
     # e2e: every rank copies the vectors from pinned host memory, builds, rank 0 reads the graph back
@@ -676,28 +680,38 @@ def run_sharded(args):
                "warmup": 0}
     rec = None
     index_file = None
+    post_errors = {}
+    if rank == 0:  # the measurement itself, on stderr, before anything that could fail
+        print(json.dumps({"timed_builds": args.steps, "seconds": elapsed, "vectors_per_s": n * args.steps / elapsed,
+                          "digest": digest}), file=sys.stderr, flush=True)
+    gt_seconds = None
     if not args.no_recall:
         t_gt = time.perf_counter()
         if big:
             q = workloads.gaussian_mixture_f32(CFG4["queries"], dim, CFG4["centroids"], CFG4["sigma"],
                                                seed=CFG4["seed"], device="cuda", stream_offset=1)
-            gt = sharded_ground_truth(x, q, 10, rank, world)
         else:
             q = make_queries("cuda")
-            gt = sharded_ground_truth(x, q, 10, rank, world)
+        gt = sharded_ground_truth(x, q, 10, rank, world)  # collective: every rank, also on errors below
         gt_seconds = time.perf_counter() - t_gt
         if rank == 0:
-            ids, _ = vamana.search_queries(store, dim, stride, graph, R, medoid, q, 100, 10)
-            rec = vamana.recall_at_k(ids.cpu().numpy(), gt.cpu().numpy())
+            try:
+                ids, _ = vamana.search_queries(store, dim, stride, graph, R, medoid, q, 100, 10)
+                rec = vamana.recall_at_k(ids.cpu().numpy(), gt.cpu().numpy())
+            except Exception as e:
+                post_errors["recall"] = f"{type(e).__name__}: {e}"
+        del gt
+        torch.cuda.empty_cache()
     if big and rank == 0:
         import tempfile
-        from dance_b200 import formats
         deg = degree[:n]
-        g = graph[:n]
-        audit = {"invalid": int(((g < 0) | (g >= n)).logical_and(
-            torch.arange(R, device="cuda")[None, :] < deg[:, None]).sum().item()),
-            "min_degree": int(deg.min().item()), "max_degree": int(deg.max().item()),
-            "avg_degree": float(deg.double().mean().item())}
+        bad = 0
+        for a in range(0, n, 1 << 22):
+            e = min(n, a + (1 << 22))
+            g = graph[a:e]
+            bad += int((((g < 0) | (g >= n)) & (torch.arange(R, device="cuda")[None, :] < deg[a:e, None])).sum())
+        audit = {"invalid": bad, "min_degree": int(deg.min().item()), "max_degree": int(deg.max().item()),
+                 "avg_degree": float(deg.double().mean().item())}
         try:
             d = args.index_dir or tempfile.mkdtemp(prefix="cfg4_index_")
             path = os.path.join(d, "cfg4_f32_100M_R64")
@@ -705,7 +719,7 @@ def run_sharded(args):
             os.remove(path)
             if not args.index_dir:
                 os.rmdir(d)
-        except OSError as e:
+        except Exception as e:
             index_file = {"error": f"{type(e).__name__}: {e}"}
         index_file["audit"] = audit
     if rank == 0:
@@ -740,6 +754,8 @@ def run_sharded(args):
         if rec is not None:
             line["recall_at_10"] = {"L_search": 100, "queries": int(q.shape[0]), "ours": rec,
                                     "ground_truth_seconds": gt_seconds}
+        if post_errors:
+            line["post_errors"] = post_errors
         if big:
             line["index_file"] = index_file
             line["data_generation_seconds"] = gen_seconds
