@@ -199,6 +199,10 @@ SIGNATURES = {
     "dance_stitched_remap": (_I, [_U32, _U32, _P, _P, _P, _P, _U32, _U32, _P, _P, _U64, _P, _P]),
     "dance_calculate_entry_point": (_I, [_I, _P, _U64, _U32, _U32, _PU32, _P]),
     "dance_select_label_starts": (_I, [_P, _P, _U32, _U32, _U32, _U64, _P, _P]),
+    "dance_kmeanspp_seed": (_I, [_P, _U64, _U64, _U32, _U32, _U64, _P, _P, _P]),
+    "dance_kmeans_lloyd": (_I, [_P, _U64, _U64, _U32, _U32, _U32, _P, _P, ctypes.POINTER(ctypes.c_double), _P]),
+    "dance_partition_assign": (_I, [_I, _P, _U64, _U64, _U32, _P, _U32, _U32, _P, _P, _P]),
+    "dance_partition_buckets": (_I, [_P, _U64, _U32, _U32, _P, _P, _P]),
     "dance_stitched_build_sharded": (_I, [_P, _I, _P, _U32, _U32, _U32, _P, _P, _U32, _U32, _U32, _U32, _U32, _P,
                                           _U32, _P, _P, _U64, _P, _P]),
     "dance_stitched_global_prune": (_I, [_I, _P, _U64, _U32, _U32, _P, _P, _P, _P, _U32, _U32, _F, _P, _P, _P,

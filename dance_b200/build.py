@@ -21,9 +21,10 @@ ROOT = PKG.parent
 CSRC = PKG / "csrc"
 LIB = PKG / "libdance_b200.so"
 
-SOURCES = ["vamana_build.cu", "vamana_sharded.cu", "gpu_merge.cu", "stitched.cu", "filtered.cu", "label_starts.cu"]
+SOURCES = ["vamana_build.cu", "vamana_sharded.cu", "gpu_merge.cu", "stitched.cu", "filtered.cu", "label_starts.cu",
+           "partition.cu"]
 HEADERS = ["dance_common.cuh", "vamana_kernels.cuh", "host_common.cuh", "filtered_kernels.cuh",
-           "gram_u8.cuh", "prune_quad.cuh", "stitched_prune.cuh"]
+           "gram_u8.cuh", "prune_quad.cuh", "stitched_prune.cuh", "replay_umma.cuh", "comm.cuh"]
 PUBLIC_HEADERS = ["dance_b200.h", "gpu_vamana_builder.h", "gpu_vamana_config.h", "gpu_merge.h",
                   "gpu_vamana_filtered.h"]
 
@@ -54,29 +55,58 @@ def up_to_date() -> bool:
     return all(p.stat().st_mtime <= t for p in _inputs() if p.exists())
 
 
+def _compile_cmd(src: Path, obj: Path, ptxas_v: bool) -> list[str]:
+    cmd = [nvcc(), *host_compiler(), *ARCH, "-O3", "-std=c++17", "-lineinfo",
+           "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
+           "--expt-relaxed-constexpr", "-I", str(ROOT / "include"), "-c", str(src), "-o", str(obj)]
+    if ptxas_v:
+        cmd += ["-Xptxas", "-v"]
+    # extra defines, e.g. DANCE_NVCC_FLAGS="-DVAMANA_ITERS=3 -DENABLE_FLOAT16_BUILD=1"
+    cmd += os.environ.get("DANCE_NVCC_FLAGS", "").split()
+    return cmd
+
+
 def build(force: bool = False, ptxas_v: bool = False, verbose: bool = False) -> Path:
+    """Compile every source to an object in parallel (one nvcc per source,
+    as many at once as the host has cores), then link the shared library."""
     if not force and up_to_date():
         return LIB
     started = time.time()
-    cmd = [nvcc(), *host_compiler(), *ARCH, "-O3", "-std=c++17", "-lineinfo",
-           "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden",
-           "--expt-relaxed-constexpr", "-shared",
-           "-I", str(ROOT / "include"), "-o", str(LIB) + ".tmp"]
-    if ptxas_v:
-        cmd += ["-Xptxas", "-v"]
-    cmd += ["--threads", "2"]
-    # extra defines, e.g. DANCE_NVCC_FLAGS="-DVAMANA_ITERS=3 -DENABLE_FLOAT16_BUILD=1"
-    cmd += os.environ.get("DANCE_NVCC_FLAGS", "").split()
-    cmd += [str(CSRC / s) for s in SOURCES]
-    cmd += ["-lnccl"]  # resolves to libnccl.so.2 (the copy torch loads when it is imported first)
+    objdir = ROOT / "_build" / "objs"
+    objdir.mkdir(parents=True, exist_ok=True)
+    jobs = []
+    for s in SOURCES:
+        obj = objdir / (Path(s).stem + ".o")
+        cmd = _compile_cmd(CSRC / s, obj, ptxas_v)
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        jobs.append((s, obj, cmd))
+    width = max(1, min(len(jobs), os.cpu_count() or 1))
+    running: list = []
+    failed = []
+    pending = list(jobs)
+    while pending or running:
+        while pending and len(running) < width:
+            s, obj, cmd = pending.pop(0)
+            running.append((s, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)))
+        s, proc = running.pop(0)
+        out, _ = proc.communicate()
+        if proc.returncode != 0:
+            failed.append((s, out))
+        elif ptxas_v or verbose:
+            sys.stderr.write(out)
+    if failed:
+        for s, out in failed:
+            sys.stderr.write(f"--- {s}\n{out}")
+        raise RuntimeError("nvcc failed building libdance_b200.so: " + ", ".join(s for s, _ in failed))
+    link = [nvcc(), *host_compiler(), *ARCH, "-shared", "-o", str(LIB) + ".tmp",
+            *[str(obj) for _, obj, _ in jobs], "-lnccl"]  # libnccl.so.2, the copy torch loads when imported first
     if verbose:
-        print(" ".join(cmd), flush=True)
-    res = subprocess.run(cmd, capture_output=True, text=True)
+        print(" ".join(link), flush=True)
+    res = subprocess.run(link, capture_output=True, text=True)
     if res.returncode != 0:
         sys.stderr.write(res.stdout + res.stderr)
-        raise RuntimeError("nvcc failed building libdance_b200.so")
-    if ptxas_v or verbose:
-        sys.stderr.write(res.stderr)
+        raise RuntimeError("linking libdance_b200.so failed")
     os.replace(str(LIB) + ".tmp", LIB)
     # stamp the library with the time the compile started, so a source edited
     # while nvcc ran leaves it stale

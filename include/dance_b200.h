@@ -393,6 +393,50 @@ DANCE_API int dance_search_queries_filtered(int dtype, const void *d_data, uint6
                                             uint32_t L_search, uint32_t K, uint32_t visited_log2,
                                             uint32_t *d_out_ids, float *d_out_dists, void *stream);
 
+/* ---- sharded disk-index pipeline: k-means partition ---------------------- */
+/* The GPU form of DiskANN's partitioner as the DANCE patch drives it before
+ * the GPU shard-build loop (partition_with_ram_budget ->
+ * shard_data_into_clusters_only_ids, integration patch lines 20629-20688;
+ * shard loop lines 3270-3600).  Distances are squared L2 in float, summed
+ * dimension by dimension without fused multiply-add; DiskANN's own
+ * (GEMM-based, randomly seeded) partitioner is not in the reference, so the
+ * shards match it in kind, not bit for bit.  Training rows are float32 with
+ * a stride that is a multiple of 4 bytes; k * dim <= 24576.  All four
+ * synchronise `stream` before they return (their scratch is freed). */
+/* k-means++ seeding: d_centers (k x dim) receives the k pivots, d_picked (k)
+ * the training rows they were copied from.  Pivot 0 is row
+ * splitmix64(seed) mod n; pivot p is drawn with probability proportional to
+ * the squared distance to the nearest earlier pivot, the weights quantised
+ * to floor(w / max w * 2^31) so that the draw (splitmix64 of seed and p,
+ * modulo the integer total) is exact. */
+DANCE_API int dance_kmeanspp_seed(const float *d_train, uint64_t row_stride_bytes, uint64_t n, uint32_t dim,
+                                  uint32_t k, uint64_t seed, float *d_centers, uint64_t *d_picked, void *stream);
+/* `iters` Lloyd iterations from the centers in d_centers (replaced in
+ * place): nearest center per row (lowest center on ties), then each center
+ * the float64 mean of its members (summed in row order within blocks of 4096
+ * rows, block sums in block order); a center without members stays.
+ * d_assign (n, optional) receives the assignment to the final centers,
+ * *residual_out (optional) the sum of squared distances of the last
+ * iteration's assignment. */
+DANCE_API int dance_kmeans_lloyd(const float *d_train, uint64_t row_stride_bytes, uint64_t n, uint32_t dim, uint32_t k,
+                                 uint32_t iters, float *d_centers, uint32_t *d_assign, double *residual_out,
+                                 void *stream);
+/* Each point's k_base (1..8) nearest centers, nearest first, lower center on
+ * ties, to d_out_centers (num_points x k_base) and, if given, their squared
+ * distances to d_out_dists.  dtype DANCE_U8, DANCE_F16 or DANCE_F32; rows
+ * need only be element-aligned (no 16-byte padding). */
+DANCE_API int dance_partition_assign(int dtype, const void *d_data, uint64_t row_stride_bytes, uint64_t num_points,
+                                     uint32_t dim, const float *d_centers, uint32_t num_centers, uint32_t k_base,
+                                     uint32_t *d_out_centers, float *d_out_dists, void *stream);
+/* Shard id lists from an assignment (num_points x k_base shard numbers):
+ * shard s holds d_shard_ids[d_shard_offsets[s] .. d_shard_offsets[s + 1]),
+ * the points that chose it, in ascending order (DiskANN's
+ * <prefix>_subshard-<s>_ids_uint32.bin contents).  num_shards <= 8192;
+ * choices >= num_shards are skipped; num_points * k_base < 2^32. */
+DANCE_API int dance_partition_buckets(const uint32_t *d_assign, uint64_t num_points, uint32_t k_base,
+                                      uint32_t num_shards, uint32_t *d_shard_offsets, uint32_t *d_shard_ids,
+                                      void *stream);
+
 #ifdef __cplusplus
 }
 #endif

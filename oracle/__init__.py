@@ -54,6 +54,10 @@ _SIGS = {
                                              _U32, _U32, _P, _P, _P, _P, _I]),
     "oracle_entry_point": (_U32, [_I, _P, _U64, _U32, _U32]),
     "oracle_label_starts": (None, [_P, _P, _U32, _U32, _U32, _U64, _P]),
+    "oracle_kmeanspp_seed": (None, [_P, _U64, _U64, _U32, _U32, _U64, _P, _P]),
+    "oracle_kmeans_lloyd": (None, [_P, _U64, _U64, _U32, _U32, _U32, _P, _P, _P]),
+    "oracle_partition_assign": (None, [_I, _P, _U64, _U64, _U32, _P, _U32, _U32, _P, _P]),
+    "oracle_partition_buckets": (None, [_P, _U64, _U32, _U32, _P, _P]),
     "oracle_stitched_global_prune": (_I, [_I, _P, _U64, _U32, _U32, _P, _P, _P, _P, _U32, _U32, _F, _P, _P]),
     "oracle_filtered_prune_lists": (_I, [_I, _P, _U64, _U32, _U32, _U32, _F, _P, _P, _U32, _P, _U32, _P, _P, _P,
                                          _P, _P]),
@@ -439,3 +443,49 @@ def filtered_prune_lists(data, lab: FilteredLabels, R, alpha, rows, lists, dists
                                        lab.num_labels, _p(rows), len(rows), _p(off), _p(ids), _p(ds), _p(g),
                                        _p(deg))
     return g, deg
+
+
+# ---------------------------------------------------------------- k-means partition
+def kmeanspp_seed(train, k, seed=42):
+    """k-means++ pivots of float32 rows as partition.cu defines them.
+    Returns (centers k x dim, picked rows)."""
+    t = np.ascontiguousarray(train, np.float32)
+    n, dim = t.shape
+    c = np.zeros((k, dim), np.float32)
+    picked = np.zeros(k, np.uint64)
+    load().oracle_kmeanspp_seed(_p(t), dim * 4, n, dim, k, seed, _p(c), _p(picked))
+    return c, picked
+
+
+def kmeans_lloyd(train, centers, iters):
+    """Lloyd iterations from `centers`; returns (centers, assignment, residual)."""
+    t = np.ascontiguousarray(train, np.float32)
+    n, dim = t.shape
+    c = np.array(centers, np.float32, copy=True, order="C")
+    asg = np.zeros(n, np.uint32)
+    res = ctypes.c_double(0.0)
+    load().oracle_kmeans_lloyd(_p(t), dim * 4, n, dim, c.shape[0], iters, _p(c), _p(asg), ctypes.byref(res))
+    return c, asg, float(res.value)
+
+
+def partition_assign(data, centers, k_base):
+    """Each row's k_base nearest centers (ids, squared distances)."""
+    d = np.ascontiguousarray(data)
+    dt = {np.dtype(np.uint8): 0, np.dtype(np.float16): 1, np.dtype(np.float32): 2}[d.dtype]
+    n, dim = d.shape
+    c = np.ascontiguousarray(centers, np.float32)
+    ids = np.zeros((n, k_base), np.uint32)
+    dists = np.zeros((n, k_base), np.float32)
+    load().oracle_partition_assign(dt, _p(d), dim * d.itemsize, n, dim, _p(c), c.shape[0], k_base, _p(ids),
+                                   _p(dists))
+    return ids, dists
+
+
+def partition_buckets(assign, num_shards):
+    """Shard id lists (offsets num_shards + 1, ids) of an n x k_base assignment."""
+    a = np.ascontiguousarray(assign, np.uint32)
+    n, kb = a.shape
+    off = np.zeros(num_shards + 1, np.uint32)
+    ids = np.zeros(max(n * kb, 1), np.uint32)
+    load().oracle_partition_buckets(_p(a), n, kb, num_shards, _p(off), _p(ids))
+    return off, ids[:int(off[-1])]

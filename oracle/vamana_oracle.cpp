@@ -2220,3 +2220,175 @@ extern "C" void oracle_label_starts(const uint32_t *off, const uint32_t *pts, ui
         counts[best] += 1;
     }
 }
+
+// ====================================================================== k-means partition
+// DiskANN's partitioner as the DANCE patch drives it before the GPU shard
+// loop (partition_with_ram_budget -> shard_data_into_clusters_only_ids,
+// integration patch lines 20629-20688), restated sequentially as
+// dance_b200/csrc/partition.cu defines it: squared L2 summed over
+// dimensions in order without fused multiply-add; k-means++ with weights
+// quantised to floor(w / max w * 2^31) and splitmix64 draws; Lloyd means in
+// float64, summed in row order within blocks of 4096 rows, block sums in
+// block order; k_base nearest centers, lower center on ties; shard id lists
+// in ascending point order.
+namespace
+{
+uint64_t part_splitmix64(uint64_t x)
+{
+    x += 0x9e3779b97f4a7c15ull;
+    x = (x ^ (x >> 30)) * 0xbf58476d1ce4e5b9ull;
+    x = (x ^ (x >> 27)) * 0x94d049bb133111ebull;
+    return x ^ (x >> 31);
+}
+
+uint64_t part_pivot_draw(uint64_t seed, uint32_t pivot)
+{
+    return part_splitmix64(seed ^ part_splitmix64(0x5deece66dull + pivot));
+}
+
+float part_sq_dist(const float *x, const float *c, uint32_t dim)
+{
+    float d = 0.0f;
+    for (uint32_t j = 0; j < dim; ++j)
+    {
+        const float diff = c[j] - x[j];
+        d += diff * diff;
+    }
+    return d;
+}
+
+const float *train_row(const float *train, uint64_t stride_bytes, uint64_t i)
+{
+    return reinterpret_cast<const float *>(reinterpret_cast<const uint8_t *>(train) + i * stride_bytes);
+}
+
+constexpr uint64_t kPartLloydChunk = 4096;
+} // namespace
+
+extern "C" void oracle_kmeanspp_seed(const float *train, uint64_t stride, uint64_t n, uint32_t dim, uint32_t k,
+                                     uint64_t seed, float *centers, uint64_t *picked)
+{
+    uint64_t pick = part_splitmix64(seed) % n;
+    picked[0] = pick;
+    std::copy(train_row(train, stride, pick), train_row(train, stride, pick) + dim, centers);
+    std::vector<float> mind(n);
+    std::vector<uint32_t> q(n);
+    for (uint32_t p = 1; p < k; ++p)
+    {
+        const float *c = centers + (uint64_t)(p - 1) * dim;
+        float mx = 0.0f;
+        for (uint64_t i = 0; i < n; ++i)
+        {
+            const float d = part_sq_dist(train_row(train, stride, i), c, dim);
+            mind[i] = p == 1 ? d : std::min(mind[i], d);
+            mx = std::max(mx, mind[i]);
+        }
+        uint64_t total = 0;
+        for (uint64_t i = 0; i < n; ++i)
+        {
+            q[i] = mx > 0.0f ? (uint32_t)((mind[i] / mx) * 2147483648.0f) : 1u;
+            total += q[i];
+        }
+        const uint64_t r = total ? part_pivot_draw(seed, p) % total : 0;
+        uint64_t run = 0;
+        pick = n - 1;
+        for (uint64_t i = 0; i < n; ++i)
+        {
+            run += q[i];
+            if (run > r)
+            {
+                pick = i;
+                break;
+            }
+        }
+        picked[p] = pick;
+        std::copy(train_row(train, stride, pick), train_row(train, stride, pick) + dim,
+                  centers + (uint64_t)p * dim);
+    }
+}
+
+extern "C" void oracle_partition_assign(int dtype, const void *data, uint64_t stride, uint64_t n, uint32_t dim,
+                                        const float *centers, uint32_t k, uint32_t kb, uint32_t *out_ids,
+                                        float *out_dists)
+{
+    const Store st = make_store(dtype, data, stride, dim);
+    std::vector<float> x(dim);
+    std::vector<std::pair<float, uint32_t>> best;
+    for (uint64_t i = 0; i < n; ++i)
+    {
+        for (uint32_t j = 0; j < dim; ++j)
+            x[j] = elem_of(st, (uint32_t)i, j);
+        best.clear();
+        for (uint32_t c = 0; c < k; ++c)
+            best.emplace_back(part_sq_dist(x.data(), centers + (uint64_t)c * dim, dim), c);
+        std::stable_sort(best.begin(), best.end(),
+                         [](const std::pair<float, uint32_t> &a, const std::pair<float, uint32_t> &b) {
+                             return a.first < b.first;
+                         });
+        for (uint32_t t = 0; t < kb; ++t)
+        {
+            out_ids[i * kb + t] = best[t].second;
+            if (out_dists)
+                out_dists[i * kb + t] = best[t].first;
+        }
+    }
+}
+
+extern "C" void oracle_kmeans_lloyd(const float *train, uint64_t stride, uint64_t n, uint32_t dim, uint32_t k,
+                                    uint32_t iters, float *centers, uint32_t *assign_out, double *residual)
+{
+    std::vector<uint32_t> asg(n);
+    std::vector<float> dist(n);
+    const uint64_t nchunks = (n + kPartLloydChunk - 1) / kPartLloydChunk;
+    std::vector<double> tot((size_t)k * dim), part((size_t)k * dim);
+    std::vector<uint64_t> cnt(k);
+    double resid = 0.0;
+    for (uint32_t it = 0; it < iters; ++it)
+    {
+        oracle_partition_assign(DANCE_F32, train, stride, n, dim, centers, k, 1, asg.data(), dist.data());
+        std::fill(tot.begin(), tot.end(), 0.0);
+        std::fill(cnt.begin(), cnt.end(), 0);
+        resid = 0.0;
+        for (uint64_t b = 0; b < nchunks; ++b)
+        {
+            std::fill(part.begin(), part.end(), 0.0);
+            double rs = 0.0;
+            const uint64_t e = std::min(n, (b + 1) * kPartLloydChunk);
+            for (uint64_t i = b * kPartLloydChunk; i < e; ++i)
+            {
+                const float *x = train_row(train, stride, i);
+                const uint32_t c = asg[i];
+                for (uint32_t j = 0; j < dim; ++j)
+                    part[(size_t)c * dim + j] += (double)x[j];
+                cnt[c] += 1;
+                rs += (double)dist[i];
+            }
+            for (size_t t = 0; t < part.size(); ++t)
+                tot[t] += part[t];
+            resid += rs;
+        }
+        for (uint32_t c = 0; c < k; ++c)
+            if (cnt[c])
+                for (uint32_t j = 0; j < dim; ++j)
+                    centers[(size_t)c * dim + j] = (float)(tot[(size_t)c * dim + j] / (double)cnt[c]);
+    }
+    if (assign_out)
+        oracle_partition_assign(DANCE_F32, train, stride, n, dim, centers, k, 1, assign_out, nullptr);
+    if (residual)
+        *residual = resid;
+}
+
+extern "C" void oracle_partition_buckets(const uint32_t *assign, uint64_t n, uint32_t kb, uint32_t S,
+                                         uint32_t *offsets, uint32_t *ids)
+{
+    std::vector<uint32_t> cnt(S + 1, 0);
+    for (uint64_t e = 0; e < n * kb; ++e)
+        if (assign[e] < S)
+            cnt[assign[e] + 1] += 1;
+    for (uint32_t s = 0; s < S; ++s)
+        cnt[s + 1] += cnt[s];
+    std::copy(cnt.begin(), cnt.end(), offsets);
+    for (uint64_t e = 0; e < n * kb; ++e)
+        if (assign[e] < S)
+            ids[cnt[assign[e]]++] = (uint32_t)(e / kb);
+}
