@@ -21,6 +21,7 @@
 #include "vamana_kernels.cuh"
 #include "gram_u8.cuh"
 #include "prune_quad.cuh"
+#include "replay_umma.cuh"
 
 namespace dance
 {
@@ -246,11 +247,93 @@ struct LaunchQuery
     }
 };
 
+// uint8 replay on the tcgen05 tensor cores (replay_umma.cuh) when
+// DANCE_REPLAY_UMMA=1 is set at the call: rows of at most 128 bytes, at most
+// 128 cached rows (R + STEPS) and C <= 128.  Off by default: on the
+// benchmarked shape it is bit-identical to replay_kernel but slower, since
+// the pair-by-pair replay evaluates only the ~9 % of the 128 x 128 pairs that
+// the insert rule reaches, while the Gram path turns every pair into bits.
+constexpr uint32_t kReplayMaskChunk = 1u << 20; // vertices per masks/bits pass
+
+inline bool replay_umma_enabled()
+{
+    const char *e = getenv("DANCE_REPLAY_UMMA");
+    return e && e[0] == '1';
+}
+
+inline bool replay_umma_fits(int dtype, uint32_t nchunks, uint32_t R, uint32_t S, uint32_t C)
+{
+    return dtype == kU8 && nchunks <= 8 && R + S <= kUmmaRows && C <= kUmmaRows && replay_umma_enabled();
+}
+
+// Mask buffer for a replay over `nverts` vertices (0 when the tensor-core
+// replay does not apply), and its vertex capacity.
+inline uint32_t replay_mask_vertices(int dtype, uint32_t nchunks, uint32_t R, uint32_t S, uint32_t C,
+                                     uint32_t nverts)
+{
+    if (!replay_umma_fits(dtype, nchunks, R, S, C))
+        return 0;
+    return std::max(1u, std::min(nverts, kReplayMaskChunk));
+}
+
+inline uint64_t replay_mask_bytes(uint32_t vertices, uint32_t S) { return (uint64_t)vertices * S * kMaskWords * 4u; }
+
+inline int launch_replay_umma(ReplayParams p, cudaStream_t s)
+{
+    auto ka = replay_masks_kernel<1>;
+    const uint32_t kch = umma_kchunks(p.st.nchunks);
+    // at least 50 KB per block: at most four blocks (4 x 128 tensor-memory
+    // columns) share an SM, so no allocation has to wait
+    const size_t smem_a =
+        std::max<size_t>((size_t)UmmaMaskLayout(p.R, p.exp_stride, kch).bytes * kWarpsPerBlock, 50u * 1024u);
+    DANCE_CUDA(cudaFuncSetAttribute(ka, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_a));
+    DANCE_CUDA(cudaFuncSetAttribute(ka, cudaFuncAttributePreferredSharedMemoryCarveout,
+                                    (int)cudaSharedmemCarveoutMaxShared));
+    int occ = 0;
+    DANCE_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, ka, kBlockThreads, smem_a));
+    const uint64_t per_sm = (uint64_t)std::max(1, std::min(occ, 4));
+    auto kb = replay_bits_kernel;
+    const size_t smem_b = (size_t)UmmaBitsLayout(p.C, p.exp_stride).bytes * kWarpsPerBlock;
+    DANCE_CUDA(allow_smem(kb, smem_b));
+    for (uint32_t c0 = p.v0; c0 < p.v1; c0 += p.mask_vertices)
+    {
+        const uint32_t c1 = c0 + std::min(p.mask_vertices, p.v1 - c0);
+        const uint64_t batches = (c1 - c0 + kWarpsPerBlock - 1) / kWarpsPerBlock;
+        const int grid_a = (int)std::max<uint64_t>(1, std::min<uint64_t>(batches, per_sm * sm_count()));
+        ka<<<grid_a, kBlockThreads, smem_a, s>>>(p, c0, c1);
+        DANCE_LAUNCHED();
+        const int grid_b = wave_grid(kb, kBlockThreads, smem_b, c1 - c0);
+        kb<<<grid_b, kBlockThreads, smem_b, s>>>(p, c0, c1);
+        DANCE_LAUNCHED();
+    }
+    return 0;
+}
+
+// Reads and clears the tensor-core replay's timeout counter (after the
+// stream has been synchronised).
+inline int replay_umma_status()
+{
+    unsigned int t = 0;
+    DANCE_CUDA(cudaMemcpyFromSymbol(&t, g_replay_umma_timeouts, sizeof(t)));
+    if (t)
+    {
+        const unsigned int z = 0;
+        DANCE_CUDA(cudaMemcpyToSymbol(g_replay_umma_timeouts, &z, sizeof(z)));
+        return fail(-4, "tensor-core replay: %u blocks timed out waiting for the MMA", t);
+    }
+    return 0;
+}
+
 template <int DT, int CPL>
 struct LaunchReplay
 {
     static int run(ReplayParams p, cudaStream_t s)
     {
+        if constexpr (DT == kU8 && CPL == 1)
+        {
+            if (p.masks && p.mask_vertices && replay_umma_fits(DT, p.st.nchunks, p.R, p.exp_stride, p.C))
+                return launch_replay_umma(p, s);
+        }
         auto k = replay_kernel<DT, CPL>;
         p.per_warp = align16(replay_smem_per_warp(p.C, p.cache_rows, p.row_bytes, p.exp_stride));
         const size_t smem = (size_t)p.per_warp * kWarpsPerBlock;
@@ -419,6 +502,7 @@ struct DanceWorkspace
     static constexpr int kHugeBlocks = 4;
     DevBuf med_scores, med_cand, medoid;
     DevBuf counters;
+    DevBuf replay_masks; // uint8 tensor-core replay (one chunk of vertices)
     // sharded build: edge exchange (per-rank counts, send/receive pairs)
     DevBuf xcnt, xmat, xoff, xcur, xsend, xrecv;
 

@@ -101,6 +101,9 @@ int build_resident_impl(int dtype, const void *d_data, uint64_t stride, uint32_t
     rc = dispatch<LaunchInit>(dtype, st.nchunks, st, R, cur_ids, cur_dists, degree, 0u, N, 0u, s);
     if (rc)
         return rc;
+    const uint32_t mask_vertices = replay_mask_vertices(dtype, st.nchunks, R, ws.S, C, N);
+    if (mask_vertices)
+        DANCE_CUDA(ws.replay_masks.ensure(replay_mask_bytes(mask_vertices, ws.S)));
 
     for (uint32_t it = 0; it < prm.iters; ++it)
     {
@@ -152,6 +155,8 @@ int build_resident_impl(int dtype, const void *d_data, uint64_t stride, uint32_t
         rp.row_bytes = st.nchunks * 16;
         rp.cache_rows = R + ws.S;
         rp.counters = sp.counters;
+        rp.masks = mask_vertices ? ws.replay_masks.as<uint32_t>() : nullptr;
+        rp.mask_vertices = mask_vertices;
         rc = dispatch<LaunchReplay>(dtype, st.nchunks, rp, s);
         if (rc)
             return rc;
@@ -186,6 +191,8 @@ int build_resident_impl(int dtype, const void *d_data, uint64_t stride, uint32_t
     if (medoid_out)
         DANCE_CUDA(cudaMemcpyAsync(medoid_out, d_medoid, 4, cudaMemcpyDeviceToHost, s));
     DANCE_CUDA(cudaStreamSynchronize(s));
+    if ((rc = replay_umma_status()))
+        return rc;
     if (times)
     {
         float a = 0;
@@ -405,7 +412,21 @@ int dance_stage_replay(int dtype, const void *d_data, uint64_t stride, uint32_t 
     rp.row_bytes = rp.st.nchunks * 16;
     rp.cache_rows = R + exp_stride;
     rp.counters = nullptr;
-    return dispatch<LaunchReplay>(dtype, rp.st.nchunks, rp, as_stream(stream));
+    DevBuf masks; // freed (device-synchronising) on return: this stage entry point serves the parity tests
+    rp.mask_vertices = replay_mask_vertices(dtype, rp.st.nchunks, R, exp_stride, C, N);
+    if (rp.mask_vertices)
+    {
+        DANCE_CUDA(masks.ensure(replay_mask_bytes(rp.mask_vertices, exp_stride)));
+        rp.masks = masks.as<uint32_t>();
+    }
+    if ((rc = dispatch<LaunchReplay>(dtype, rp.st.nchunks, rp, as_stream(stream))))
+        return rc;
+    if (rp.mask_vertices)
+    {
+        DANCE_CUDA(cudaStreamSynchronize(as_stream(stream)));
+        return replay_umma_status();
+    }
+    return 0;
 }
 
 int dance_stage_reverse_merge(int dtype, const void *d_data, uint64_t stride, uint32_t N, uint32_t dim, uint32_t R,

@@ -747,6 +747,8 @@ struct ReplayParams
     uint32_t cache_rows;  // R + exp_stride
     uint32_t per_warp;    // smem bytes per warp
     unsigned long long *counters; // [2] pair evaluations
+    uint32_t *masks;              // uint8 tensor-core replay: OCC/VIC masks of mask_vertices vertices
+    uint32_t mask_vertices;       // (0: the pair-by-pair replay_kernel)
 };
 
 // Per-warp scratch of replay_kernel: the vector cache (initial neighbours,

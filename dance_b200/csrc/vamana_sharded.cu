@@ -452,6 +452,9 @@ DANCE_API int dance_vamana_build_sharded(DanceComm *comm, int dtype, const void 
     graph_recv += peer_rows * (R + 1) * 4;
     if ((rc = clk.mark(kStMedoidInit, s)))
         return rc;
+    const uint32_t mask_vertices = nloc ? replay_mask_vertices(dtype, st.nchunks, R, ws->S, C, nloc) : 0u;
+    if (mask_vertices)
+        DANCE_CUDA(ws->replay_masks.ensure(replay_mask_bytes(mask_vertices, ws->S)));
 
     for (uint32_t it = 0; it < prm.iters; ++it)
     {
@@ -504,6 +507,8 @@ DANCE_API int dance_vamana_build_sharded(DanceComm *comm, int dtype, const void 
             rp.row_bytes = st.nchunks * 16;
             rp.cache_rows = R + ws->S;
             rp.counters = sp.counters;
+            rp.masks = mask_vertices ? ws->replay_masks.as<uint32_t>() : nullptr;
+            rp.mask_vertices = mask_vertices;
             if ((rc = dispatch<LaunchReplay>(dtype, st.nchunks, rp, s)))
                 return rc;
         }
@@ -556,6 +561,8 @@ DANCE_API int dance_vamana_build_sharded(DanceComm *comm, int dtype, const void 
     if ((rc = clk.mark(kStGraphExchange, s)))
         return rc;
     if ((rc = stream_wait(comm, s, deadline_of(comm))))
+        return rc;
+    if ((rc = replay_umma_status())) // after the last collective: no rank is left waiting
         return rc;
     double acc[kStCount] = {0};
     clk.sum(acc);

@@ -204,6 +204,24 @@ def test_replay_bit_exact(dtype, alpha):
         assert np.array_equal(a, b)
 
 
+@pytest.mark.parametrize("dim,R,S,C", [(128, 64, 64, 80), (32, 24, 20, 56), (100, 40, 88, 128), (16, 8, 8, 12)])
+def test_replay_tensor_core_shapes_u8(dim, R, S, C, monkeypatch):
+    # DANCE_REPLAY_UMMA=1: the uint8 replay on the tcgen05 tensor cores
+    # (R + S <= 128, C <= 128, rows of at most 128 bytes): the benchmarked
+    # shape, small dimensions, an odd number of 16-byte chunks (zero-padded
+    # K), a full 128-row cache with the widest work row, and a tiny row
+    monkeypatch.setenv("DANCE_REPLAY_UMMA", "1")
+    x = make(np.uint8, 3000, dim=dim, centroids=24)
+    L = max(S, 32)
+    m, ids, ds, deg = _round_inputs(x, R, 1, C=C)
+    e = oracle.search(x, R, L, S, m, 8, ids, ds, deg, S)
+    for alpha in (1.0, 1.2):
+        g = _gpu_replay(x, R, C, np.float32(alpha), ids, ds, deg, *e)
+        o = oracle.replay(x, R, C, np.float32(alpha), ids, ds, deg, *e)
+        for a, b in zip(g, o):
+            assert np.array_equal(a, b)
+
+
 def _gpu_merge(x, R, C, wid, wd, wdeg, prm=None):
     import ctypes as ct
     lib = load()
@@ -312,8 +330,11 @@ def test_full_build_bit_exact(dtype):
     assert np.array_equal(g[2], o[2])
 
 
-def test_full_build_config_shape_u8():
-    # BASELINE config shape (R64 L100 C80 STEPS64) at a size the oracle finishes quickly
+@pytest.mark.parametrize("tensor_core_replay", ["0", "1"])
+def test_full_build_config_shape_u8(tensor_core_replay, monkeypatch):
+    # BASELINE config shape (R64 L100 C80 STEPS64) at a size the oracle
+    # finishes quickly, with the pair-by-pair and the tensor-core replay
+    monkeypatch.setenv("DANCE_REPLAY_UMMA", tensor_core_replay)
     x = make(np.uint8, 8000, centroids=64)
     R, L, C, S = 64, 100, 80, 64
     g = _gpu_build(x, R, L, C, S)
