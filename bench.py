@@ -62,12 +62,16 @@ def parse():
     ap.add_argument("--ref-gpu", action="store_true", default=True,
                     help="also time the reference's own GPU builder (oracle/_ref, sm_100a) once on the workload")
     ap.add_argument("--workload", choices=["cfg1_u8_10M", "cfg0_f32", "cfg2_filtered", "cfg3_stitched",
-                                           "cfg4_f32_100M"],
+                                           "cfg4_f32_100M", "cfg1_disk_sharded"],
                     default="cfg1_u8_10M",
                     help="cfg1_u8_10M: the headline standard build; cfg0_f32: configs[0], 1M float vectors "
                          "stored in fp16 (FAST_SMALL); cfg2_filtered: the GPU-FilteredVamana build of "
                          "BASELINE.json configs[2]; cfg3_stitched: the per-label stitched build of configs[3]; "
-                         "cfg4_f32_100M: configs[4], 100M x 96 float32 over the GPUs of one box (torchrun)")
+                         "cfg4_f32_100M: configs[4], 100M x 96 float32 over the GPUs of one box (torchrun); "
+                         "cfg1_disk_sharded: the sharded disk-index pipeline (k-means partition, shard builds, "
+                         "GPU merge, DiskANN files) on the configs[1] vectors")
+    ap.add_argument("--ram-budget-gb", type=float, default=3.0,
+                    help="cfg1_disk_sharded: DiskANN's per-shard build-memory budget (sets the part count)")
     ap.add_argument("--index-dir", default="",
                     help="cfg4: where to write (and read back) the DiskANN graph file; default: a temp dir")
     return ap.parse_args()
@@ -1637,8 +1641,97 @@ def run_filtered_reference(args):
     return 0
 
 
+def read_graph_padded(path, R):
+    """A DiskANN graph file as (N x R uint32 rows padded with 0xFFFFFFFF,
+    degrees, start)."""
+    import struct
+    import numpy as np
+    blob = np.fromfile(path, dtype=np.uint8)
+    _, width, start, _ = struct.unpack_from("<QIIQ", blob.tobytes()[:24])
+    words = blob[24:].view(np.uint32)
+    pos = []
+    i, nw = 0, len(words)
+    while i < nw:
+        pos.append(i)
+        i += 1 + int(words[i])
+    pos = np.array(pos, np.int64)
+    deg = words[pos].astype(np.int64)
+    g = np.full((len(pos), R), 0xFFFFFFFF, np.uint32)
+    cols = np.arange(R)[None, :]
+    mask = cols < np.minimum(deg, R)[:, None]
+    g[mask] = words[(pos[:, None] + 1 + cols)[mask]]
+    return g, deg.astype(np.uint32), int(start)
+
+
+def run_disk_sharded(args):
+    """The sharded disk-index pipeline (DiskANN build_merged_vamana_index with
+    the DANCE GPU shard build and GPU merge) on the configs[1] vectors: one
+    step is partition + shard builds + merge from a .u8bin file to the merged
+    DiskANN graph, wall clock; value = N / step seconds."""
+    import tempfile
+    import numpy as np
+    import torch
+    from dance_b200 import formats, shards, vamana, workloads
+    n = args.n
+    R, L = WORKLOAD["R"], WORKLOAD["L"]
+    x = make_workload("cuda", n)
+    d = tempfile.mkdtemp(prefix="disk_sharded_")
+    base = os.path.join(d, "base.u8bin")
+    hx = x.cpu().numpy()
+    with open(base, "wb") as f:
+        np.array([n, hx.shape[1]], np.uint32).tofile(f)
+        hx.tofile(f)
+    runs = []
+    for it in range(args.warmup + args.steps):
+        prefix = os.path.join(d, f"idx{it}")
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        res = shards.build_merged_vamana_index(base, "uint8", R, L, args.ram_budget_gb, prefix + "_mem.index",
+                                               prefix + "_medoids.bin", prefix + "_centroids.bin",
+                                               sampling_rate=0.01, k_base=2, seed=WORKLOAD["seed"])
+        torch.cuda.synchronize()
+        res["wall_seconds"] = time.perf_counter() - t0
+        if it >= args.warmup:
+            runs.append(res)
+    last = prefix + "_mem.index"
+    secs = [r["wall_seconds"] for r in runs]
+    g, deg, start = read_graph_padded(last, R)
+    audit = {k: int(v) for k, v in formats.audit_graph(g, deg, R, start).items()}
+    q = make_queries("cuda")
+    store, stride = vamana.padded_store(x)
+    gt, _ = workloads.brute_force_knn(x, q, 10)
+    found, _ = vamana.search_queries(store, x.shape[1], stride, torch.from_numpy(g.view(np.int32)).cuda(), R, start,
+                                     q, 100, 10)
+    recall = vamana.recall_at_k(found.cpu().numpy(), gt.cpu().numpy())
+    mean = float(np.mean(secs))
+    r0 = runs[-1]
+    line = {"metric": "vamana_disk_sharded_build_vectors_per_s", "value": n / mean, "unit": "vectors/s",
+            "n_gpus": 1, "steps": args.steps, "warmup": args.warmup, "ms_per_step": mean * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "u8",
+            "data": "synthetic (seeded GPU generator, BASELINE.json configs[1] recipe), written to a .u8bin file",
+            "config": {"workload": "cfg1_disk_sharded", "N": n, "dim": hx.shape[1], "R": R, "L": L,
+                       "ram_budget_gb": args.ram_budget_gb, "sampling_rate": 0.01, "k_base": 2,
+                       "shard_params": dict(zip(("R_shard", "C", "STEPS"), shards.shard_build_params(R, L))),
+                       "timing": "wall clock of build_merged_vamana_index (file in, DiskANN files out)"},
+            "num_parts": r0["num_parts"], "shard_sizes": r0["shard_sizes"],
+            "stage_seconds": {k: r0[k] for k in ("partition_seconds", "shard_build_seconds", "merge_seconds",
+                                                 "total_seconds")},
+            "graph": {"start": start, "avg_degree": float(deg.mean()), "max_degree": int(deg.max()),
+                      "audit": audit},
+            "recall_at_10": {"L_search": 100, "queries": int(q.shape[0]), "ours": recall}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def main():
     args = parse()
+    if args.workload == "cfg1_disk_sharded":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "workload": "cfg1_disk_sharded",
+                              "unavailable": "the reference's sharded disk pipeline runs inside DiskANN, which the "
+                                             "reference repository does not contain"}), flush=True)
+            return 0
+        return run_disk_sharded(args)
     if args.workload == "cfg0_f32":
         if args.impl == "reference":
             return run_cfg0_reference(args)

@@ -602,39 +602,59 @@ DANCE_API int merge_shards_gpu(const std::string &vamana_prefix, const std::stri
     auto bucket_of = [&](uint32_t src) { return std::min<uint64_t>(((uint64_t)src * buckets) / nnodes, buckets - 1); };
     auto bucket_begin = [&](uint64_t b) { return (uint32_t)((b * nnodes + buckets - 1) / buckets); };
 
-    // pass 1: remap and bucket the edges in host memory
+    // pass 1: remap and bucket the edges in host memory (each shard file is
+    // read whole, then parsed row by row)
     std::vector<std::vector<uint32_t>> bsrc(buckets), bdst(buckets);
+    {
+        const uint64_t per = est_edges / buckets + est_edges / (8 * buckets) + 1024;
+        for (uint64_t b = 0; b < buckets; ++b)
+        {
+            bsrc[b].reserve(per);
+            bdst[b].reserve(per);
+        }
+    }
+    std::vector<uint32_t> body;
     for (uint64_t i = 0; i < nshards; ++i)
     {
         const ShardMeta &s = shards[i];
-        std::ifstream in(s.graph_path, std::ios::binary);
-        uint32_t w, m;
-        uint64_t f;
-        read_header(in, w, m, f);
-        std::vector<uint32_t> nb;
-        for (uint32_t ls = 0; ls < s.idmap.size(); ++ls)
+        std::ifstream in(s.graph_path, std::ios::binary | std::ios::ate);
+        const uint64_t fbytes = (uint64_t)in.tellg();
+        if (fbytes < 24 || (fbytes - 24) % 4 != 0)
+            return -6;
+        in.seekg(24);
+        body.resize((fbytes - 24) / 4);
+        if (!body.empty())
+            in.read(reinterpret_cast<char *>(body.data()), fbytes - 24);
+        if (!in)
+            return -6;
+        uint64_t pos = 0;
+        const uint64_t nw = body.size();
+        const uint32_t nloc = (uint32_t)s.idmap.size();
+        for (uint32_t ls = 0; ls < nloc; ++ls)
         {
             const uint32_t gs = s.idmap[ls];
-            uint32_t deg = 0;
-            in.read(reinterpret_cast<char *>(&deg), 4);
-            nb.resize(deg);
-            if (deg)
-                in.read(reinterpret_cast<char *>(nb.data()), 4ull * deg);
-            if (!in)
+            if (pos >= nw)
+                return -6;
+            const uint32_t deg = body[pos++];
+            if (deg > nw - pos)
                 return -6;
             const uint64_t b = bucket_of(gs);
-            for (uint32_t ld : nb)
+            std::vector<uint32_t> &vs = bsrc[b], &vd = bdst[b];
+            for (uint32_t j = 0; j < deg; ++j)
             {
-                if (ld >= s.idmap.size())
+                const uint32_t ld = body[pos + j];
+                if (ld >= nloc)
                     return -7;
                 const uint32_t gd = s.idmap[ld];
                 if (gd == gs)
                     continue;
-                bsrc[b].push_back(gs);
-                bdst[b].push_back(gd);
+                vs.push_back(gs);
+                vd.push_back(gd);
             }
+            pos += deg;
         }
     }
+    std::vector<uint32_t>().swap(body);
     // medoids file
     {
         std::ofstream mw(medoids_file, std::ios::binary);
@@ -729,18 +749,23 @@ DANCE_API int merge_shards_gpu(const std::string &vamana_prefix, const std::stri
     cudaSetDevice(saved);
     if (status != 0)
         return status;
+    std::vector<uint32_t> packed;
     for (uint64_t b = 0; b < buckets; ++b)
     {
         const uint32_t cnt = bucket_begin(b + 1) - bucket_begin(b);
+        packed.clear();
+        packed.reserve((uint64_t)cnt * (max_degree + 1));
         for (uint32_t l = 0; l < cnt; ++l)
         {
             const uint32_t d = degs[b][l];
             if (d > max_degree)
                 return -19;
-            out.write(reinterpret_cast<const char *>(&d), 4);
-            out.write(reinterpret_cast<const char *>(rows[b].data() + (uint64_t)l * max_degree), 4ull * d);
-            size += 4ull + 4ull * d;
+            packed.push_back(d);
+            const uint32_t *r = rows[b].data() + (uint64_t)l * max_degree;
+            packed.insert(packed.end(), r, r + d);
         }
+        out.write(reinterpret_cast<const char *>(packed.data()), 4ull * packed.size());
+        size += 4ull * packed.size();
         std::vector<uint32_t>().swap(rows[b]);
         std::vector<uint32_t>().swap(degs[b]);
     }

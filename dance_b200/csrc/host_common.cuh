@@ -247,18 +247,16 @@ struct LaunchQuery
     }
 };
 
-// uint8 replay on the tcgen05 tensor cores (replay_umma.cuh) when
-// DANCE_REPLAY_UMMA=1 is set at the call: rows of at most 128 bytes, at most
-// 128 cached rows (R + STEPS) and C <= 128.  Off by default: on the
-// benchmarked shape it is bit-identical to replay_kernel but slower, since
-// the pair-by-pair replay evaluates only the ~9 % of the 128 x 128 pairs that
-// the insert rule reaches, while the Gram path turns every pair into bits.
+// uint8 replay on the tcgen05 tensor cores (replay_umma.cuh) for rows of at
+// most 128 bytes, at most 128 cached rows (R + STEPS) and C <= 128; the
+// same graph as replay_kernel.  DANCE_REPLAY_UMMA=0 at the call selects the
+// pair-by-pair replay_kernel instead.
 constexpr uint32_t kReplayMaskChunk = 1u << 20; // vertices per masks/bits pass
 
 inline bool replay_umma_enabled()
 {
     const char *e = getenv("DANCE_REPLAY_UMMA");
-    return e && e[0] == '1';
+    return !(e && e[0] == '0');
 }
 
 inline bool replay_umma_fits(int dtype, uint32_t nchunks, uint32_t R, uint32_t S, uint32_t C)
@@ -289,9 +287,19 @@ inline int launch_replay_umma(ReplayParams p, cudaStream_t s)
     DANCE_CUDA(cudaFuncSetAttribute(ka, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_a));
     DANCE_CUDA(cudaFuncSetAttribute(ka, cudaFuncAttributePreferredSharedMemoryCarveout,
                                     (int)cudaSharedmemCarveoutMaxShared));
-    int occ = 0;
-    DANCE_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, ka, kBlockThreads, smem_a));
-    const uint64_t per_sm = (uint64_t)std::max(1, std::min(occ, 4));
+    // resident blocks per SM from the shared memory and registers they take
+    // (the occupancy query does not account for the carveout set above), at
+    // most four for the tensor memory
+    int dev = 0, smem_sm = 0, regs_sm = 0;
+    DANCE_CUDA(cudaGetDevice(&dev));
+    DANCE_CUDA(cudaDeviceGetAttribute(&smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev));
+    DANCE_CUDA(cudaDeviceGetAttribute(&regs_sm, cudaDevAttrMaxRegistersPerMultiprocessor, dev));
+    cudaFuncAttributes fa{};
+    DANCE_CUDA(cudaFuncGetAttributes(&fa, ka));
+    const size_t per_block = smem_a + fa.sharedSizeBytes + 1024; // + the driver's reserve per block
+    const int by_smem = (int)((size_t)smem_sm / per_block);
+    const int by_regs = regs_sm / std::max(1, ((fa.numRegs + 7) / 8 * 8) * kBlockThreads);
+    const uint64_t per_sm = (uint64_t)std::max(1, std::min(4, std::min(by_smem, by_regs)));
     auto kb = replay_bits_kernel;
     const size_t smem_b = (size_t)UmmaBitsLayout(p.C, p.exp_stride).bytes * kWarpsPerBlock;
     DANCE_CUDA(allow_smem(kb, smem_b));

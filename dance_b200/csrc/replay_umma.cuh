@@ -20,11 +20,10 @@
 // (lowest slot on ties), else is appended while the row has room, else
 // replaces the worst kept row if closer -- replay_kernel's decisions.
 //
-// Selected by DANCE_REPLAY_UMMA=1 (host_common.cuh).  Measured on the 10M
-// uint8 build (R64 STEPS64 C80): 1.54 s of replay per build against 1.25 s
-// for replay_kernel, graph bit-identical; turning all 128 x 64 pair values
-// into predicate bits costs more issue slots than replay_kernel's dp4a pairs,
-// of which the insert rule reaches only ~700 per vertex.
+// The default uint8 replay where it fits (host_common.cuh; DANCE_REPLAY_UMMA=0
+// selects replay_kernel).  On the 10M uint8 build (R64 STEPS64 C80) the
+// replay takes 0.85 s per build against 1.25 s for replay_kernel, graph
+// bit-identical.
 //
 // Two kernels per chunk of vertices, so that the sequential part does not
 // hold the tensor-memory block:

@@ -69,8 +69,10 @@ def encode_graph(graph: np.ndarray, degree: np.ndarray, start: int) -> bytes:
     offs = np.concatenate([[0], np.cumsum(counts)[:-1]])
     out[offs] = deg
     mask = np.arange(R)[None, :] < deg[:, None]
-    rows = np.repeat(offs + 1, deg.astype(np.int64))
-    within = np.concatenate([np.arange(k) for k in deg.astype(np.int64)]) if n else np.zeros(0, np.int64)
+    d64 = deg.astype(np.int64)
+    rows = np.repeat(offs + 1, d64)
+    first = np.cumsum(d64) - d64  # index of each row's first id among all ids
+    within = np.arange(int(d64.sum()), dtype=np.int64) - np.repeat(first, d64)
     out[rows + within] = graph[mask]
     parts.append(out.tobytes())
     blob = b"".join(parts)

@@ -33,3 +33,18 @@ def test_workload_configs_name_the_workload(fn, n, name):
     cfg = getattr(bench, fn)(n)
     assert cfg["workload"] == name and cfg["N"] == n
     assert {"R", "L", "C", "STEPS"} <= set(cfg) and "model" not in cfg
+
+
+def test_read_graph_padded_matches_file(tmp_path):
+    import numpy as np
+    import bench
+    from dance_b200 import formats
+    rng = np.random.default_rng(0)
+    n, R = 400, 12
+    deg = rng.integers(0, R + 1, n).astype(np.uint32)
+    g = np.full((n, R), 0xFFFFFFFF, np.uint32)
+    for i in range(n):
+        g[i, :deg[i]] = rng.integers(0, n, deg[i])
+    formats.write_graph(tmp_path / "g.idx", g, deg, 7)
+    g2, d2, start = bench.read_graph_padded(tmp_path / "g.idx", R)
+    assert np.array_equal(g, g2) and np.array_equal(deg, d2) and start == 7

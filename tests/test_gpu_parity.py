@@ -206,7 +206,7 @@ def test_replay_bit_exact(dtype, alpha):
 
 @pytest.mark.parametrize("dim,R,S,C", [(128, 64, 64, 80), (32, 24, 20, 56), (100, 40, 88, 128), (16, 8, 8, 12)])
 def test_replay_tensor_core_shapes_u8(dim, R, S, C, monkeypatch):
-    # DANCE_REPLAY_UMMA=1: the uint8 replay on the tcgen05 tensor cores
+    # the uint8 replay on the tcgen05 tensor cores (the default where it fits)
     # (R + S <= 128, C <= 128, rows of at most 128 bytes): the benchmarked
     # shape, small dimensions, an odd number of 16-byte chunks (zero-padded
     # K), a full 128-row cache with the widest work row, and a tiny row
