@@ -1716,6 +1716,8 @@ def run_disk_sharded(args):
             "num_parts": r0["num_parts"], "shard_sizes": r0["shard_sizes"],
             "stage_seconds": {k: r0[k] for k in ("partition_seconds", "shard_build_seconds", "merge_seconds",
                                                  "total_seconds")},
+            "shard_seconds_summed": {k: sum(sh[k] for sh in r0["shards"])
+                                     for k in ("gather_seconds", "build_seconds", "write_seconds")},
             "graph": {"start": start, "avg_degree": float(deg.mean()), "max_degree": int(deg.max()),
                       "audit": audit},
             "recall_at_10": {"L_search": 100, "queries": int(q.shape[0]), "ours": recall}}

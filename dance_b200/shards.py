@@ -265,60 +265,81 @@ def shard_build_params(R: int, L: int) -> tuple[int, int, int]:
 
 
 def build_shard(base: np.ndarray, ids: np.ndarray, out_file, R: int, L: int, C: int, STEPS: int, device: int,
-                store_fp16: bool = False) -> dict:
-    """One shard: gather its rows, build on `device`, save the graph in
-    DiskANN's format with the shard medoid as start."""
+                store_fp16: bool = False, workspace=None, stream=None) -> dict:
+    """One shard: gather its rows, build on `device` (on `stream`, in
+    `workspace` when given), save the graph in DiskANN's format with the
+    shard medoid as start."""
     import torch
     from . import vamana
     t0 = time.perf_counter()
     torch.cuda.set_device(device)
-    x = _rows_to_device(base, ids, torch.device("cuda", device))
-    if store_fp16 and x.dtype == torch.float32:
-        x = x.half()
-    store, stride = vamana.padded_store(x)
-    graph, degree, _, medoid = vamana.build_resident(store, x.shape[1], stride, R, L, C, STEPS)
-    torch.cuda.synchronize(device)
-    g = graph.cpu().numpy().view(np.uint32)
-    deg = degree.cpu().numpy().view(np.uint32)
+    stream = stream or torch.cuda.current_stream(device)
+    with torch.cuda.stream(stream):
+        x = _rows_to_device(base, ids, torch.device("cuda", device))
+        if store_fp16 and x.dtype == torch.float32:
+            x = x.half()
+        store, stride = vamana.padded_store(x)
+        stream.synchronize()
+        t1 = time.perf_counter()
+        graph, degree, _, medoid = vamana.build_resident(store, x.shape[1], stride, R, L, C, STEPS,
+                                                         workspace=workspace, stream=stream.cuda_stream)
+        stream.synchronize()
+        t2 = time.perf_counter()
+        g = graph.cpu().numpy().view(np.uint32)
+        deg = degree.cpu().numpy().view(np.uint32)
     write_graph(out_file, g, deg, medoid)
-    return {"points": int(len(ids)), "medoid": int(medoid), "seconds": time.perf_counter() - t0,
-            "device": device}
+    t3 = time.perf_counter()
+    return {"points": int(len(ids)), "medoid": int(medoid), "seconds": t3 - t0, "gather_seconds": t1 - t0,
+            "build_seconds": t2 - t1, "write_seconds": t3 - t2, "device": device}
 
 
 def build_shards(data_file, data_type: str, prefix_path, num_parts: int, R: int, L: int,
-                 devices: list[int] | None = None, store_fp16: bool = False) -> list[dict]:
-    """Builds every shard listed by the partition's idmaps, one GPU per
-    worker, each worker taking the next unbuilt shard."""
+                 devices: list[int] | None = None, store_fp16: bool = False,
+                 workers_per_device: int = 2) -> list[dict]:
+    """Builds every shard listed by the partition's idmaps.  Each GPU runs
+    `workers_per_device` workers (own stream and build workspace, so one
+    shard's file reads and writes overlap another's build), each taking the
+    next unbuilt shard, largest first."""
     import torch
+    from . import vamana
     if devices is None:
         par = max(1, min(_env_u32("DISKANN_SHARD_BUILD_PARALLELISM", torch.cuda.device_count()), num_parts))
         devices = list(range(min(par, torch.cuda.device_count())))
     shard_r, C, steps = shard_build_params(R, L)
     base = open_base(data_file, data_type)
     prefix = str(prefix_path)
+    sizes = [int(np.fromfile(f"{prefix}_subshard-{p}_ids_uint32.bin", dtype=np.uint32, count=1)[0])
+             for p in range(num_parts)]
     todo: queue.Queue[int] = queue.Queue()
-    for p in range(num_parts):
+    for p in sorted(range(num_parts), key=lambda q: -sizes[q]):
         todo.put(p)
     results: dict[int, dict] = {}
     errors: list[BaseException] = []
 
     def worker(dev: int) -> None:
-        while not errors:
-            try:
-                p = todo.get_nowait()
-            except queue.Empty:
-                return
-            try:
+        ws = None
+        try:
+            torch.cuda.set_device(dev)
+            stream = torch.cuda.Stream(dev)
+            while not errors:
+                try:
+                    p = todo.get_nowait()
+                except queue.Empty:
+                    return
                 ids = read_idmap(f"{prefix}_subshard-{p}_ids_uint32.bin").astype(np.int64)
                 if len(ids) == 0:
                     raise ValueError(f"shard {p} is empty")
+                if ws is None:
+                    ws = vamana.Workspace.create(max(sizes), shard_r, L, C, steps)
                 results[p] = build_shard(base, ids, f"{prefix}_subshard-{p}_mem.index", shard_r, L, C, steps,
-                                         dev, store_fp16)
-            except BaseException as e:  # reported after every worker stops
-                errors.append(e)
-                return
+                                         dev, store_fp16, workspace=ws, stream=stream)
+        except BaseException as e:  # reported after every worker stops
+            errors.append(e)
+        finally:
+            if ws is not None:
+                ws.close()
 
-    threads = [threading.Thread(target=worker, args=(d,)) for d in devices]
+    threads = [threading.Thread(target=worker, args=(d,)) for d in devices for _ in range(max(1, workers_per_device))]
     for t in threads:
         t.start()
     for t in threads:
