@@ -271,7 +271,16 @@ inline uint32_t replay_mask_vertices(int dtype, uint32_t nchunks, uint32_t R, ui
 {
     if (!replay_umma_fits(dtype, nchunks, R, S, C))
         return 0;
-    return std::max(1u, std::min(nverts, kReplayMaskChunk));
+    // DANCE_REPLAY_MASK_CHUNK (vertices) shrinks the chunk, e.g. to test the
+    // chunk loop on small inputs
+    uint32_t chunk = kReplayMaskChunk;
+    if (const char *e = getenv("DANCE_REPLAY_MASK_CHUNK"))
+    {
+        const unsigned long v = strtoul(e, nullptr, 10);
+        if (v > 0 && v < chunk)
+            chunk = (uint32_t)v;
+    }
+    return std::max(1u, std::min(nverts, chunk));
 }
 
 inline uint64_t replay_mask_bytes(uint32_t vertices, uint32_t S) { return (uint64_t)vertices * S * kMaskWords * 4u; }

@@ -330,6 +330,23 @@ def test_full_build_bit_exact(dtype):
     assert np.array_equal(g[2], o[2])
 
 
+def test_replay_tensor_core_mask_chunks(monkeypatch):
+    # the masks/bits kernels run over chunks of vertices (2^20 by default);
+    # chunks of 777 vertices exercise the chunk offsets on a small input
+    monkeypatch.setenv("DANCE_REPLAY_MASK_CHUNK", "777")
+    x = make(np.uint8, 3000, centroids=24)
+    R, L, S, C = 64, 100, 64, 80
+    m, ids, ds, deg = _round_inputs(x, R, 1, C=C)
+    e = oracle.search(x, R, L, S, m, 8, ids, ds, deg, S)
+    g = _gpu_replay(x, R, C, np.float32(1.2), ids, ds, deg, *e)
+    o = oracle.replay(x, R, C, np.float32(1.2), ids, ds, deg, *e)
+    for a, b in zip(g, o):
+        assert np.array_equal(a, b)
+    gb = _gpu_build(x, R, L, C, S)
+    ob = oracle.build_graph(x, R, L, C, S)
+    assert gb[3] == ob[3] and np.array_equal(gb[0], ob[0]) and np.array_equal(gb[1], ob[1])
+
+
 @pytest.mark.parametrize("tensor_core_replay", ["0", "1"])
 def test_full_build_config_shape_u8(tensor_core_replay, monkeypatch):
     # BASELINE config shape (R64 L100 C80 STEPS64) at a size the oracle
