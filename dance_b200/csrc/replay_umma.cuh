@@ -345,10 +345,20 @@ __global__ void __launch_bounds__(kBlockThreads, 1) replay_masks_kernel(ReplayPa
                     const bool mine = r < cw;
                     const uint32_t nx = mine ? wn[r] : 0u;
                     const float dx = mine ? wdv[r] : 0.0f;
+                    // expansion k only meets kept rows of earlier expansions
+                    // (j < k) and of initial slots (S .. S + R): a column
+                    // chunk of expansion rows at or beyond this warp's last
+                    // expansion, or past the initial rows, stays zero
+                    const uint32_t kend = min(cw, (uint32_t)warp * 32u + 32u);
                     uint32_t ob[4], vb[4];
 #pragma unroll
                     for (uint32_t q = 0; q < 4; ++q)
                     {
+                        ob[q] = 0u;
+                        vb[q] = 0u;
+                        const uint32_t c0q = 32u * q;
+                        if ((c0q + 32u <= S && c0q + 1u >= kend) || c0q >= S + R)
+                            continue; // warp-uniform
                         uint32_t g[32];
                         tmem_ld32(tmem + (((uint32_t)warp * 32u) << 16) + 32u * q, g);
                         uint32_t o = 0, vv = 0;
