@@ -56,39 +56,41 @@ def graph_bytes(degree: np.ndarray, R: int) -> int:
     return GRAPH_HEADER.size + 4 * len(deg) + 4 * int(deg.sum())
 
 
-def encode_graph(graph: np.ndarray, degree: np.ndarray, start: int) -> bytes:
-    """Serialise an N x R graph (rows padded with 0xFFFFFFFF) in DiskANN layout."""
+def _graph_header_and_words(graph: np.ndarray, degree: np.ndarray, start: int):
+    """DiskANN graph layout of an N x R graph (rows padded with 0xFFFFFFFF):
+    the 24-byte header and the body words [deg, ids...] row after row."""
     n, R = graph.shape
     deg = np.minimum(degree.astype(np.int64), R).astype(np.uint32)
     max_degree = int(degree.max()) if n else 0
     total = graph_bytes(degree, R)
-    parts = [GRAPH_HEADER.pack(total, max_degree, int(start), 0)]
-    # vectorised row packing: [deg, ids...] per row
-    counts = deg.astype(np.int64) + 1
-    out = np.empty(int(counts.sum()), dtype=np.uint32)
-    offs = np.concatenate([[0], np.cumsum(counts)[:-1]])
-    out[offs] = deg
-    mask = np.arange(R)[None, :] < deg[:, None]
-    d64 = deg.astype(np.int64)
-    rows = np.repeat(offs + 1, d64)
-    first = np.cumsum(d64) - d64  # index of each row's first id among all ids
-    within = np.arange(int(d64.sum()), dtype=np.int64) - np.repeat(first, d64)
-    out[rows + within] = graph[mask]
-    parts.append(out.tobytes())
-    blob = b"".join(parts)
-    assert len(blob) == total
-    return blob
+    header = GRAPH_HEADER.pack(total, max_degree, int(start), 0)
+    # rows as [deg, id_0 .. id_{R-1}], kept up to each row's degree, read row-major
+    rows = np.empty((n, R + 1), dtype=np.uint32)
+    rows[:, 0] = deg
+    rows[:, 1:] = graph
+    keep = np.arange(R + 1, dtype=np.uint32)[None, :] <= deg[:, None]
+    words = rows[keep]
+    assert GRAPH_HEADER.size + 4 * len(words) == total
+    return header, words
+
+
+def encode_graph(graph: np.ndarray, degree: np.ndarray, start: int) -> bytes:
+    """Serialise an N x R graph (rows padded with 0xFFFFFFFF) in DiskANN layout."""
+    header, words = _graph_header_and_words(graph, degree, start)
+    return header + words.tobytes()
 
 
 def write_graph(path: str | os.PathLike, graph: np.ndarray, degree: np.ndarray, start: int) -> None:
     path = Path(path)
     tmp = path.with_name(path.name + ".tmp")
     _refuse_existing(path, tmp)
-    blob = encode_graph(graph, degree, start)
+    header, words = _graph_header_and_words(graph, degree, start)
+    total = len(header) + 4 * len(words)
     try:
         with open(tmp, "wb") as f:
-            f.write(blob)
-        if tmp.stat().st_size != len(blob):
+            f.write(header)
+            words.tofile(f)
+        if tmp.stat().st_size != total:
             raise IOError(f"short write to {tmp}")
         os.replace(tmp, path)
     except BaseException:
