@@ -231,6 +231,9 @@ def partition_with_ram_budget(data_file, data_type: str, sampling_rate: float, r
         if est <= ram_budget_gb * 1024.0 ** 3:
             break
         parts += 2
+        if parts > min(len(train_ids), 8192):
+            raise ValueError(f"no partition of at most {parts - 2} parts fits a {ram_budget_gb} GB build budget; "
+                             "raise the budget or the sampling rate")
     kb = min(k_base, parts)
     prefix = str(prefix_path)
     write_centroids(prefix + "_centroids.bin", centers.cpu().numpy())
